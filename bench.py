@@ -1,0 +1,475 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path (paged decode by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|decode_fp8|decode_long]
+
+Default workload (N = 1): paged-attention decode, bf16, batch 64, 32 query /
+8 KV heads, head_dim 128, block_size 16, context length per sequence
+uniform in [128, 4096], block table = seeded random permutation of a
+20,000-block KV pool, K/V ~ N(0,1)*0.5, one new token per sequence.
+Metric: algorithmic HBM bytes per step / time (GB/s).
+
+A step is one call of rbln_custom_ops.paged_causal_attn_decode over the
+batch (append + attention). `value` times K steps with inputs resident in
+HBM (the KV pool, 1.3 GB, is far larger than the 126 MB L2, so no flush is
+needed); `e2e` times the same op through the public torch op with the
+step's inputs (q, k, v, seq, block_table) copied from pinned host memory
+and the output copied back inside the timed region. `roofline` is the main
+kernel alone, timed with CUDA events recorded on its launch stream around
+that kernel (C-ABI measurement hook).
+
+Under torchrun (N > 1) every rank runs its own batch of the same workload
+(sequences are independent; no collective on the data path) and the JSON
+line reports the whole-job aggregate over max-over-ranks time.
+
+--impl reference times the reference's CPU algorithm for the same workload
+on this host's cores (the oracle's restatement of the reference CPU op,
+oracle/paged_attention.py, on a bounded sample of sequences).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "torch-rbln_b200"))
+
+import torch  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+WORKLOADS = {
+    "decode": dict(desc="paged decode bf16 B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=20000",
+                   B=64, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=20000, fp8=False),
+    "decode_fp8": dict(desc="paged decode fp8-e4m3 KV B=256 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
+                       B=256, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
+    "decode_long": dict(desc="paged decode bf16 B=32 Hq=64 Hkv=8 D=128 bs=16 L=32768 pool=65536",
+                        B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False),
+}
+
+
+def build_decode(wl: dict, device, seed: int = 0):
+    """Seeded synthetic decode inputs. Lengths / block table on the CPU
+    generator; the KV pool is drawn on the device (same seed) for speed."""
+    g = torch.Generator().manual_seed(seed)
+    B, Hkv, G, D, bs = wl["B"], wl["Hkv"], wl["G"], wl["D"], wl["bs"]
+    lens = torch.randint(wl["lmin"], wl["lmax"] + 1, (B,), generator=g)
+    max_blocks = int(math.ceil(int(lens.max()) / bs))
+    nblk = wl["pool"] or int(sum(math.ceil(int(x) / bs) for x in lens)) + B
+    nblk = max(nblk, B * max_blocks)
+    perm = torch.randperm(nblk, generator=g)
+    # each sequence takes its blocks from the permutation in turn
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    cursor = 0
+    for b in range(B):
+        n = int(math.ceil(int(lens[b]) / bs))
+        bt[b, :n] = perm[cursor:cursor + n].to(torch.int32)
+        cursor += n
+    q = torch.randn([B, Hkv, G, 1, D], generator=g).to(torch.bfloat16)
+    k = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
+    seq = (lens - 1).to(torch.int32).reshape(B, 1)
+    gd = torch.Generator(device=device).manual_seed(seed + 1)
+    shape = [nblk, Hkv, 1, bs, D]
+    if wl["fp8"]:
+        kc, ks = _fp8_pool(shape, gd, device)
+        vc, vs = _fp8_pool(shape, gd, device)
+    else:
+        kc = (torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5)
+        vc = (torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5)
+        ks = vs = None
+    return dict(q=q, k=k, v=v, seq=seq, bt=bt, kcache=kc, vcache=vc, k_scale=ks, v_scale=vs, lens=lens,
+                scale=1.0 / math.sqrt(D), bs=bs, B=B, Hkv=Hkv, G=G, D=D, fp8=wl["fp8"])
+
+
+def _fp8_pool(shape, gd, device):
+    x = torch.randn(shape, generator=gd, device=device, dtype=torch.float32)
+    amax = x.abs().amax(dim=(2, 3, 4)).clamp_min(1e-6)
+    sc = (amax / 448.0).contiguous()
+    q = (x / sc[:, :, None, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    del x
+    return q, sc
+
+
+def decode_bytes(d: dict) -> int:
+    """Algorithmic HBM bytes of one decode step: every attended K/V element
+    read once, q read, output written, new k/v read and written to the
+    cache, block-table entries and (fp8) scales read."""
+    lens = d["lens"].to(torch.int64)
+    Hkv, G, D, bs = d["Hkv"], d["G"], d["D"], d["bs"]
+    el = 1 if d["fp8"] else 2
+    kv = int(lens.sum()) * Hkv * D * el * 2
+    blocks = int(((lens + bs - 1) // bs).sum())
+    scales = blocks * Hkv * 4 * 2 if d["fp8"] else 0
+    qo = d["B"] * Hkv * G * D * 2 * 2
+    new = d["B"] * Hkv * D * (2 * 2 + el * 2)
+    return kv + scales + qo + new + blocks * 4
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, wl_name):
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import torch_rbln_b200  # noqa: F401
+    from torch_rbln_b200 import cabi
+
+    wl = WORKLOADS[wl_name]
+    d = build_decode(wl, dev, seed=1000 * rank)
+    q, k, v = d["q"].to(dev), d["k"].to(dev), d["v"].to(dev)
+    seq, bt = d["seq"].to(dev), d["bt"].to(dev)
+    kc, vc = d["kcache"], d["vcache"]
+    ks, vs = d["k_scale"], d["v_scale"]
+    scale_t = torch.tensor(d["scale"])
+    nbytes = decode_bytes(d)
+    ops = torch.ops.rbln_custom_ops
+
+    def op_call(qq, kk, vv, ss, bb):
+        if d["fp8"]:
+            return ops.paged_causal_attn_decode_kvfp8(qq, kk, vv, kc, vc, ks, vs, ss, scale_t, bb, d["bs"])
+        return ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
+
+    # C-ABI parameter block with the timing hook around the main kernel
+    p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs)
+    cabi.attach_workspace(p, dev, keep)
+    L = cabi.lib()
+    stream = torch.cuda.current_stream(dev)
+    entry = L.rbln_paged_causal_attn_decode
+    import ctypes
+
+    pref = ctypes.byref(p)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    ws_bytes = p.workspace_bytes
+
+    def cabi_step(ev0=None, ev1=None):
+        p.prof_events[0] = ev0.cuda_event if ev0 is not None else None
+        p.prof_events[1] = ev1.cuda_event if ev1 is not None else None
+        rc = entry(pref, sh)
+        if rc != 0:
+            raise RuntimeError(f"rbln_paged_causal_attn_decode failed: {rc}")
+
+    for _ in range(args.warmup):
+        cabi_step()
+        op_call(q, k, v, seq, bt)
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident inputs, K steps, events around the whole op
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in kev:  # create the events on the device before timing
+        e0.record(stream)
+        e1.record(stream)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            cabi_step(*kev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+    ms_total = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in kev]
+    ms_step = ms_total / args.steps
+
+    # ---- e2e: public torch op, host buffers, H2D + D2H inside the timed region
+    pin = lambda t: t.cpu().pin_memory()
+    hq, hk, hv, hs, hb = pin(d["q"]), pin(d["k"]), pin(d["v"]), pin(d["seq"]), pin(d["bt"])
+    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs, hb))
+    d2h = hout.numel() * hout.element_size()
+    for _ in range(max(2, args.warmup)):
+        o = op_call(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
+                    hs.to(dev, non_blocking=True), hb.to(dev, non_blocking=True))
+        hout.copy_(o, non_blocking=True)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        o = op_call(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
+                    hs.to(dev, non_blocking=True), hb.to(dev, non_blocking=True))
+        hout.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    # max over ranks
+    if ws > 1:
+        tt = torch.tensor([ms_step, e2e_ms, statistics.mean(kern_ms)], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_step, e2e_ms, kmean = tt.tolist()
+    else:
+        kmean = statistics.mean(kern_ms)
+
+    hbm_peak, tf_peak, peak_src = load_peaks()
+    achieved = nbytes / (kmean * 1e-3) / 1e9
+    value = ws * nbytes / (ms_step * 1e-3) / 1e9
+    launches_per_step = 1 + (1 if ws_bytes > 0 else 0)
+    line = {
+        "metric": "paged decode HBM GB/s",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
+        "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
+        "config": {"workload": wl["desc"], "global_batch": d["B"] * ws, "parallelism": f"batch-sharded x{ws}",
+                   "l2": "inputs larger than L2 (KV pool " + f"{kc.numel() * kc.element_size() * 2 / 1e9:.2f} GB)",
+                   "bytes_per_step_per_gpu": nbytes},
+        "e2e": {"value": round(ws * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "torch.ops.rbln_custom_ops.paged_causal_attn_decode" + ("_kvfp8" if d["fp8"] else "")},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "kernel": "paged_decode_split_kernel", "kernel_ms": round(kmean, 4),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                     else "fallback 6.65 TB/s"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    traffic = _traffic_from_profiles(wl_name)
+    if traffic is not None:
+        line["roofline"]["traffic"] = traffic
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl_name, d, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _traffic_from_profiles(wl_name):
+    """DRAM bytes per launch of the main kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", f"traffic_{wl_name}.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ---------------------------------------------------------------------------
+def cpu_sample(d: dict, n_seq: int, device_pool: bool = True):
+    """First n_seq sequences, gathered into the reference's contiguous
+    per-sequence layout [n, Hkv, 1, max_seq, D] (gather not timed)."""
+    from oracle import paged_attention as opa
+
+    n = n_seq
+    lens = d["lens"][:n]
+    bs = d["bs"]
+    span = int(math.ceil(int(lens.max()) / bs)) * bs
+    bt = d["bt"][:n, : span // bs]
+    kcs, vcs = [], []
+    for b in range(n):
+        blocks = bt[b].long()
+        kb = d["kcache"][blocks.to(d["kcache"].device)].cpu()
+        vb = d["vcache"][blocks.to(d["vcache"].device)].cpu()
+        if d["fp8"]:
+            ksb = d["k_scale"][blocks.to(d["kcache"].device)].cpu()
+            vsb = d["v_scale"][blocks.to(d["kcache"].device)].cpu()
+            kb = (kb.float() * ksb[:, :, None, None, None]).to(torch.bfloat16)
+            vb = (vb.float() * vsb[:, :, None, None, None]).to(torch.bfloat16)
+        # [nb, Hkv, 1, bs, D] -> [Hkv, 1, nb*bs, D]
+        kcs.append(kb.permute(1, 2, 0, 3, 4).reshape(d["Hkv"], 1, span, d["D"]))
+        vcs.append(vb.permute(1, 2, 0, 3, 4).reshape(d["Hkv"], 1, span, d["D"]))
+    kc = torch.stack(kcs)
+    vc = torch.stack(vcs)
+    sub = dict(d)
+    sub["lens"] = lens
+    sub["B"] = n
+    return (d["q"][:n].clone(), d["k"][:n].clone(), d["v"][:n].clone(), kc, vc, d["seq"][:n].clone(),
+            torch.tensor(d["scale"]), opa, decode_bytes(sub))
+
+
+def cpu_baseline(wl_name, d, budget_s=20.0, steps=None):
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    # size the sample: time one sequence, then take as many as fit the budget
+    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, 1)
+    t = time.perf_counter()
+    opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
+    one = max(time.perf_counter() - t, 1e-4)
+    n = int(max(1, min(d["B"], budget_s / 4 / one)))
+    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, n)
+    times = []
+    reps = steps if steps is not None else 3
+    opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)  # warm-up
+    for _ in range(reps):
+        kk, vv = kc.clone(), vc.clone()
+        t = time.perf_counter()
+        opa.mock_decode_contiguous(q, k, v, kk, vv, seq, sc)
+        times.append(time.perf_counter() - t)
+    med = statistics.median(times)
+    return {"value": round(nb / med / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{n} of {d['B']} sequences of the same workload, reference CPU algorithm "
+                      f"(oracle.paged_attention.mock_decode_contiguous, bf16 over the gathered per-sequence "
+                      f"layout), median of {reps} runs, {med * 1e3:.1f} ms per sample",
+            "ms_per_sample": round(med * 1e3, 2), "bytes_per_sample": nb}
+
+
+def run_reference(args, wl_name):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    wl = WORKLOADS[wl_name]
+    dev = torch.device("cpu")
+    d = build_decode(wl, dev, seed=0)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, 1)
+    t = time.perf_counter()
+    opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
+    one = max(time.perf_counter() - t, 1e-4)
+    per_step_budget = max(0.5, 120.0 / max(1, args.steps + args.warmup))
+    n = int(max(1, min(d["B"], per_step_budget / one)))
+    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, n)
+    for _ in range(args.warmup):
+        opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
+    times = []
+    for _ in range(args.steps):
+        kk, vv = kc.clone(), vc.clone()
+        t = time.perf_counter()
+        opa.mock_decode_contiguous(q, k, v, kk, vv, seq, sc)
+        times.append(time.perf_counter() - t)
+    ms = statistics.mean(times) * 1e3
+    val = nb / (ms * 1e-3) / 1e9
+    sample = (f"{n} of {d['B']} sequences per step, reference CPU algorithm (oracle restatement of "
+              f"test_custom_kernel.py paged_causal_attn_decode on the per-sequence layout), wall clock")
+    line = {"impl": "reference", "metric": "paged decode HBM GB/s", "value": round(val, 3), "unit": "GB/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "global_batch": d["B"]},
+            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, args.workload)
+    else:
+        run_ours(args, args.workload)
+
+
+if __name__ == "__main__":
+    main()

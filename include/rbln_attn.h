@@ -1,0 +1,151 @@
+/*
+ * rbln_attn.h — C-ABI of the B200 (sm_100a) attention kernels behind the
+ * torch-rbln attention hot path.
+ *
+ * Every entry point takes a plain-old-data parameter struct (device pointers,
+ * element strides, shapes, dtype codes) and a cudaStream_t, launches its
+ * kernels on that stream without any host synchronisation, allocates nothing
+ * (scratch memory is passed in by the caller; ask the *_workspace_size query
+ * for its size), throws nothing, and returns an rbln_status_t.
+ *
+ * Tensor layouts follow the reference's custom-op contract
+ * (test/rbln/test_custom_kernel.py:31-486, torch_rbln/_internal/
+ * register_custom_ops.py:154-450):
+ *   q, out        [B, Hkv, G, S_q, D]     (S_q = 1 for decode)
+ *   k, v (new)    [B, Hkv, 1, S_q, D]
+ *   kcache,vcache [num_blocks, Hkv, 1, block_size, D_cache >= D]
+ *   seq           [B, 1] int32   decode: position of the new token
+ *                                prefill: start offset of the chunk
+ *   block_table   [B, max_blocks] int16/int32/int64
+ * The innermost dimension of every tensor must be contiguous and every row
+ * must start on a 16-byte boundary.
+ */
+#ifndef RBLN_ATTN_H_
+#define RBLN_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RBLN_ATTN_ABI_VERSION 1
+
+typedef enum {
+  RBLN_OK = 0,
+  RBLN_ERR_INVALID_ARGUMENT = -1, /* null pointer, bad shape/stride/alignment */
+  RBLN_ERR_UNSUPPORTED = -2,      /* valid, but not a configuration built here */
+  RBLN_ERR_WORKSPACE = -3,        /* workspace missing or too small */
+  RBLN_ERR_LAUNCH = -4,           /* cudaLaunch* reported an error */
+  RBLN_ERR_NO_DEVICE = -5         /* no sm_100 device current */
+} rbln_status_t;
+
+typedef enum {
+  RBLN_DT_F32 = 0,
+  RBLN_DT_F16 = 1,
+  RBLN_DT_BF16 = 2,
+  RBLN_DT_FP8_E4M3 = 3,
+  RBLN_DT_I16 = 4,
+  RBLN_DT_I32 = 5,
+  RBLN_DT_I64 = 6,
+  RBLN_DT_BOOL = 7 /* one byte, non-zero = keep */
+} rbln_dtype_t;
+
+/* Device-side error bits, OR-ed into *error_flags when a kernel meets an
+ * input it must not dereference. The access is skipped (the position is
+ * treated as masked) and the kernel carries on. */
+#define RBLN_DEVERR_BLOCK_ID_RANGE 0x1u /* block_table entry outside [0, num_blocks) */
+#define RBLN_DEVERR_SEQ_RANGE 0x2u      /* seq < 0, or a write past the table's span */
+
+/* Paged attention over a block-table-indexed KV cache: one parameter block
+ * serves decode (S_q = 1) and chunked prefill (S_q >= 1). */
+typedef struct {
+  /* shapes */
+  int32_t batch;        /* B */
+  int32_t num_kv_heads; /* Hkv */
+  int32_t group;        /* G = query heads per KV head */
+  int32_t q_len;        /* S_q (1 for decode) */
+  int32_t head_dim;     /* D: 64 or 128 */
+  int32_t num_blocks;   /* physical blocks in the pool (kcache.size(0)) */
+  int32_t block_size;   /* tokens per block */
+  int32_t max_blocks;   /* block_table.size(1); span = max_blocks*block_size */
+
+  /* query / output, dtype q_dtype (F16 or BF16), strides in elements */
+  const void* q;
+  int64_t q_stride[4]; /* b, h, g, s */
+  void* out;
+  int64_t out_stride[4];
+  int32_t q_dtype;
+
+  /* new keys/values to append (same dtype as q); NULL = no append */
+  const void* k_new;
+  const void* v_new;
+  int64_t k_new_stride[3]; /* b, h, s */
+  int64_t v_new_stride[3];
+
+  /* paged caches: dtype kv_dtype (F16, BF16 or FP8_E4M3) */
+  void* kcache;
+  void* vcache;
+  int32_t kv_dtype;
+  int64_t cache_stride[3]; /* block, head, token (same for K and V) */
+  /* fp8 only: one fp32 dequant scale per (block, head), K and V separately */
+  const float* k_scale;
+  const float* v_scale;
+  int64_t scale_stride[2]; /* block, head */
+
+  const int32_t* seq;
+  int64_t seq_stride;
+  const void* block_table;
+  int32_t block_table_dtype; /* I16, I32 or I64 */
+  int64_t block_table_stride;
+
+  /* optional keep-mask (value > 0 keeps the position); NULL = causal/length.
+   * decode:  [B, mask_len]          (mask_stride[0] = batch stride)
+   * prefill: [B, S_q, mask_len]     (mask_stride = batch, query row) */
+  const void* mask;
+  int32_t mask_dtype;
+  int32_t mask_len;
+  int64_t mask_stride[2];
+  int32_t causal;        /* prefill: 1 = causal offset by seq[b], 0 = bidirectional */
+
+  float scale;            /* softmax scale, used when scale_dev == NULL */
+  const float* scale_dev; /* optional device pointer to an fp32 scale */
+
+  void* workspace;        /* caller-allocated scratch (see *_workspace_size) */
+  size_t workspace_bytes;
+  uint32_t* error_flags;  /* optional device word, see RBLN_DEVERR_* */
+  int32_t num_splits;     /* 0 = heuristic; else context splits per sequence */
+  /* optional cudaEvent_t pair recorded on `stream` right before and right
+   * after the main attention kernel (measurement hook; NULL = none) */
+  void* prof_events[2];
+} rbln_paged_attn_params_t;
+
+/* ABI checks for foreign-function bindings. */
+int rbln_attn_abi_version(void);
+size_t rbln_paged_attn_params_sizeof(void);
+
+/* Scratch needed by the decode entry points for these parameters. */
+int rbln_paged_decode_workspace_size(const rbln_paged_attn_params_t* p, size_t* bytes);
+
+/* rbln_custom_ops::paged_causal_attn_decode
+ * (reference frontend torch_rbln/_internal/register_custom_ops.py:409-450,
+ *  CPU semantics test/rbln/test_custom_kernel.py:388-486).
+ * Appends k_new/v_new at position seq[b] (when seq[b] < span), then attends
+ * the G query heads of every KV head over positions [0, min(seq[b]+1, span)),
+ * or over the positions whose mask value is > 0 when p->mask is set. */
+int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* rbln_custom_ops::paged_attn_decode
+ * (reference frontend register_custom_ops.py:253-293,
+ *  CPU semantics test_custom_kernel.py:138-216).
+ * Same append; attention over the positions whose mask value is > 0.
+ * p->mask is required. */
+int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* RBLN_ATTN_H_ */

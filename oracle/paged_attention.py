@@ -1,0 +1,242 @@
+"""CPU oracle for the paged-attention custom ops. TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+module, and only to check or time against it. No product code path imports
+it.
+
+It restates, in torch CPU ops, the reference's own CPU definition of the four
+rbln_custom_ops paged ops (test/rbln/test_custom_kernel.py, the "simplified
+mock implementations" of optimum-rbln's operators):
+
+  paged_attn_prefill         test_custom_kernel.py:31-92
+  paged_attn_decode          test_custom_kernel.py:138-216
+  paged_causal_attn_prefill  test_custom_kernel.py:262-343
+  paged_causal_attn_decode   test_custom_kernel.py:388-486
+
+The reference's CPU definitions only cover one physical block per sequence
+(prefill always uses block 0, decode uses kcache[b]; block_table and
+block_size are ignored). This restatement generalises them to a real block
+table, which is what the CUDA kernels implement:
+
+  * position t of sequence b lives in block block_table[b, t // block_size],
+    row t % block_size; the addressable span is max_blocks * block_size;
+  * new k/v rows are written first (decode: at seq[b] when seq[b] < span,
+    like test_custom_kernel.py:182-186; prefill: at [seq[b], seq[b] + S_q)),
+    then read back (write-then-read);
+  * causal prefill masks key t for query i when t > seq[b] + i (the
+    reference's tril at :326-331 has no seq offset and is only right for
+    seq[b] == 0); bidirectional prefill attends [0, seq[b] + S_q);
+  * an fp8-e4m3 cache holds x / scale[block, head] (saturated to +-448);
+    it is read as float(e4m3) * scale[block, head];
+  * a block_table entry outside [0, num_blocks) makes its positions masked
+    (the CUDA kernels skip such reads and raise a device error flag).
+
+Two arithmetic modes:
+  mode="mock": the op sequence of the reference (scores in q.dtype, fp32
+      softmax, probabilities rounded to q.dtype, P.V in q.dtype). On the
+      reference's own single-block configurations this equals the reference
+      bit for bit (tests/test_oracle_golden.py pins it).
+  mode="fp32": every product in float32 with no intermediate rounding; the
+      tolerance reference for the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+FP8_MAX = 448.0
+
+
+def span_of(block_table: torch.Tensor, block_size: int) -> int:
+    return int(block_table.shape[-1]) * int(block_size)
+
+
+def _bt_row(block_table: torch.Tensor, b: int) -> torch.Tensor:
+    bt = block_table if block_table.dim() == 2 else block_table.reshape(1, -1)
+    return bt[b if bt.shape[0] > 1 else 0].to(torch.int64)
+
+
+def _locate(block_table: torch.Tensor, b: int, pos: torch.Tensor, block_size: int, num_blocks: int):
+    """Physical (block, row, valid) of logical positions `pos` of sequence b."""
+    row = _bt_row(block_table, b)
+    blk = row[pos // block_size]
+    valid = (blk >= 0) & (blk < num_blocks)
+    return blk.clamp(0, max(num_blocks - 1, 0)), pos % block_size, valid
+
+
+def quantize_fp8(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """x / scale, saturated to the e4m3 range, rounded to nearest even."""
+    return (x.float() / scale.float()).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+
+def _write_rows(cache, new, block_table, b, positions, block_size, scale=None):
+    """Writes new[:, i, :D] (per KV head) at logical positions[i] of sequence b."""
+    num_blocks = cache.shape[0]
+    span = span_of(block_table, block_size)
+    D = new.shape[-1]
+    for i, t in enumerate(positions.tolist()):
+        if t < 0 or t >= span:
+            continue
+        blk, off, ok = _locate(block_table, b, torch.tensor([t]), block_size, num_blocks)
+        if not bool(ok[0]):
+            continue
+        blk, off = int(blk[0]), int(off[0])
+        rows = new[:, i, :D]  # [Hkv, D]
+        if cache.dtype == torch.float8_e4m3fn:
+            rows = quantize_fp8(rows, scale[blk].reshape(-1, 1))
+        cache[blk, :, 0, off, :D] = rows.to(cache.dtype)
+
+
+def _gather(cache, block_table, b, span, block_size, D, scale=None):
+    """Per-sequence view [Hkv, span, D] of the paged cache (+ validity)."""
+    pos = torch.arange(span)
+    blk, off, ok = _locate(block_table, b, pos, block_size, cache.shape[0])
+    rows = cache[blk, :, 0, off, :D]  # [span, Hkv, D]
+    if cache.dtype == torch.float8_e4m3fn:
+        rows = rows.float() * scale[blk].float().unsqueeze(-1)
+    return rows.permute(1, 0, 2), ok
+
+
+def _attend(q, K, V, keep, scale, mode):
+    """softmax(q.K^T * scale | keep) . V for one sequence.
+
+    q [Hkv, G, S, D], K/V [Hkv, T, D], keep [S, T] bool -> [Hkv, G, S, D].
+    """
+    if mode == "mock":
+        dt = q.dtype
+        Kc, Vc = K.to(dt), V.to(dt)
+        # matmul in q.dtype, then `* scale` (test_custom_kernel.py:87,199)
+        w = torch.matmul(q, Kc.unsqueeze(1).transpose(-1, -2)) * scale
+        add = torch.where(keep, 0.0, -float("inf"))  # float32, like :88,204
+        w = w + add
+        p = torch.nn.functional.softmax(w, dim=-1, dtype=torch.float32).to(dt)
+        return torch.matmul(p, Vc.unsqueeze(1))
+    qf, Kf, Vf = q.float(), K.float(), V.float()
+    w = torch.matmul(qf, Kf.unsqueeze(1).transpose(-1, -2)) * float(scale)
+    w = w.masked_fill(~keep, -float("inf"))
+    p = torch.softmax(w, dim=-1)
+    return torch.matmul(p, Vf.unsqueeze(1))
+
+
+def paged_decode(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
+                 mask: Optional[torch.Tensor] = None, *, k_scale=None, v_scale=None,
+                 mode: str = "fp32") -> torch.Tensor:
+    """paged_causal_attn_decode (mask=None or [B, L]) / paged_attn_decode (mask [B,1,1,1,L]).
+
+    Mutates kcache/vcache. Returns [B, Hkv, G, 1, D] in q.dtype (mode="mock")
+    or float32 (mode="fp32").
+    """
+    B, Hkv, G, S, D = q.shape
+    assert S == 1
+    span = span_of(block_table, block_size)
+    seqv = seq.reshape(-1).to(torch.int64)
+    outs = []
+    for b in range(B):
+        p = int(seqv[b])
+        if p >= 0:
+            _write_rows(kcache, k[b, :, 0], block_table, b, torch.tensor([p]), block_size, k_scale)
+            _write_rows(vcache, v[b, :, 0], block_table, b, torch.tensor([p]), block_size, v_scale)
+        K, okk = _gather(kcache, block_table, b, span, block_size, D, k_scale)
+        V, _ = _gather(vcache, block_table, b, span, block_size, D, v_scale)
+        t = torch.arange(span)
+        if mask is not None:
+            mrow = mask[b if mask.shape[0] > 1 else 0].reshape(-1)
+            L = min(span, mrow.numel())
+            keep = torch.zeros(span, dtype=torch.bool)
+            keep[:L] = mrow[:L] > 0
+        else:
+            L = min(p + 1, span) if p >= 0 else 0
+            keep = t < L
+        keep = (keep & okk).reshape(1, span)
+        outs.append(_attend(q[b], K, V, keep, scale, mode))
+    out = torch.stack(outs, 0)
+    return out if mode == "mock" else out.float()
+
+
+def paged_prefill(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
+                  mask: Optional[torch.Tensor] = None, *, causal: bool = True,
+                  position_mask: Optional[torch.Tensor] = None, mode: str = "fp32") -> torch.Tensor:
+    """Chunked prefill over a paged cache.
+
+    paged_attn_prefill:        mask = keep-mask [B|1, 1, 1, S_q, L], causal ignored.
+    paged_causal_attn_prefill: mask=None, causal = not is_bidirectional,
+                               position_mask = optional [B|1, L] keep-mask.
+    Mutates kcache/vcache. Returns [B, Hkv, G, S_q, D].
+    """
+    B, Hkv, G, S, D = q.shape
+    span = span_of(block_table, block_size)
+    seqv = seq.reshape(-1).to(torch.int64)
+    outs = []
+    for b in range(B):
+        s0 = int(seqv[b if seqv.numel() > 1 else 0])
+        pos = torch.arange(S) + s0
+        _write_rows(kcache, k[b, :, 0], block_table, b, pos, block_size)
+        _write_rows(vcache, v[b, :, 0], block_table, b, pos, block_size)
+        K, okk = _gather(kcache, block_table, b, span, block_size, D)
+        V, _ = _gather(vcache, block_table, b, span, block_size, D)
+        t = torch.arange(span).reshape(1, span)
+        qi = pos.reshape(S, 1)
+        if mask is not None:
+            m = mask[b if mask.shape[0] > 1 else 0].reshape(-1, mask.shape[-1])[-S:]  # [S, L]
+            L = min(span, m.shape[-1])
+            keep = torch.zeros(S, span, dtype=torch.bool)
+            keep[:, :L] = m[:, :L] > 0
+        elif causal:
+            keep = t <= qi
+        else:
+            keep = (t < s0 + S).expand(S, span)
+        if position_mask is not None:
+            pm = position_mask[b if position_mask.shape[0] > 1 else 0].reshape(-1)
+            L = min(span, pm.numel())
+            pk = torch.zeros(span, dtype=torch.bool)
+            pk[:L] = pm[:L] > 0
+            keep = keep & pk.reshape(1, span)
+        keep = keep & okk.reshape(1, span)
+        outs.append(_attend(q[b], K, V, keep, scale, mode))
+    out = torch.stack(outs, 0)
+    return out if mode == "mock" else out.float()
+
+
+def contiguous_cache(kcache, block_table, block_size, b, D, scale=None):
+    """Gathers sequence b of a paged cache into the reference's per-sequence
+    layout [1, Hkv, 1, span, D] (used to feed the CPU baseline)."""
+    span = span_of(block_table, block_size)
+    K, _ = _gather(kcache, block_table, b, span, block_size, D, scale)
+    return K.unsqueeze(0).unsqueeze(2)
+
+
+def mock_decode_contiguous(q, k, v, kcache, vcache, seq, scale, mask=None):
+    """The reference's CPU decode on its own layout, op for op
+    (test_custom_kernel.py:431-486 for mask=None or [B, L];
+    :178-216 when `mask` is [B, 1, 1, 1, L]).
+
+    kcache/vcache: [B, Hkv, 1, max_seq, D] contiguous per-sequence caches
+    (cache b belongs to sequence b). Mutates the caches; returns q.dtype.
+    This is the CPU path the benchmark times as the baseline.
+    """
+    B, Hkv, G, _, D = q.shape
+    max_seq = kcache.shape[-2]
+    outs = []
+    for b in range(B):
+        p = int(seq[b, 0])
+        if p < max_seq:
+            kcache[b, :, :, p, :] = k[b].squeeze(-2)
+            vcache[b, :, :, p, :] = v[b].squeeze(-2)
+        ks = kcache[b].unsqueeze(0)[..., :D].unsqueeze(2)
+        vs = vcache[b].unsqueeze(0)[..., :D].unsqueeze(2)
+        qi = q[b].view(Hkv, 1, G, 1, D)
+        w = torch.matmul(qi, ks.transpose(-1, -2)) * scale
+        if mask is not None and mask.dim() == 5:
+            add = torch.where(mask[b, :, :, :, :max_seq] > 0, 0.0, -float("inf"))
+        elif mask is not None:
+            add = torch.where(mask[b:b + 1].view(1, 1, 1, 1, -1)[..., :max_seq] > 0, 0.0, -float("inf"))
+        else:
+            n = min(p + 1, max_seq)
+            add = torch.full((1, max_seq), -float("inf"), dtype=q.dtype)
+            add[:, :n] = 0.0
+            add = add.view(1, 1, 1, 1, max_seq)
+        w = torch.softmax(w + add, dim=-1, dtype=torch.float32).to(q.dtype)
+        outs.append(torch.matmul(w, vs).view(Hkv, G, 1, D))
+    return torch.stack(outs, 0)

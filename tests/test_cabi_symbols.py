@@ -1,0 +1,116 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every entry
+point include/*.h declares, and the ctypes struct matches the C layout."""
+
+import ctypes
+import glob
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"^\s*(?:int|size_t|void|const char\s*\*)\s+(rbln_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_headers_declare_entry_points():
+    names = declared_functions()
+    assert "rbln_paged_causal_attn_decode" in names and "rbln_paged_attn_decode" in names
+
+
+def test_library_exports_every_declared_symbol():
+    from torch_rbln_b200 import cabi
+
+    lib = ctypes.CDLL(cabi._LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    assert set(cabi.ENTRY_POINTS) <= set(declared_functions())
+
+
+def test_abi_version_and_struct_size():
+    from torch_rbln_b200 import cabi
+
+    L = cabi.lib()
+    assert L.rbln_attn_abi_version() == 1
+    assert L.rbln_paged_attn_params_sizeof() == ctypes.sizeof(cabi.PagedAttnParams)
+
+
+def test_struct_field_offsets_match_c():
+    from torch_rbln_b200 import cabi
+
+    fields = [f for f, _ in cabi.PagedAttnParams._fields_]
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"rbln_attn.h\"\nint main(void){\n"
+    for f in fields:
+        src += f'  printf("%zu\\n", offsetof(rbln_paged_attn_params_t, {f}));\n'
+    src += "  return 0;\n}\n"
+    with tempfile.TemporaryDirectory() as td:
+        c = os.path.join(td, "off.c")
+        exe = os.path.join(td, "off")
+        open(c, "w").write(src)
+        cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+        r = subprocess.run(["gcc", c, "-o", exe, "-I", os.path.join(ROOT, "include"), "-I", cuda_inc],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            pytest.skip("gcc or CUDA headers unavailable: " + r.stderr[-200:])
+        offs = [int(x) for x in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    got = [getattr(cabi.PagedAttnParams, f).offset for f in fields]
+    assert offs == got
+
+
+def test_torch_ops_registered_with_reference_schemas():
+    import torch
+    import torch_rbln_b200  # noqa: F401
+
+    ops = torch.ops.rbln_custom_ops
+    assert str(ops.paged_attn_decode.default._schema) == (
+        "rbln_custom_ops::paged_attn_decode(Tensor q, Tensor k, Tensor v, Tensor mask, Tensor(a4!) kcache, "
+        "Tensor(a5!) vcache, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size) -> Tensor")
+    assert str(ops.paged_causal_attn_decode.default._schema) == (
+        "rbln_custom_ops::paged_causal_attn_decode(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, "
+        "Tensor(a4!) vcache, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, "
+        "Tensor? mask=None) -> Tensor")
+    assert str(ops.paged_causal_attn_prefill.default._schema) == (
+        "rbln_custom_ops::paged_causal_attn_prefill(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, "
+        "Tensor(a4!) vcache, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, "
+        "bool is_bidirectional, Tensor? mask=None) -> Tensor")
+    assert str(ops.paged_attn_prefill.default._schema) == (
+        "rbln_custom_ops::paged_attn_prefill(Tensor q, Tensor k, Tensor v, Tensor mask, Tensor(a4!) kcache, "
+        "Tensor(a5!) vcache, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size) -> Tensor")
+
+
+def test_fake_kernels_give_q_metadata():
+    import torch
+    import torch_rbln_b200  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        q = torch.empty(2, 8, 4, 1, 64, dtype=torch.float16)
+        k = torch.empty(2, 8, 1, 1, 64, dtype=torch.float16)
+        kc = torch.empty(4, 8, 1, 16, 64, dtype=torch.float16)
+        out = torch.ops.rbln_custom_ops.paged_causal_attn_decode(
+            q, k, k, kc, kc, torch.empty(2, 1, dtype=torch.int32), torch.empty(()), torch.empty(2, 2, dtype=torch.int32), 16)
+        assert out.shape == q.shape and out.dtype == q.dtype
+
+
+def test_cpu_tensors_are_rejected_no_fallback():
+    """No CPU fallback: the ops have no CPU kernel."""
+    import torch
+    import torch_rbln_b200  # noqa: F401
+
+    q = torch.zeros(1, 1, 4, 1, 64, dtype=torch.bfloat16)
+    k = torch.zeros(1, 1, 1, 1, 64, dtype=torch.bfloat16)
+    kc = torch.zeros(2, 1, 1, 16, 64, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        torch.ops.rbln_custom_ops.paged_causal_attn_decode(
+            q, k, k, kc, kc, torch.zeros(1, 1, dtype=torch.int32), torch.tensor(0.125),
+            torch.zeros(1, 2, dtype=torch.int32), 16)

@@ -1,0 +1,189 @@
+"""Pins the CPU oracle to the reference's own outputs (tests/golden/*.pt).
+
+The fixtures were produced by running the reference's CPU definitions
+(test/rbln/test_custom_kernel.py:31-486 and sdpa.py:_sdpa_cpu_fallback) in
+tests/golden/make_golden.py. The oracle's mode="mock" must match them bit
+for bit on the reference's single-block configurations; mode="fp32" must
+match within the reference's own tolerance (test_custom_kernel.py:654-655).
+"""
+
+import hashlib
+import math
+import os
+
+import pytest
+import torch
+
+from oracle import paged_attention as opa
+from oracle import sdpa as osd
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+RTOL, ATOL = 1e-3, 1.2e-2
+
+
+def _tol(dtype):
+    """The reference's tolerance (test_custom_kernel.py:654-655, float16). The
+    reference's bfloat16 path rounds the scores to bfloat16 (8-bit mantissa),
+    so its distance from an exact fp32 evaluation is wider."""
+    return dict(rtol=1.6e-2, atol=3e-2) if dtype == torch.bfloat16 else dict(rtol=RTOL, atol=ATOL)
+
+
+def _load(name):
+    return torch.load(os.path.join(GOLDEN, name), weights_only=False)
+
+
+def _sha(t):
+    return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def _full(pre, max_seq):
+    B, H, one, P, D = pre.shape
+    c = torch.zeros([B, H, one, max_seq, D], dtype=pre.dtype)
+    c[:, :, :, :P] = pre
+    return c
+
+
+DECODE = _load("paged_decode.pt")
+PREFILL = _load("paged_prefill.pt")
+
+
+@pytest.mark.parametrize("idx", range(len(DECODE)))
+@pytest.mark.parametrize("op", ["paged_attn_decode", "paged_causal_attn_decode", "paged_causal_attn_decode_pmask"])
+def test_decode_oracle_matches_reference(idx, op):
+    c = DECODE[idx]
+    exp = c["results"][op]
+    scale = torch.tensor(1.0 / math.sqrt(c["D"]))
+    bt = torch.tensor([[0], [1]], dtype=torch.int16)
+    mask = {"paged_attn_decode": c["mask"], "paged_causal_attn_decode": None,
+            "paged_causal_attn_decode_pmask": c["pmask"]}[op]
+    for mode in ("mock", "fp32"):
+        kc, vc = _full(c["kpre"], c["max_seq"]), _full(c["vpre"], c["max_seq"])
+        out = opa.paged_decode(c["q"], c["k"], c["v"], kc, vc, c["ctx"], scale, bt, c["max_seq"], mask, mode=mode)
+        if mode == "mock":
+            assert out.dtype == exp["out"].dtype and out.shape == exp["out"].shape
+            assert torch.equal(out, exp["out"]), f"max diff {(out.float() - exp['out'].float()).abs().max()}"
+        else:
+            torch.testing.assert_close(out, exp["out"].float(), **_tol(c["dtype"]))
+        rows_k = torch.stack([kc[b, :, 0, int(c["ctx"][b, 0])] for b in range(c["B"])])
+        rows_v = torch.stack([vc[b, :, 0, int(c["ctx"][b, 0])] for b in range(c["B"])])
+        assert torch.equal(rows_k, exp["krow"]) and torch.equal(rows_v, exp["vrow"])
+
+
+@pytest.mark.parametrize("idx", range(len(PREFILL)))
+@pytest.mark.parametrize("op", ["paged_attn_prefill_s0", "paged_attn_prefill_s1", "paged_causal_attn_prefill",
+                                "paged_causal_attn_prefill_bidir"])
+def test_prefill_oracle_matches_reference(idx, op):
+    c = PREFILL[idx]
+    exp = c["results"][op]
+    D, S, ms, dt = c["D"], c["S"], c["max_seq"], c["dtype"]
+    scale = torch.tensor(1.0 / math.sqrt(D))
+    bt = torch.tensor([0], dtype=torch.int16)
+    for mode in ("mock", "fp32"):
+        kc = torch.zeros([1, c["Hkv"], 1, ms, D], dtype=dt)
+        vc = torch.zeros_like(kc)
+        kw = {}
+        if op == "paged_attn_prefill_s0":
+            kw["mask"] = torch.ones([1, S, ms], dtype=dt).tril().view(1, 1, 1, S, ms)
+        elif op == "paged_attn_prefill_s1":
+            s1 = c["s1"]
+            kc[:, :, :, :s1] = c["kpre"]
+            vc[:, :, :, :s1] = c["vpre"]
+            kw["mask"] = torch.ones([1, S, ms], dtype=dt).tril(diagonal=s1).view(1, 1, 1, S, ms)
+        elif op == "paged_causal_attn_prefill":
+            kw["causal"] = True
+        else:
+            pm = torch.zeros([1, ms], dtype=dt)
+            pm[:, :S] = 1
+            kw["causal"] = False
+            kw["position_mask"] = pm
+        seq = torch.tensor([[exp["seq"]]], dtype=torch.int32)
+        out = opa.paged_prefill(c["q"], c["k"], c["v"], kc, vc, seq, scale, bt, ms, mode=mode, **kw)
+        if mode == "mock":
+            assert torch.equal(out, exp["out"]), f"max diff {(out.float() - exp['out'].float()).abs().max()}"
+        else:
+            torch.testing.assert_close(out, exp["out"].float(), **_tol(dt))
+        assert _sha(kc) == exp["kc"] and _sha(vc) == exp["vc"]
+
+
+def test_offset_causal_equals_explicit_mask():
+    """paged_causal_attn_prefill's offset-causal rule (the generalisation) equals
+    the reference's paged_attn_prefill driven by an offset tril keep-mask."""
+    c = PREFILL[0]
+    D, S, ms, dt, s1 = c["D"], c["S"], c["max_seq"], c["dtype"], c["s1"]
+    scale = torch.tensor(1.0 / math.sqrt(D))
+    bt = torch.tensor([0], dtype=torch.int16)
+    seq = torch.tensor([[s1]], dtype=torch.int32)
+    kc = torch.zeros([1, c["Hkv"], 1, ms, D], dtype=dt)
+    vc = torch.zeros_like(kc)
+    kc[:, :, :, :s1], vc[:, :, :, :s1] = c["kpre"], c["vpre"]
+    out = opa.paged_prefill(c["q"], c["k"], c["v"], kc.clone(), vc.clone(), seq, scale, bt, ms, causal=True,
+                            mode="mock")
+    assert torch.equal(out, c["results"]["paged_attn_prefill_s1"]["out"])
+
+
+SDPA = _load("sdpa_small.pt")
+
+
+@pytest.mark.parametrize("idx", range(len(SDPA)))
+def test_sdpa_oracle_matches_reference(idx):
+    c = SDPA[idx]
+    out = osd.sdpa_reference(c["q"], c["k"], c["v"], c["mask"], 0.0, c["causal"], None)
+    assert torch.equal(out, c["out"])
+    ref = osd.sdpa_math(c["q"], c["k"], c["v"], c["mask"], c["causal"])
+    tol = {torch.float32: 1e-5, torch.float16: 2e-3, torch.bfloat16: 2e-2}[c["dtype"]]
+    assert (out.double() - ref).abs().max() / ref.abs().max() < tol
+
+
+def sdpa_config1_inputs():
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn([1, 32, 512, 64], generator=g)
+    k = torch.randn([1, 8, 512, 64], generator=g)
+    v = torch.randn([1, 8, 512, 64], generator=g)
+    return q, k, v
+
+
+def test_sdpa_config1_oracle_matches_reference():
+    fx = _load("sdpa_config1.pt")
+    q, k, v = sdpa_config1_inputs()
+    assert (_sha(q), _sha(k), _sha(v)) == (fx["sha_q"], fx["sha_k"], fx["sha_v"])
+    out = osd.sdpa_reference(q, k, v, None, 0.0, True, 1.0 / 8.0)
+    assert torch.equal(out[0][fx["heads"]][:, fx["rows"]], fx["out_sample"])
+    assert out.double().sum().item() == fx["out_sum"].item()
+    ref = osd.sdpa_math(q, k, v, None, True, 1.0 / 8.0)
+    assert ((out.double() - ref).abs().max() / ref.abs().max()).item() < 1e-5
+
+
+def test_paged_block_table_gather_is_a_permutation():
+    """Scattering a contiguous cache through a random block table and reading it
+    back through the oracle reproduces the contiguous result exactly."""
+    g = torch.Generator().manual_seed(3)
+    B, Hkv, G, D, bs, nblk = 3, 2, 4, 64, 16, 40
+    max_blocks = 8
+    q = torch.randn([B, Hkv, G, 1, D], generator=g)
+    k = torch.randn([B, Hkv, 1, 1, D], generator=g)
+    v = torch.randn([B, Hkv, 1, 1, D], generator=g)
+    seq = torch.tensor([[5], [77], [127]], dtype=torch.int32)
+    perm = torch.randperm(nblk, generator=g)[: B * max_blocks].reshape(B, max_blocks).to(torch.int32)
+    kp = torch.randn([nblk, Hkv, 1, bs, D], generator=g)
+    vp = torch.randn([nblk, Hkv, 1, bs, D], generator=g)
+    out_paged = opa.paged_decode(q, k, v, kp.clone(), vp.clone(), seq, 0.125, perm, bs)
+    # same data laid out contiguously, one block per sequence
+    kc = torch.stack([opa.contiguous_cache(kp, perm, bs, b, D)[0] for b in range(B)])
+    vc = torch.stack([opa.contiguous_cache(vp, perm, bs, b, D)[0] for b in range(B)])
+    bt = torch.arange(B, dtype=torch.int32).reshape(B, 1)
+    out_contig = opa.paged_decode(q, k, v, kc, vc, seq, 0.125, bt, max_blocks * bs)
+    assert torch.equal(out_paged, out_contig)
+
+
+@pytest.mark.parametrize("idx", range(len(DECODE)))
+@pytest.mark.parametrize("op", ["paged_attn_decode", "paged_causal_attn_decode", "paged_causal_attn_decode_pmask"])
+def test_contiguous_mock_restatement_matches_reference(idx, op):
+    """The CPU-baseline restatement (reference layout) equals the reference bit for bit."""
+    c = DECODE[idx]
+    exp = c["results"][op]
+    mask = {"paged_attn_decode": c["mask"], "paged_causal_attn_decode": None,
+            "paged_causal_attn_decode_pmask": c["pmask"]}[op]
+    kc, vc = _full(c["kpre"], c["max_seq"]), _full(c["vpre"], c["max_seq"])
+    out = opa.mock_decode_contiguous(c["q"], c["k"], c["v"], kc, vc, c["ctx"], torch.tensor(1.0 / math.sqrt(c["D"])),
+                                     mask)
+    assert torch.equal(out, exp["out"])

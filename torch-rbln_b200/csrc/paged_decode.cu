@@ -1,0 +1,665 @@
+// Paged-attention decode for sm_100a: one new query token per sequence,
+// G query heads per KV head, KV read through a block table.
+//
+// Semantics follow the reference's CPU definition of
+// rbln_custom_ops::paged_causal_attn_decode / paged_attn_decode
+// (test/rbln/test_custom_kernel.py:138-216, 388-486): append the new k/v at
+// position seq[b] when seq[b] < span, then softmax(q.K^T * scale + mask) . V
+// over the span, generalised from the reference's single-block case to a
+// real block table (position t lives in block block_table[b, t / bs], row
+// t % bs).
+//
+// Design (bandwidth-bound):
+//  * grid = (context splits, Hkv, B); a CTA owns one (sequence, KV head,
+//    context split) and all G query heads of that KV head, so every KV byte
+//    is read from HBM exactly once.
+//  * 4 warps per CTA take 16-token tiles round-robin. A warp loads its tile
+//    straight from HBM into MMA fragments with 16-byte coalesced loads: the
+//    head dimension of K (and of q) is permuted so that each lane's fragment
+//    elements are contiguous in memory, which leaves the dot products
+//    unchanged. No shared-memory staging, no barriers in the main loop.
+//  * Scores use the tensor cores with tokens as M and heads as N:
+//    S^T[16 tok x 8 head] = K[16 x D] . Q^T, then O^T[D x 8] += V^T . P^T. P
+//    goes from the accumulator layout to the B-operand layout with two
+//    movmatrix transposes. fp32 online softmax, max reduced with shuffles.
+//  * fp8-e4m3 caches are converted exactly to f16 in registers
+//    (cvt.rn.f16x2.e4m3x2); the per-(block, head) K scale multiplies the
+//    scores and the V scale is folded into P before the PV product.
+//  * Splits write (O/l, log2-sum-exp) partials; a merge kernel combines them.
+//    A sequence that needs one split is written directly by its CTA.
+
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace rbln {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 16;
+
+enum KvKind { KV_BF16 = 0, KV_F16 = 1, KV_FP8 = 2 };
+
+struct DecodeArgs {
+  const char* q;
+  int64_t qs_b, qs_h, qs_g;  // bytes
+  char* out;
+  int64_t os_b, os_h, os_g;  // bytes
+  const char* k_new;
+  const char* v_new;
+  int64_t kn_b, kn_h, vn_b, vn_h;  // bytes
+  char* kcache;
+  char* vcache;
+  int64_t cs_block, cs_head, cs_tok;  // elements
+  const float* k_scale;
+  const float* v_scale;
+  int64_t ss_block, ss_head;
+  const int32_t* seq;
+  int64_t seq_stride;
+  const void* bt;
+  int bt_dtype;
+  int64_t bt_stride;
+  const void* mask;
+  int mask_dtype;
+  int mask_len;
+  int64_t mask_stride;
+  float scale;
+  const float* scale_dev;
+  int B, Hkv, G, num_blocks, bs, span;
+  int chunk;
+  int max_splits;
+  float* part_o;    // [B][Hkv][max_splits][G][D]
+  float* part_lse;  // [B][Hkv][max_splits][G]  (log2 domain)
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void flag_error(uint32_t* err, uint32_t bit) {
+  if (err) atomicOr(err, bit);
+}
+
+// Context length seen by sequence b, and the number of splits covering it.
+__device__ __forceinline__ void decode_extent(const DecodeArgs& a, int b, int& pos, int& L,
+                                              int& nsplit) {
+  pos = a.seq[b * a.seq_stride];
+  if (a.mask) {
+    L = min(a.span, a.mask_len);
+  } else {
+    L = pos < 0 ? 0 : min(pos + 1, a.span);
+  }
+  nsplit = max(1, (L + a.chunk - 1) / a.chunk);
+}
+
+template <int D, int KV>
+struct Cfg {
+  static constexpr int SZ = (KV == KV_FP8) ? 1 : 2;  // bytes per cache element
+  static constexpr int ROW = D * SZ;                  // bytes per token row
+  static constexpr int KCH = ROW / 64;                // 16-B K chunks per lane per row
+  static constexpr int KR = D / 8;                    // u32 MMA registers per K row
+  static constexpr int VSEG = (KV == KV_FP8) ? ((D == 128) ? 16 : 8) : 8;  // contiguous d per seg
+  static constexpr int NVE = D / 8;                   // d values per lane per V row
+  static constexpr int NSEG = NVE / VSEG;             // 2 for 16-bit D=128, else 1
+  static constexpr int NVW = NVE * SZ / 4;            // raw u32 per lane per V row
+  static constexpr int MT = D / 16;                   // PV m-tiles
+  static constexpr bool MMA_BF16 = (KV == KV_BF16);
+};
+
+// d index of a lane's e-th V value (gid = lane/4).
+template <int D, int KV>
+__device__ __forceinline__ int v_dim(int gid, int e) {
+  using C = Cfg<D, KV>;
+  return gid * C::VSEG + (e / C::VSEG) * 64 + (e % C::VSEG);
+}
+
+template <int D, int KV, bool Q_BF16, int NT>
+__global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_split_kernel(const DecodeArgs a) {
+  using C = Cfg<D, KV>;
+  constexpr bool MB = C::MMA_BF16;
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+
+  int pos, L, nsplit;
+  decode_extent(a, b, pos, L, nsplit);
+  if (split >= nsplit) return;
+  if (pos < 0 && tid == 0 && split == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
+  const int t0 = split * a.chunk;
+  const int t1 = min(t0 + a.chunk, L);
+
+  // ---- append the new token (write-then-read, like the reference) --------
+  if (a.k_new != nullptr && pos >= 0 && pos < a.span && min(pos / a.chunk, nsplit - 1) == split) {
+    const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + pos / a.bs);
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (tid == 0) flag_error(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    } else {
+      const int64_t row = (blk * a.cs_block + h * a.cs_head + (pos % a.bs) * a.cs_tok) * C::SZ;
+      const int part = tid >> 6;  // 0: K, 1: V
+      const int j = tid & 63;     // 8 elements per thread
+      if (j < D / 8) {
+        const char* src = (part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h
+                                     : a.v_new + b * a.vn_b + h * a.vn_h) + j * 16;
+        char* dst = (part == 0 ? a.kcache : a.vcache) + row;
+        const uint4 x = *reinterpret_cast<const uint4*>(src);
+        if constexpr (KV != KV_FP8) {
+          *reinterpret_cast<uint4*>(dst + j * 16) = x;
+        } else {
+          const float sc = (part == 0 ? a.k_scale : a.v_scale)[blk * a.ss_block + h * a.ss_head];
+          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+          uint32_t o[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            float f[4];
+            float2 lo = unpack2<Q_BF16>(w[2 * k]), hi = unpack2<Q_BF16>(w[2 * k + 1]);
+            f[0] = lo.x / sc; f[1] = lo.y / sc; f[2] = hi.x / sc; f[3] = hi.y / sc;
+            __nv_fp8x2_storage_t p01 = __nv_cvt_float2_to_fp8x2(make_float2(f[0], f[1]), __NV_SATFINITE, __NV_E4M3);
+            __nv_fp8x2_storage_t p23 = __nv_cvt_float2_to_fp8x2(make_float2(f[2], f[3]), __NV_SATFINITE, __NV_E4M3);
+            o[k] = uint32_t(p01) | (uint32_t(p23) << 16);
+          }
+          *reinterpret_cast<uint2*>(dst + j * 8) = make_uint2(o[0], o[1]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- query fragments: B operand (k = head_dim, n = head) ---------------
+  float scale = a.scale_dev ? *a.scale_dev : a.scale;
+  uint32_t qf[NT][C::KR];
+  float qmax = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int g = gid + 8 * nt;
+    const bool live = g < a.G;
+    const char* qrow = a.q + b * a.qs_b + h * a.qs_h + (int64_t)g * a.qs_g;
+#pragma unroll
+    for (int i = 0; i < C::KCH; ++i) {
+      if constexpr (KV != KV_FP8) {
+        uint4 x = live ? *reinterpret_cast<const uint4*>(qrow + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
+        qf[nt][4 * i + 0] = x.x; qf[nt][4 * i + 1] = x.y; qf[nt][4 * i + 2] = x.z; qf[nt][4 * i + 3] = x.w;
+      } else {
+        // 16 fp8 K elements <-> 16 q elements (32 bytes) at d = 16*(4i+tig)
+        const char* src = qrow + (4 * i + tig) * 32;
+        uint4 x0 = live ? *reinterpret_cast<const uint4*>(src) : make_uint4(0, 0, 0, 0);
+        uint4 x1 = live ? *reinterpret_cast<const uint4*>(src + 16) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          qf[nt][8 * i + k] = w[k];
+          float2 f = unpack2<Q_BF16>(w[k]);
+          qmax = fmaxf(qmax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+  }
+  float qk_mult = scale * kLog2e;
+  if constexpr (KV == KV_FP8) {
+    // q goes to f16 for the f16 MMA. A bf16 q is rescaled by a power of two
+    // so its largest magnitude sits in [2^14, 2^15): exact, no overflow.
+    float qs = 1.f;
+    if constexpr (Q_BF16) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
+      if (qmax > 0.f) {
+        int ex;
+        frexpf(qmax, &ex);
+        ex = min(max(15 - ex, -120), 120);
+        qs = ldexpf(1.f, ex);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int k = 0; k < C::KR; ++k) {
+          float2 f = unpack2<true>(qf[nt][k]);
+          qf[nt][k] = pack2<false>(f.x * qs, f.y * qs);
+        }
+    }
+    qk_mult = qk_mult / qs;
+  }
+
+  // ---- main loop over this warp's tiles -----------------------------------
+  float o_acc[NT][C::MT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o_acc[nt][mt][k] = 0.f;
+  float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = neg_inf();
+    l_run[nt][0] = l_run[nt][1] = 0.f;
+  }
+
+  const char* kc = a.kcache;
+  const char* vc = a.vcache;
+  const int tv0 = 2 * tig, tv1 = 2 * tig + 1, tv2 = 2 * tig + 8, tv3 = 2 * tig + 9;
+
+  for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile) {
+    // per-token row offsets: lane l (mod 16) resolves token ts + l
+    const int tpos = ts + (lane & 15);
+    bool valid = tpos < t1;
+    if (valid && a.mask) valid = load_keep(a.mask, a.mask_dtype, b * a.mask_stride + tpos);
+    uint32_t off16 = 0;  // row byte offset / 16
+    float ksc = 1.f, vsc = 1.f;
+    if (valid) {
+      const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + tpos / a.bs);
+      if (blk < 0 || blk >= a.num_blocks) {
+        valid = false;
+        flag_error(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+      } else {
+        off16 = (uint32_t)(((blk * a.cs_block + h * a.cs_head + (tpos % a.bs) * a.cs_tok) * C::SZ) >> 4);
+        if constexpr (KV == KV_FP8) {
+          ksc = a.k_scale[blk * a.ss_block + h * a.ss_head];
+          vsc = a.v_scale[blk * a.ss_block + h * a.ss_head];
+        }
+      }
+    }
+    const uint32_t vmask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
+    if (vmask == 0) continue;
+
+    const uint32_t ok0 = __shfl_sync(0xffffffffu, off16, gid);
+    const uint32_t ok1 = __shfl_sync(0xffffffffu, off16, gid + 8);
+    const bool vk0 = (vmask >> gid) & 1, vk1 = (vmask >> (gid + 8)) & 1;
+    uint32_t ov[4];
+    bool vv[4];
+    ov[0] = __shfl_sync(0xffffffffu, off16, tv0); vv[0] = (vmask >> tv0) & 1;
+    ov[1] = __shfl_sync(0xffffffffu, off16, tv1); vv[1] = (vmask >> tv1) & 1;
+    ov[2] = __shfl_sync(0xffffffffu, off16, tv2); vv[2] = (vmask >> tv2) & 1;
+    ov[3] = __shfl_sync(0xffffffffu, off16, tv3); vv[3] = (vmask >> tv3) & 1;
+
+    // K rows gid and gid+8, chunks 4i+tig
+    uint4 kraw[2][C::KCH];
+#pragma unroll
+    for (int i = 0; i < C::KCH; ++i) {
+      kraw[0][i] = vk0 ? ld_stream_v4(kc + (size_t)ok0 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
+      kraw[1][i] = vk1 ? ld_stream_v4(kc + (size_t)ok1 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
+    }
+    // V rows tv0..tv3, this lane's d segments
+    uint32_t vraw[4][C::NVW];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const char* rowp = vc + (size_t)ov[j] * 16;
+      if constexpr (C::NVW >= 4) {
+#pragma unroll
+        for (int sg = 0; sg < C::NVW / 4; ++sg) {
+          uint4 x = vv[j] ? ld_stream_v4(rowp + (gid * C::VSEG + sg * 64) * C::SZ) : make_uint4(0, 0, 0, 0);
+          vraw[j][4 * sg + 0] = x.x; vraw[j][4 * sg + 1] = x.y;
+          vraw[j][4 * sg + 2] = x.z; vraw[j][4 * sg + 3] = x.w;
+        }
+      } else {
+        uint2 x = vv[j] ? ld_stream_v2(rowp + gid * C::VSEG * C::SZ) : make_uint2(0, 0);
+        vraw[j][0] = x.x; vraw[j][1] = x.y;
+      }
+    }
+
+    // S^T = K . Q^T
+    float s[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    if constexpr (KV != KV_FP8) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int i = kk >> 1, sgl = (kk & 1) * 2;
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&kraw[0][i]);
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&kraw[1][i]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          mma16816<MB>(s[nt], r0[sgl], r1[sgl], r0[sgl + 1], r1[sgl + 1], qf[nt][2 * kk], qf[nt][2 * kk + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < C::KCH; ++i) {
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&kraw[0][i]);
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&kraw[1][i]);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {  // kk = 4i + w uses chunk word w (4 fp8)
+          const uint32_t a0 = e4m3x2_to_f16x2(r0[w] & 0xffffu), a2 = e4m3x2_to_f16x2(r0[w] >> 16);
+          const uint32_t a1 = e4m3x2_to_f16x2(r1[w] & 0xffffu), a3 = e4m3x2_to_f16x2(r1[w] >> 16);
+          const int kk = 4 * i + w;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma16816<false>(s[nt], a0, a1, a2, a3, qf[nt][2 * kk], qf[nt][2 * kk + 1]);
+        }
+      }
+    }
+
+    // online softmax (log2 domain); rows gid / gid+8 are tokens
+    float k0m = qk_mult, k1m = qk_mult;
+    float vs0 = 1.f, vs1 = 1.f;
+    if constexpr (KV == KV_FP8) {
+      k0m *= __shfl_sync(0xffffffffu, ksc, gid);
+      k1m *= __shfl_sync(0xffffffffu, ksc, gid + 8);
+      vs0 = __shfl_sync(0xffffffffu, vsc, gid);
+      vs1 = __shfl_sync(0xffffffffu, vsc, gid + 8);
+    }
+    uint32_t pb0[NT], pb1[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float x0 = vk0 ? s[nt][0] * k0m : neg_inf();
+      const float x1 = vk0 ? s[nt][1] * k0m : neg_inf();
+      const float x2 = vk1 ? s[nt][2] * k1m : neg_inf();
+      const float x3 = vk1 ? s[nt][3] * k1m : neg_inf();
+      const float mx0 = warp_max_xor_rows(fmaxf(x0, x2));
+      const float mx1 = warp_max_xor_rows(fmaxf(x1, x3));
+      const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
+      const float ms0 = (mn0 == neg_inf()) ? 0.f : mn0;
+      const float ms1 = (mn1 == neg_inf()) ? 0.f : mn1;
+      const float al0 = exp2_approx(m_run[nt][0] - ms0), al1 = exp2_approx(m_run[nt][1] - ms1);
+      const float p0 = exp2_approx(x0 - ms0), p2 = exp2_approx(x2 - ms0);
+      const float p1 = exp2_approx(x1 - ms1), p3 = exp2_approx(x3 - ms1);
+      l_run[nt][0] = l_run[nt][0] * al0 + p0 + p2;
+      l_run[nt][1] = l_run[nt][1] * al1 + p1 + p3;
+      m_run[nt][0] = mn0;
+      m_run[nt][1] = mn1;
+#pragma unroll
+      for (int mt = 0; mt < C::MT; ++mt) {
+        o_acc[nt][mt][0] *= al0; o_acc[nt][mt][2] *= al0;
+        o_acc[nt][mt][1] *= al1; o_acc[nt][mt][3] *= al1;
+      }
+      pb0[nt] = movmatrix_trans(pack2<MB>(p0 * vs0, p1 * vs0));
+      pb1[nt] = movmatrix_trans(pack2<MB>(p2 * vs1, p3 * vs1));
+    }
+
+    // O^T += V^T . P^T
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      if constexpr (KV != KV_FP8) {
+        a0 = prmt(vraw[0][mt], vraw[1][mt], 0x5410);
+        a1 = prmt(vraw[0][mt], vraw[1][mt], 0x7632);
+        a2 = prmt(vraw[2][mt], vraw[3][mt], 0x5410);
+        a3 = prmt(vraw[2][mt], vraw[3][mt], 0x7632);
+      } else {
+        const int w = mt >> 1;
+        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+        const uint32_t x = prmt(vraw[0][w], vraw[1][w], sel);
+        const uint32_t y = prmt(vraw[2][w], vraw[3][w], sel);
+        a0 = e4m3x2_to_f16x2(x & 0xffffu);
+        a1 = e4m3x2_to_f16x2(x >> 16);
+        a2 = e4m3x2_to_f16x2(y & 0xffffu);
+        a3 = e4m3x2_to_f16x2(y >> 16);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816<MB>(o_acc[nt][mt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
+    }
+  }
+
+  // ---- combine the 4 warps of this CTA ------------------------------------
+  constexpr int GP = 8 * NT;
+  __shared__ float sO[kWarps][GP][D];
+  __shared__ float sM[kWarps][GP], sL[kWarps][GP];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const float l0 = warp_sum_xor_rows(l_run[nt][0]);
+    const float l1 = warp_sum_xor_rows(l_run[nt][1]);
+    const int h0 = 2 * tig + 8 * nt;
+    if (gid == 0) {
+      sM[warp][h0] = m_run[nt][0]; sM[warp][h0 + 1] = m_run[nt][1];
+      sL[warp][h0] = l0; sL[warp][h0 + 1] = l1;
+    }
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt) {
+      const int d0 = v_dim<D, KV>(gid, 2 * mt), d1 = v_dim<D, KV>(gid, 2 * mt + 1);
+      sO[warp][h0][d0] = o_acc[nt][mt][0];
+      sO[warp][h0 + 1][d0] = o_acc[nt][mt][1];
+      sO[warp][h0][d1] = o_acc[nt][mt][2];
+      sO[warp][h0 + 1][d1] = o_acc[nt][mt][3];
+    }
+  }
+  __syncthreads();
+
+  const bool final_out = (nsplit == 1);
+  for (int idx = tid; idx < a.G * (D / 4); idx += kThreads) {
+    const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+    float M = neg_inf();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sM[w][g]);
+    float Lsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = (sM[w][g] == neg_inf()) ? 0.f : exp2_approx(sM[w][g] - M);
+      Lsum += f * sL[w][g];
+      const float4 o = *reinterpret_cast<const float4*>(&sO[w][g][d4]);
+      acc.x += f * o.x; acc.y += f * o.y; acc.z += f * o.z; acc.w += f * o.w;
+    }
+    const float inv = 1.f / Lsum;
+    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    if (final_out) {
+      char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
+    } else {
+      const int64_t slot = ((int64_t)(b * a.Hkv + h) * a.max_splits + split) * a.G + g;
+      *reinterpret_cast<float4*>(a.part_o + slot * D + d4) = acc;
+      if (d4 == 0) a.part_lse[slot] = (M == neg_inf()) ? neg_inf() : M + __log2f(Lsum);
+    }
+  }
+}
+
+// Combines the per-split partials of one (sequence, KV head).
+template <int D, bool Q_BF16>
+__global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int pos, L, nsplit;
+  decode_extent(a, b, pos, L, nsplit);
+  if (nsplit <= 1) return;
+  extern __shared__ float sw[];  // [nsplit][G] weights, then [G] flags
+  float* s_lse = sw + nsplit * a.G;
+  const int64_t base = (int64_t)(b * a.Hkv + h) * a.max_splits;
+  for (int g = warp; g < a.G; g += kWarps) {
+    float M = neg_inf();
+    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, a.part_lse[(base + s) * a.G + g]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float S = 0.f;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float l = a.part_lse[(base + s) * a.G + g];
+      const float w = (l == neg_inf()) ? 0.f : exp2_approx(l - M);
+      sw[s * a.G + g] = w;
+      S += w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    if (lane == 0) s_lse[g] = (M == neg_inf()) ? 0.f : 1.f / S;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < a.G * (D / 4); idx += kThreads) {
+    const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = sw[s * a.G + g];
+      if (w != 0.f) {
+        const float4 o = *reinterpret_cast<const float4*>(a.part_o + ((base + s) * a.G + g) * D + d4);
+        acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
+      }
+    }
+    float inv = s_lse[g];
+    if (inv == 0.f) inv = pos_nan();  // every position masked: NaN, as softmax of all -inf
+    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int dtype_bytes(int dt) {
+  switch (dt) {
+    case RBLN_DT_F32: case RBLN_DT_I32: return 4;
+    case RBLN_DT_F16: case RBLN_DT_BF16: case RBLN_DT_I16: return 2;
+    case RBLN_DT_I64: return 8;
+    default: return 1;
+  }
+}
+
+int choose_chunk(const rbln_paged_attn_params_t* p, int span) {
+  if (p->num_splits > 0) {
+    int c = (span + p->num_splits - 1) / p->num_splits;
+    return std::max(64, (c + 63) / 64 * 64);
+  }
+  // Aim at roughly 16 CTAs per SM over the whole launch (the span is an
+  // upper bound of the real context), never below 256 tokens per split.
+  const int64_t target_ctas = 148LL * 16;
+  int64_t c = ((int64_t)span * p->batch * p->num_kv_heads + target_ctas - 1) / target_ctas;
+  c = (c + 63) / 64 * 64;
+  c = std::max<int64_t>(c, 256);
+  c = std::min<int64_t>(c, std::max(span, 64));
+  return (int)((c + 63) / 64 * 64);
+}
+
+struct Plan {
+  int span, chunk, max_splits;
+  size_t ws_bytes;
+};
+
+int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
+  if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 ||
+      p->max_blocks <= 0 || p->num_blocks <= 0)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->head_dim != 64 && p->head_dim != 128) return RBLN_ERR_UNSUPPORTED;
+  if (p->group > 16) return RBLN_ERR_UNSUPPORTED;
+  const int64_t span64 = (int64_t)p->max_blocks * p->block_size;
+  if (span64 > (1 << 30)) return RBLN_ERR_UNSUPPORTED;
+  pl->span = (int)span64;
+  pl->chunk = choose_chunk(p, pl->span);
+  pl->max_splits = (pl->span + pl->chunk - 1) / pl->chunk;
+  if (pl->max_splits > 2048) return RBLN_ERR_UNSUPPORTED;
+  pl->ws_bytes = 0;
+  if (pl->max_splits > 1) {
+    const size_t slots = (size_t)p->batch * p->num_kv_heads * pl->max_splits * p->group;
+    pl->ws_bytes = slots * p->head_dim * sizeof(float) + slots * sizeof(float) + 256;
+  }
+  return RBLN_OK;
+}
+
+template <int D, int KV, bool QB, int NT>
+int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
+  dim3 grid(pl.max_splits, a.Hkv, a.B);
+  if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
+  paged_decode_split_kernel<D, KV, QB, NT><<<grid, kThreads, 0, st>>>(a);
+  if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
+  if (pl.max_splits > 1) {
+    const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);
+    if (smem > 48 * 1024) {
+      cudaFuncSetAttribute(paged_decode_merge_kernel<D, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    }
+    paged_decode_merge_kernel<D, QB><<<dim3(a.Hkv, a.B), kThreads, smem, st>>>(a);
+  }
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+template <int D, int KV, bool QB>
+int launch_nt(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
+  return a.G <= 8 ? launch_typed<D, KV, QB, 1>(a, pl, st, ev) : launch_typed<D, KV, QB, 2>(a, pl, st, ev);
+}
+
+template <int D>
+int launch_d(const DecodeArgs& a, const Plan& pl, int kv_dt, int q_dt, cudaStream_t st, void* const* ev) {
+  if (kv_dt == RBLN_DT_BF16 && q_dt == RBLN_DT_BF16) return launch_nt<D, KV_BF16, true>(a, pl, st, ev);
+  if (kv_dt == RBLN_DT_F16 && q_dt == RBLN_DT_F16) return launch_nt<D, KV_F16, false>(a, pl, st, ev);
+  if (kv_dt == RBLN_DT_FP8_E4M3 && q_dt == RBLN_DT_BF16) return launch_nt<D, KV_FP8, true>(a, pl, st, ev);
+  if (kv_dt == RBLN_DT_FP8_E4M3 && q_dt == RBLN_DT_F16) return launch_nt<D, KV_FP8, false>(a, pl, st, ev);
+  return RBLN_ERR_UNSUPPORTED;
+}
+
+int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_mask) {
+  Plan pl;
+  int rc = plan_decode(p, &pl);
+  if (rc != RBLN_OK) return rc;
+  if (require_mask && !p->mask) return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->batch == 0) return RBLN_OK;
+  if (!p->q || !p->out || !p->kcache || !p->vcache || !p->seq || !p->block_table)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->q_len != 1) return RBLN_ERR_INVALID_ARGUMENT;
+  if ((p->k_new == nullptr) != (p->v_new == nullptr)) return RBLN_ERR_INVALID_ARGUMENT;
+  const int kv_sz = dtype_bytes(p->kv_dtype);
+  const int q_sz = dtype_bytes(p->q_dtype);
+  if (q_sz != 2) return RBLN_ERR_UNSUPPORTED;
+  if (p->kv_dtype == RBLN_DT_FP8_E4M3 && (!p->k_scale || !p->v_scale)) return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->block_table_dtype != RBLN_DT_I16 && p->block_table_dtype != RBLN_DT_I32 &&
+      p->block_table_dtype != RBLN_DT_I64)
+    return RBLN_ERR_UNSUPPORTED;
+  // 16-byte rows everywhere
+  for (int i = 0; i < 3; ++i)
+    if ((p->cache_stride[i] * kv_sz) % 16 != 0) return RBLN_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 3; ++i)
+    if ((p->q_stride[i] * q_sz) % 16 != 0 || (p->out_stride[i] * q_sz) % 8 != 0)
+      return RBLN_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->q) || !aligned16(p->kcache) || !aligned16(p->vcache) ||
+      (reinterpret_cast<uintptr_t>(p->out) & 7u) != 0)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->k_new) {
+    if (!aligned16(p->k_new) || !aligned16(p->v_new)) return RBLN_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < 2; ++i)
+      if ((p->k_new_stride[i] * q_sz) % 16 != 0 || (p->v_new_stride[i] * q_sz) % 16 != 0)
+        return RBLN_ERR_INVALID_ARGUMENT;
+  }
+  const int64_t cache_bytes_hint = ((int64_t)p->num_blocks * p->cache_stride[0]) * kv_sz;
+  if (cache_bytes_hint / 16 > (int64_t)UINT32_MAX) return RBLN_ERR_UNSUPPORTED;
+  if (pl.max_splits > 1 && (!p->workspace || p->workspace_bytes < pl.ws_bytes)) return RBLN_ERR_WORKSPACE;
+
+  DecodeArgs a{};
+  a.q = static_cast<const char*>(p->q);
+  a.qs_b = p->q_stride[0] * q_sz; a.qs_h = p->q_stride[1] * q_sz; a.qs_g = p->q_stride[2] * q_sz;
+  a.out = static_cast<char*>(p->out);
+  a.os_b = p->out_stride[0] * q_sz; a.os_h = p->out_stride[1] * q_sz; a.os_g = p->out_stride[2] * q_sz;
+  a.k_new = static_cast<const char*>(p->k_new);
+  a.v_new = static_cast<const char*>(p->v_new);
+  a.kn_b = p->k_new_stride[0] * q_sz; a.kn_h = p->k_new_stride[1] * q_sz;
+  a.vn_b = p->v_new_stride[0] * q_sz; a.vn_h = p->v_new_stride[1] * q_sz;
+  a.kcache = static_cast<char*>(p->kcache);
+  a.vcache = static_cast<char*>(p->vcache);
+  a.cs_block = p->cache_stride[0]; a.cs_head = p->cache_stride[1]; a.cs_tok = p->cache_stride[2];
+  a.k_scale = p->k_scale; a.v_scale = p->v_scale;
+  a.ss_block = p->scale_stride[0]; a.ss_head = p->scale_stride[1];
+  a.seq = p->seq; a.seq_stride = p->seq_stride;
+  a.bt = p->block_table; a.bt_dtype = p->block_table_dtype; a.bt_stride = p->block_table_stride;
+  a.mask = p->mask; a.mask_dtype = p->mask_dtype; a.mask_len = p->mask_len; a.mask_stride = p->mask_stride[0];
+  a.scale = p->scale; a.scale_dev = p->scale_dev;
+  a.B = p->batch; a.Hkv = p->num_kv_heads; a.G = p->group; a.num_blocks = p->num_blocks;
+  a.bs = p->block_size; a.span = pl.span; a.chunk = pl.chunk; a.max_splits = pl.max_splits;
+  if (pl.max_splits > 1) {
+    uintptr_t w = (reinterpret_cast<uintptr_t>(p->workspace) + 255) & ~uintptr_t(255);
+    const size_t slots = (size_t)p->batch * p->num_kv_heads * pl.max_splits * p->group;
+    a.part_o = reinterpret_cast<float*>(w);
+    a.part_lse = a.part_o + slots * p->head_dim;
+  }
+  a.err = p->error_flags;
+  if (p->head_dim == 128) return launch_d<128>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
+  return launch_d<64>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
+}
+
+}  // namespace
+}  // namespace rbln
+
+extern "C" {
+
+int rbln_attn_abi_version(void) { return RBLN_ATTN_ABI_VERSION; }
+
+size_t rbln_paged_attn_params_sizeof(void) { return sizeof(rbln_paged_attn_params_t); }
+
+int rbln_paged_decode_workspace_size(const rbln_paged_attn_params_t* p, size_t* bytes) {
+  if (!bytes) return RBLN_ERR_INVALID_ARGUMENT;
+  rbln::Plan pl;
+  const int rc = rbln::plan_decode(p, &pl);
+  if (rc != RBLN_OK) return rc;
+  *bytes = pl.ws_bytes;
+  return RBLN_OK;
+}
+
+int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  return rbln::run_decode(p, stream, /*require_mask=*/false);
+}
+
+int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  return rbln::run_decode(p, stream, /*require_mask=*/true);
+}
+
+}  // extern "C"

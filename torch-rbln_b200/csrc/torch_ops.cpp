@@ -1,0 +1,284 @@
+// PyTorch operator layer: defines the rbln_custom_ops schemas (identical to
+// the ones the reference's torch.library.custom_op definitions generate,
+// test/rbln/test_custom_kernel.py:31-486) and registers CUDA kernels that
+// validate the tensors, allocate the output and scratch from the PyTorch
+// caching allocator, and call the C-ABI entry points of librbln_attn.
+//
+// Argument checks follow the reference frontends
+// (torch_rbln/_internal/register_custom_ops.py:175-450): the cache's last
+// dimension must be a multiple of 64, inputs are made contiguous. Departures,
+// on purpose: the output dtype is q.dtype (not forced fp16), the caller's
+// scale is honoured, batch > 1 prefill is allowed.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstdlib>
+#include <string>
+
+#include "rbln_attn.h"
+
+namespace {
+
+int to_rbln_dtype(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return RBLN_DT_F32;
+    case at::kHalf: return RBLN_DT_F16;
+    case at::kBFloat16: return RBLN_DT_BF16;
+    case at::kFloat8_e4m3fn: return RBLN_DT_FP8_E4M3;
+    case at::kShort: return RBLN_DT_I16;
+    case at::kInt: return RBLN_DT_I32;
+    case at::kLong: return RBLN_DT_I64;
+    case at::kBool: return RBLN_DT_BOOL;
+    case at::kByte: return RBLN_DT_BOOL;
+    default: return -1;
+  }
+}
+
+const char* status_name(int rc) {
+  switch (rc) {
+    case RBLN_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RBLN_ERR_UNSUPPORTED: return "unsupported configuration";
+    case RBLN_ERR_WORKSPACE: return "workspace too small";
+    case RBLN_ERR_LAUNCH: return "kernel launch failed";
+    case RBLN_ERR_NO_DEVICE: return "no sm_100 device";
+    default: return "unknown error";
+  }
+}
+
+bool debug_checks() {
+  static const bool on = [] {
+    const char* e = std::getenv("RBLN_ATTN_CHECK");
+    return e && std::string(e) != "0";
+  }();
+  return on;
+}
+
+// Moves an index/mask tensor to q's device (callers may keep small tensors on
+// the host, as the reference's tests do for `scale`).
+at::Tensor on_device(const at::Tensor& t, const at::Tensor& like) {
+  return t.device() == like.device() ? t : t.to(like.device());
+}
+
+struct Common {
+  at::Tensor q, k, v, seq, bt, mask, scale_dev, out, err;
+  rbln_paged_attn_params_t p{};
+};
+
+// Shared validation and parameter fill for the four paged ops.
+void fill_paged(Common& c, const char* op, const at::Tensor& q_in, const at::Tensor& k_in,
+                const at::Tensor& v_in, at::Tensor& kcache, at::Tensor& vcache, const at::Tensor& seq_in,
+                const at::Tensor& scale, const at::Tensor& block_table_in, int64_t block_size,
+                const std::optional<at::Tensor>& mask_in, bool decode) {
+  TORCH_CHECK(q_in.is_cuda(), op, ": expected CUDA tensors, q is on ", q_in.device());
+  TORCH_CHECK(q_in.dim() == 5 && k_in.dim() == 5 && v_in.dim() == 5, op,
+              ": q/k/v must be 5-D [B, Hkv, G, S, D] / [B, Hkv, 1, S, D]");
+  TORCH_CHECK(kcache.dim() == 5 && vcache.dim() == 5, op,
+              ": kcache/vcache must be 5-D [num_blocks, Hkv, 1, block_size, D]");
+  TORCH_CHECK(kcache.size(-1) % 64 == 0, op,
+              ": the last dimension of K-cache must be a multiple of 64, but got shape ", kcache.sizes());
+  TORCH_CHECK(vcache.size(-1) % 64 == 0, op,
+              ": the last dimension of V-cache must be a multiple of 64, but got shape ", vcache.sizes());
+  TORCH_CHECK(kcache.sizes() == vcache.sizes() && kcache.strides() == vcache.strides() &&
+                  kcache.scalar_type() == vcache.scalar_type(),
+              op, ": kcache and vcache must match in shape, strides and dtype");
+  TORCH_CHECK(kcache.is_cuda() && kcache.device() == q_in.device(), op, ": caches must be on q's device");
+  TORCH_CHECK(kcache.stride(-1) == 1 && kcache.size(2) == 1, op,
+              ": caches must be [num_blocks, Hkv, 1, block_size, D] with a contiguous last dim");
+  const auto dt = q_in.scalar_type();
+  TORCH_CHECK(dt == at::kBFloat16 || dt == at::kHalf, op, ": q must be bfloat16 or float16, got ", dt);
+  TORCH_CHECK(k_in.scalar_type() == dt && v_in.scalar_type() == dt, op, ": q, k, v must share a dtype");
+
+  c.q = q_in.contiguous();
+  c.k = k_in.contiguous();
+  c.v = v_in.contiguous();
+  const int64_t B = c.q.size(0), Hkv = c.q.size(1), G = c.q.size(2), S = c.q.size(3), D = c.q.size(4);
+  TORCH_CHECK(c.k.size(0) == B && c.k.size(1) == Hkv && c.k.size(2) == 1 && c.k.size(3) == S &&
+                  c.k.size(4) == D && c.v.sizes() == c.k.sizes(),
+              op, ": k/v must be [B, Hkv, 1, S, D] matching q ", c.q.sizes(), ", got ", c.k.sizes());
+  TORCH_CHECK(kcache.size(1) == Hkv, op, ": caches hold ", kcache.size(1), " KV heads, q has ", Hkv);
+  TORCH_CHECK(D <= kcache.size(-1), op, ": head_dim ", D, " exceeds the cache's last dim ", kcache.size(-1));
+  TORCH_CHECK(kcache.size(3) == block_size, op, ": block_size ", block_size,
+              " does not match the cache's block dimension ", kcache.size(3));
+  if (decode) TORCH_CHECK(S == 1, op, ": decode takes one query token per sequence, got S = ", S);
+
+  c.seq = on_device(seq_in, c.q);
+  TORCH_CHECK(c.seq.numel() == B, op, ": seq must hold one entry per sequence, got ", c.seq.sizes());
+  if (c.seq.scalar_type() != at::kInt) c.seq = c.seq.to(at::kInt);
+  c.seq = c.seq.contiguous();
+
+  c.bt = on_device(block_table_in, c.q);
+  if (c.bt.dim() == 1) c.bt = c.bt.unsqueeze(0).expand({B, c.bt.size(0)});
+  TORCH_CHECK(c.bt.dim() == 2 && (c.bt.size(0) == B || c.bt.size(0) == 1), op,
+              ": block_table must be [B, max_blocks], got ", c.bt.sizes());
+  const auto btt = c.bt.scalar_type();
+  TORCH_CHECK(btt == at::kShort || btt == at::kInt || btt == at::kLong, op,
+              ": block_table must be int16/int32/int64");
+  if (c.bt.stride(1) != 1) c.bt = c.bt.contiguous();
+
+  auto& p = c.p;
+  p.batch = (int32_t)B;
+  p.num_kv_heads = (int32_t)Hkv;
+  p.group = (int32_t)G;
+  p.q_len = (int32_t)S;
+  p.head_dim = (int32_t)D;
+  p.num_blocks = (int32_t)kcache.size(0);
+  p.block_size = (int32_t)block_size;
+  p.max_blocks = (int32_t)c.bt.size(1);
+  p.q = c.q.data_ptr();
+  for (int i = 0; i < 4; ++i) p.q_stride[i] = c.q.stride(i);
+  p.q_dtype = to_rbln_dtype(dt);
+  c.out = at::empty_like(c.q, at::MemoryFormat::Contiguous);
+  p.out = c.out.data_ptr();
+  for (int i = 0; i < 4; ++i) p.out_stride[i] = c.out.stride(i);
+  p.k_new = c.k.data_ptr();
+  p.v_new = c.v.data_ptr();
+  p.k_new_stride[0] = c.k.stride(0); p.k_new_stride[1] = c.k.stride(1); p.k_new_stride[2] = c.k.stride(3);
+  p.v_new_stride[0] = c.v.stride(0); p.v_new_stride[1] = c.v.stride(1); p.v_new_stride[2] = c.v.stride(3);
+  p.kcache = kcache.data_ptr();
+  p.vcache = vcache.data_ptr();
+  p.kv_dtype = to_rbln_dtype(kcache.scalar_type());
+  p.cache_stride[0] = kcache.stride(0);
+  p.cache_stride[1] = kcache.stride(1);
+  p.cache_stride[2] = kcache.stride(3);
+  p.seq = c.seq.data_ptr<int32_t>();
+  p.seq_stride = 1;
+  p.block_table = c.bt.data_ptr();
+  p.block_table_dtype = to_rbln_dtype(btt);
+  p.block_table_stride = c.bt.size(0) == 1 ? 0 : c.bt.stride(0);
+
+  if (mask_in.has_value() && mask_in->defined()) {
+    c.mask = on_device(*mask_in, c.q);
+    TORCH_CHECK(c.mask.scalar_type() == at::kFloat || c.mask.scalar_type() == at::kHalf ||
+                    c.mask.scalar_type() == at::kBFloat16 || c.mask.scalar_type() == at::kBool,
+                op, ": mask must be floating point or bool");
+    if (c.mask.stride(-1) != 1) c.mask = c.mask.contiguous();
+    p.mask = c.mask.data_ptr();
+    p.mask_dtype = to_rbln_dtype(c.mask.scalar_type());
+    p.mask_len = (int32_t)std::min<int64_t>(c.mask.size(-1), (int64_t)p.max_blocks * block_size);
+    // batch stride: the mask's leading dim is the batch (or broadcast 1)
+    p.mask_stride[0] = c.mask.size(0) == 1 ? 0 : c.mask.stride(0);
+    // query-row stride for prefill masks [B, 1, 1, S_q, L] / [B, S_q, L]
+    p.mask_stride[1] = (c.mask.dim() >= 2 && c.mask.size(-2) == S && S > 1) ? c.mask.stride(-2) : 0;
+  }
+
+  if (scale.is_cuda()) {
+    c.scale_dev = scale.scalar_type() == at::kFloat ? scale : scale.to(at::kFloat);
+    p.scale_dev = c.scale_dev.data_ptr<float>();
+  } else {
+    p.scale = scale.item<float>();
+  }
+  if (debug_checks()) {
+    c.err = at::zeros({1}, c.q.options().dtype(at::kInt));
+    p.error_flags = reinterpret_cast<uint32_t*>(c.err.data_ptr<int32_t>());
+  }
+}
+
+void check_rc(int rc, const char* op) {
+  TORCH_CHECK(rc == RBLN_OK, op, ": ", status_name(rc), " (status ", rc, ")");
+}
+
+void check_device_flags(const Common& c, const char* op) {
+  if (!c.err.defined()) return;
+  const int flags = c.err.item<int>();
+  TORCH_CHECK(flags == 0, op, ": device-side input check failed (flags 0x", std::hex, flags,
+              "): block_table entry out of range or seq out of range");
+}
+
+at::Tensor run_decode(Common& c, at::Tensor& kcache, const char* op, bool require_mask) {
+  c10::cuda::CUDAGuard guard(c.q.device());
+  size_t ws = 0;
+  check_rc(rbln_paged_decode_workspace_size(&c.p, &ws), op);
+  at::Tensor wst;
+  if (ws > 0) {
+    wst = at::empty({(int64_t)ws}, c.q.options().dtype(at::kByte));
+    c.p.workspace = wst.data_ptr();
+    c.p.workspace_bytes = ws;
+  }
+  auto stream = at::cuda::getCurrentCUDAStream(c.q.device().index());
+  const int rc = require_mask ? rbln_paged_attn_decode(&c.p, stream.stream())
+                              : rbln_paged_causal_attn_decode(&c.p, stream.stream());
+  check_rc(rc, op);
+  check_device_flags(c, op);
+  return c.out;
+}
+
+// rbln_custom_ops::paged_attn_decode (register_custom_ops.py:253-293)
+at::Tensor paged_attn_decode_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                  const at::Tensor& mask, at::Tensor& kcache, at::Tensor& vcache,
+                                  const at::Tensor& seq, const at::Tensor& scale,
+                                  const at::Tensor& block_table, int64_t block_size) {
+  Common c;
+  TORCH_CHECK(kcache.scalar_type() == q.scalar_type(), "paged_attn_decode: cache dtype must equal q dtype");
+  fill_paged(c, "paged_attn_decode", q, k, v, kcache, vcache, seq, scale, block_table, block_size, mask, true);
+  return run_decode(c, kcache, "paged_attn_decode", true);
+}
+
+// rbln_custom_ops::paged_causal_attn_decode (register_custom_ops.py:409-450)
+at::Tensor paged_causal_attn_decode_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                         at::Tensor& kcache, at::Tensor& vcache, const at::Tensor& seq,
+                                         const at::Tensor& scale, const at::Tensor& block_table,
+                                         int64_t block_size, const std::optional<at::Tensor>& mask) {
+  Common c;
+  TORCH_CHECK(kcache.scalar_type() == q.scalar_type(),
+              "paged_causal_attn_decode: cache dtype must equal q dtype (use the _kvfp8 op for fp8 caches)");
+  fill_paged(c, "paged_causal_attn_decode", q, k, v, kcache, vcache, seq, scale, block_table, block_size,
+             mask, true);
+  return run_decode(c, kcache, "paged_causal_attn_decode", false);
+}
+
+// fp8-e4m3 KV cache with one fp32 dequant scale per (block, KV head). No
+// counterpart in the reference's op set; same contract as
+// paged_causal_attn_decode plus the two scale tensors [num_blocks, Hkv].
+at::Tensor paged_causal_attn_decode_kvfp8_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                               at::Tensor& kcache, at::Tensor& vcache,
+                                               const at::Tensor& k_scale, const at::Tensor& v_scale,
+                                               const at::Tensor& seq, const at::Tensor& scale,
+                                               const at::Tensor& block_table, int64_t block_size,
+                                               const std::optional<at::Tensor>& mask) {
+  const char* op = "paged_causal_attn_decode_kvfp8";
+  TORCH_CHECK(kcache.scalar_type() == at::kFloat8_e4m3fn, op, ": caches must be float8_e4m3fn");
+  TORCH_CHECK(k_scale.scalar_type() == at::kFloat && v_scale.scalar_type() == at::kFloat, op,
+              ": k_scale/v_scale must be float32 [num_blocks, Hkv]");
+  TORCH_CHECK(k_scale.dim() == 2 && k_scale.size(0) == kcache.size(0) && k_scale.size(1) == kcache.size(1) &&
+                  v_scale.sizes() == k_scale.sizes() && v_scale.strides() == k_scale.strides(),
+              op, ": k_scale/v_scale must be [num_blocks, Hkv]");
+  TORCH_CHECK(k_scale.device() == q.device() && v_scale.device() == q.device(), op,
+              ": scales must be on q's device");
+  Common c;
+  fill_paged(c, op, q, k, v, kcache, vcache, seq, scale, block_table, block_size, mask, true);
+  c.p.k_scale = k_scale.data_ptr<float>();
+  c.p.v_scale = v_scale.data_ptr<float>();
+  c.p.scale_stride[0] = k_scale.stride(0);
+  c.p.scale_stride[1] = k_scale.stride(1);
+  return run_decode(c, kcache, op, false);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(rbln_custom_ops, m) {
+  m.def(
+      "paged_attn_prefill(Tensor q, Tensor k, Tensor v, Tensor mask, Tensor(a4!) kcache, Tensor(a5!) vcache, "
+      "Tensor seq, Tensor scale, Tensor block_table, SymInt block_size) -> Tensor");
+  m.def(
+      "paged_attn_decode(Tensor q, Tensor k, Tensor v, Tensor mask, Tensor(a4!) kcache, Tensor(a5!) vcache, "
+      "Tensor seq, Tensor scale, Tensor block_table, SymInt block_size) -> Tensor");
+  m.def(
+      "paged_causal_attn_prefill(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, Tensor(a4!) vcache, "
+      "Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, bool is_bidirectional, "
+      "Tensor? mask=None) -> Tensor");
+  m.def(
+      "paged_causal_attn_decode(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, Tensor(a4!) vcache, "
+      "Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, Tensor? mask=None) -> Tensor");
+  m.def(
+      "paged_causal_attn_decode_kvfp8(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, Tensor(a4!) vcache, "
+      "Tensor k_scale, Tensor v_scale, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, "
+      "Tensor? mask=None) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(rbln_custom_ops, CUDA, m) {
+  m.impl("paged_attn_decode", &paged_attn_decode_cuda);
+  m.impl("paged_causal_attn_decode", &paged_causal_attn_decode_cuda);
+  m.impl("paged_causal_attn_decode_kvfp8", &paged_causal_attn_decode_kvfp8_cuda);
+}

@@ -1,0 +1,24 @@
+"""Fake (meta) kernels: output metadata equals q's, as in the reference's
+register_fake functions (test/rbln/test_custom_kernel.py:95-135, 219-259,
+346-385, 489-526)."""
+
+from __future__ import annotations
+
+import torch
+
+_NAMES = (
+    "paged_attn_prefill",
+    "paged_attn_decode",
+    "paged_causal_attn_prefill",
+    "paged_causal_attn_decode",
+    "paged_causal_attn_decode_kvfp8",
+)
+
+
+def _like_q(q, *args, **kwargs):
+    return torch.empty_like(q)
+
+
+for _name in _NAMES:
+    if hasattr(torch.ops.rbln_custom_ops, _name):
+        torch.library.register_fake(f"rbln_custom_ops::{_name}", _like_q)

@@ -195,10 +195,13 @@ def test_decode_block_table_known_answer():
         else:
             d["kcache"][int(bt[b, tt // bs]), :, 0, tt % bs, :] = 8.0
     d["vcache"] = vp.to(d["vcache"].dtype)
+    # the appended token of every sequence encodes its own position too
     d["v"].zero_()
-    d["v"][3, :, 0, 0, 0] = 4096 // 256
-    d["v"][3, :, 0, 0, 1] = 4096 % 256
-    d["v"][3, :, 0, 0, 2] = 3
+    for b in range(B):
+        t = lens[b] - 1
+        d["v"][b, :, 0, 0, 0] = t // 256
+        d["v"][b, :, 0, 0, 1] = t % 256
+        d["v"][b, :, 0, 0, 2] = b
     out, _, _ = run_op(d)
     for b in range(B):
         exp = torch.tensor([target[b] // 256, target[b] % 256, b], dtype=out.dtype)

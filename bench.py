@@ -57,6 +57,9 @@ WORKLOADS = {
                    B=64, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=20000, fp8=False),
     "decode_fp8": dict(desc="paged decode fp8-e4m3 KV B=256 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
                        B=256, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
+    # profiling case for ncu --set full: inputs still larger than L2, ~0.35 GB on the device
+    "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
+                         B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False),
     "decode_long": dict(desc="paged decode bf16 B=32 Hq=64 Hkv=8 D=128 bs=16 L=32768 pool=65536",
                         B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False),
 }

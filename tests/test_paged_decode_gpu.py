@@ -191,9 +191,9 @@ def test_decode_block_table_known_answer():
             vp[blk, :, 0, off, 2] = b
         tt = target[b]
         if tt == lens[b] - 1:
-            d["k"][b, :, 0, 0, :] = 8.0
+            d["k"][b, :, 0, 0, :] = 64.0
         else:
-            d["kcache"][int(bt[b, tt // bs]), :, 0, tt % bs, :] = 8.0
+            d["kcache"][int(bt[b, tt // bs]), :, 0, tt % bs, :] = 64.0
     d["vcache"] = vp.to(d["vcache"].dtype)
     # the appended token of every sequence encodes its own position too
     d["v"].zero_()

@@ -39,7 +39,8 @@ typedef enum {
   RBLN_ERR_UNSUPPORTED = -2,      /* valid, but not a configuration built here */
   RBLN_ERR_WORKSPACE = -3,        /* workspace missing or too small */
   RBLN_ERR_LAUNCH = -4,           /* cudaLaunch* reported an error */
-  RBLN_ERR_NO_DEVICE = -5         /* no sm_100 device current */
+  RBLN_ERR_NO_DEVICE = -5,        /* no sm_100 device current */
+  RBLN_ERR_SCRATCH_LIMIT = -6     /* needs more than the fixed no-allocation scratch */
 } rbln_status_t;
 
 typedef enum {
@@ -143,6 +144,25 @@ int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_
  * Same append; attention over the positions whose mask value is > 0.
  * p->mask is required. */
 int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* No counterpart in the reference: a variant of rbln_paged_causal_attn_decode
+ * for callers that cannot allocate device memory -- for example a runtime
+ * that has handed all device memory to its own pool at start-up, or a
+ * plugin whose host framework forbids allocation while work is enqueued
+ * (cudaMalloc may also synchronise the device, which a latency-bound decode
+ * loop cannot afford). Same semantics and parameters; p->workspace and
+ * p->workspace_bytes are ignored. Its split-K scratch is a fixed array of
+ * RBLN_NOALLOC_SCRATCH_BYTES in device memory, owned by this library and held
+ * on every GPU that loads it until the process exits. Requests that need
+ * more return RBLN_ERR_SCRATCH_LIMIT and launch nothing.
+ * The first call on each device looks up the array's device address (with
+ * that device current); make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race on it and must be serialised by the caller.
+ * Nothing in it needs to start at zero: every partial the merge step reads
+ * is written earlier in the same call. Allocates nothing. */
+#define RBLN_NOALLOC_SCRATCH_BYTES (16u << 20)
+int rbln_paged_causal_attn_decode_noalloc(const rbln_paged_attn_params_t* p, cudaStream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

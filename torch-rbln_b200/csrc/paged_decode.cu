@@ -30,8 +30,15 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
+
+// Fixed device scratch for rbln_paged_causal_attn_decode_noalloc (callers
+// that cannot allocate). Host code must not use this name as an address: it
+// is a host-side stand-in; the device address comes from
+// cudaGetSymbolAddress, looked up once per device below.
+static __device__ __align__(256) unsigned char rbln_noalloc_scratch[RBLN_NOALLOC_SCRATCH_BYTES];
 
 namespace rbln {
 namespace {
@@ -660,6 +667,43 @@ int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_
 
 int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
   return rbln::run_decode(p, stream, /*require_mask=*/true);
+}
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoallocMaxDevices];
+void* g_noalloc_addr[kNoallocMaxDevices];
+cudaError_t g_noalloc_status[kNoallocMaxDevices];
+
+// Device address of the fixed scratch on the current device (looked up once
+// per device, with that device current).
+int noalloc_scratch(void** addr) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) return RBLN_ERR_NO_DEVICE;
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* a = nullptr;
+    g_noalloc_status[dev] = cudaGetSymbolAddress(&a, rbln_noalloc_scratch);
+    g_noalloc_addr[dev] = a;
+  });
+  if (g_noalloc_status[dev] != cudaSuccess || g_noalloc_addr[dev] == nullptr) return RBLN_ERR_LAUNCH;
+  *addr = g_noalloc_addr[dev];
+  return RBLN_OK;
+}
+}  // namespace
+
+int rbln_paged_causal_attn_decode_noalloc(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  if (!p) return RBLN_ERR_INVALID_ARGUMENT;
+  rbln::Plan pl;
+  int rc = rbln::plan_decode(p, &pl);
+  if (rc != RBLN_OK) return rc;
+  if (pl.ws_bytes > RBLN_NOALLOC_SCRATCH_BYTES) return RBLN_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != RBLN_OK) return rc;
+  rbln_paged_attn_params_t q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = RBLN_NOALLOC_SCRATCH_BYTES;
+  return rbln::run_decode(&q, stream, /*require_mask=*/false);
 }
 
 }  // extern "C"

@@ -347,13 +347,18 @@ def run_ours(args, wl_name):
 
 
 def _traffic_from_profiles(wl_name):
-    """DRAM bytes per launch of the main kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", f"traffic_{wl_name}.json")
-    if os.path.exists(p):
-        try:
-            return json.load(open(p)).get("dram_bytes_per_launch")
-        except (OSError, ValueError):
-            return None
+    """DRAM bytes per launch of the main kernel, from the committed ncu summary
+    (a `traffic_bytes_per_launch[<workload>]: N` line), if one exists."""
+    import glob
+    import re
+
+    key = f"traffic_bytes_per_launch[{wl_name}]:"
+    for p in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
+        for line in open(p):
+            if line.startswith(key):
+                m = re.search(r"(\d+)", line[len(key):])
+                if m:
+                    return int(m.group(1))
     return None
 
 

@@ -59,6 +59,7 @@ typedef enum {
  * treated as masked) and the kernel carries on. */
 #define RBLN_DEVERR_BLOCK_ID_RANGE 0x1u /* block_table entry outside [0, num_blocks) */
 #define RBLN_DEVERR_SEQ_RANGE 0x2u      /* seq < 0, or a write past the table's span */
+#define RBLN_DEVERR_TIMEOUT 0x4u        /* a pipeline wait gave up (the CTA returned early) */
 
 /* Paged attention over a block-table-indexed KV cache: one parameter block
  * serves decode (S_q = 1) and chunked prefill (S_q >= 1). */
@@ -144,6 +145,53 @@ int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_
  * Same append; attention over the positions whose mask value is > 0.
  * p->mask is required. */
 int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* rbln_custom_ops::paged_causal_attn_prefill
+ * (reference frontend register_custom_ops.py:324-379,
+ *  CPU semantics test_custom_kernel.py:262-343).
+ * Writes k_new/v_new at positions [seq[b], seq[b] + S_q), then attends query
+ * row s (absolute position seq[b] + s) over keys t <= seq[b] + s
+ * (p->causal = 1) or t < seq[b] + S_q (p->causal = 0, "is_bidirectional");
+ * p->mask, when set, is an extra [B, L] keep-mask over keys.
+ * bf16/f16 only, q and caches of one dtype, D in {64, 128}, block_size in
+ * {8, 16, 32, 64, 128} or a multiple of 128. No workspace. */
+int rbln_paged_causal_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* rbln_custom_ops::paged_attn_prefill
+ * (reference frontend register_custom_ops.py:175-229,
+ *  CPU semantics test_custom_kernel.py:31-92).
+ * Same write; attention keeps key t for query row s when
+ * mask[b, s, t] > 0 (p->mask required, mask_stride = {batch, query row}). */
+int rbln_paged_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* Dense scaled dot-product attention, forward. */
+typedef struct {
+  int32_t batch, num_heads, num_kv_heads, q_len, kv_len, head_dim; /* GQA: num_heads % num_kv_heads == 0 */
+  int32_t dtype;          /* F32, F16 or BF16, shared by q, k, v and out */
+  const void* q;          /* [B, Hq, L, D]; strides in elements: b, h, l (d contiguous) */
+  int64_t q_stride[3];
+  const void* k;          /* [B, Hkv, S, D] */
+  int64_t k_stride[3];
+  const void* v;
+  int64_t v_stride[3];
+  void* out;              /* [B, Hq, L, D] */
+  int64_t out_stride[3];
+  float* lse;             /* optional [B, Hq, L] fp32 natural-log logsumexp */
+  int64_t lse_stride[3];
+  const void* mask;       /* optional [B|1, Hq|1, L, S] */
+  int32_t mask_dtype;     /* BOOL (keep) or F32/F16/BF16 */
+  int32_t mask_additive;  /* 1: float mask added to the scores; 0: value > 0 keeps */
+  int64_t mask_stride[4]; /* b, h, l, s (s stride must be 1 for F16/BF16 inputs) */
+  int32_t causal;         /* top-left: query l sees keys s <= l */
+  float scale;
+  uint32_t* error_flags;
+} rbln_sdpa_params_t;
+
+/* aten::_scaled_dot_product_fused_attention_overrideable, forward
+ * (reference torch_rbln/_internal/kernels/sdpa.py:670-751; math of
+ * _sdpa_cpu_fallback, sdpa.py:244-289). bf16/f16 on the tensor cores,
+ * f32 exactly in fp32. D in {64, 128}. */
+int rbln_sdpa_fwd(const rbln_sdpa_params_t* p, cudaStream_t stream);
 
 /* No counterpart in the reference: a variant of rbln_paged_causal_attn_decode
  * for callers that cannot allocate device memory -- for example a runtime

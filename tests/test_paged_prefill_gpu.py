@@ -1,0 +1,172 @@
+"""Parity of the tcgen05 chunked-prefill kernel with the oracle and the reference.
+
+Tolerance (stated): rtol 1e-3, atol 1.2e-2 (test/rbln/test_custom_kernel.py:
+654-655) against the oracle's exact fp32 evaluation; cache writes bit-exact.
+"""
+
+import math
+import os
+
+import pytest
+import torch
+
+from oracle import paged_attention as opa
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 1.2e-2
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _ext():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import torch_rbln_b200  # noqa: F401
+
+
+def make_prefill(B, Hkv, G, D, bs, S, starts, dtype=torch.bfloat16, seed=0, extra_blocks=1, bt_dtype=torch.int32):
+    g = torch.Generator().manual_seed(seed)
+    ends = [s + S for s in starts]
+    max_blocks = math.ceil(max(ends) / bs) + extra_blocks
+    nblk = B * max_blocks + 2
+    bt = torch.randperm(nblk, generator=g)[: B * max_blocks].reshape(B, max_blocks).to(bt_dtype)
+    q = torch.randn([B, Hkv, G, S, D], generator=g).to(dtype)
+    k = torch.randn([B, Hkv, 1, S, D], generator=g).to(dtype)
+    v = torch.randn([B, Hkv, 1, S, D], generator=g).to(dtype)
+    kc = torch.randn([nblk, Hkv, 1, bs, D], generator=g).to(dtype)
+    vc = torch.randn([nblk, Hkv, 1, bs, D], generator=g).to(dtype)
+    seq = torch.tensor(starts, dtype=torch.int32).reshape(B, 1)
+    return dict(q=q, k=k, v=v, kcache=kc, vcache=vc, seq=seq, block_table=bt, block_size=bs,
+                scale=torch.tensor(1.0 / math.sqrt(D)))
+
+
+def run_gpu(d, *, op="causal", causal=True, mask=None):
+    x = {k: (v.to(DEV) if isinstance(v, torch.Tensor) and k != "scale" else v) for k, v in d.items()}
+    ops = torch.ops.rbln_custom_ops
+    if op == "keep":
+        out = ops.paged_attn_prefill(x["q"], x["k"], x["v"], mask.to(DEV), x["kcache"], x["vcache"], x["seq"],
+                                     x["scale"], x["block_table"], x["block_size"])
+    else:
+        out = ops.paged_causal_attn_prefill(x["q"], x["k"], x["v"], x["kcache"], x["vcache"], x["seq"], x["scale"],
+                                            x["block_table"], x["block_size"], not causal,
+                                            None if mask is None else mask.to(DEV))
+    torch.cuda.synchronize()
+    return out.cpu(), x["kcache"].cpu(), x["vcache"].cpu()
+
+
+def run_oracle(d, *, op="causal", causal=True, mask=None):
+    kc, vc = d["kcache"].clone(), d["vcache"].clone()
+    if op == "keep":
+        out = opa.paged_prefill(d["q"], d["k"], d["v"], kc, vc, d["seq"], d["scale"], d["block_table"],
+                                d["block_size"], mask=mask)
+    else:
+        out = opa.paged_prefill(d["q"], d["k"], d["v"], kc, vc, d["seq"], d["scale"], d["block_table"],
+                                d["block_size"], causal=causal, position_mask=mask)
+    return out, kc, vc
+
+
+def check(got, ref):
+    assert torch.isfinite(got[0].float()).all()
+    torch.testing.assert_close(got[0].float(), ref[0], rtol=RTOL, atol=ATOL)
+    assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
+
+
+GOLDEN = torch.load(os.path.join(os.path.dirname(__file__), "golden", "paged_prefill.pt"), weights_only=False)
+
+
+@pytest.mark.parametrize("idx", [i for i, c in enumerate(GOLDEN) if c["dtype"] != torch.float32])
+@pytest.mark.parametrize("case", ["paged_attn_prefill_s0", "paged_attn_prefill_s1", "paged_causal_attn_prefill",
+                                  "paged_causal_attn_prefill_bidir"])
+def test_prefill_matches_reference_fixtures(idx, case):
+    c = GOLDEN[idx]
+    exp = c["results"][case]
+    D, S, ms, dt, s1 = c["D"], c["S"], c["max_seq"], c["dtype"], c["s1"]
+    kc = torch.zeros([1, c["Hkv"], 1, ms, D], dtype=dt)
+    vc = torch.zeros_like(kc)
+    if case == "paged_attn_prefill_s0":
+        kw = dict(op="keep", mask=torch.ones([1, S, ms], dtype=dt).tril().view(1, 1, 1, S, ms))
+    elif case == "paged_attn_prefill_s1":
+        kc[:, :, :, :s1], vc[:, :, :, :s1] = c["kpre"], c["vpre"]
+        kw = dict(op="keep", mask=torch.ones([1, S, ms], dtype=dt).tril(diagonal=s1).view(1, 1, 1, S, ms))
+    elif case == "paged_causal_attn_prefill":
+        kw = dict(causal=True)
+    else:
+        pm = torch.zeros([1, ms], dtype=dt)
+        pm[:, :S] = 1
+        kw = dict(causal=False, mask=pm)
+    d = dict(q=c["q"], k=c["k"], v=c["v"], kcache=kc, vcache=vc, seq=torch.tensor([[exp["seq"]]], dtype=torch.int32),
+             block_table=torch.tensor([0], dtype=torch.int16), block_size=ms, scale=torch.tensor(1.0 / math.sqrt(D)))
+    got = run_gpu(d, **kw)
+    check(got, run_oracle(d, **kw))
+    tol = dict(rtol=1.6e-2, atol=3e-2) if dt == torch.bfloat16 else dict(rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(got[0].float(), exp["out"].float(), **tol)
+
+
+CASES = [
+    # B, Hkv, G, D, bs, S, starts
+    (3, 2, 4, 128, 16, 100, [0, 37, 300]),
+    (2, 2, 4, 64, 16, 130, [5, 1000]),
+    (2, 1, 8, 128, 32, 64, [0, 129]),
+    (2, 2, 1, 128, 16, 200, [17, 0]),
+    (1, 2, 2, 64, 8, 77, [3]),
+    (2, 1, 16, 128, 128, 40, [250, 0]),
+    (1, 1, 4, 128, 256, 300, [100]),
+    (2, 2, 6, 64, 64, 50, [70, 2]),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("case", CASES)
+def test_prefill_random_block_table(case, causal, dtype):
+    B, Hkv, G, D, bs, S, starts = case
+    d = make_prefill(B, Hkv, G, D, bs, S, starts, dtype=dtype, seed=S + B * D + bs)
+    check(run_gpu(d, causal=causal), run_oracle(d, causal=causal))
+
+
+def test_prefill_keep_mask_matches_causal():
+    """paged_attn_prefill with an offset-causal keep-mask equals the causal op."""
+    B, Hkv, G, D, bs, S, starts = 2, 2, 4, 128, 16, 96, [40, 500]
+    d = make_prefill(B, Hkv, G, D, bs, S, starts, seed=7)
+    span = d["block_table"].shape[1] * bs
+    t = torch.arange(span).reshape(1, 1, span)
+    qi = torch.arange(S).reshape(1, S, 1) + torch.tensor(starts).reshape(B, 1, 1)
+    keep = (t <= qi).to(torch.bfloat16).reshape(B, 1, 1, S, span)
+    got_keep = run_gpu(d, op="keep", mask=keep)
+    check(got_keep, run_oracle(d, op="keep", mask=keep))
+    got_causal = run_gpu(d, causal=True)
+    torch.testing.assert_close(got_keep[0].float(), got_causal[0].float(), rtol=0, atol=0)
+
+
+def test_prefill_position_mask():
+    B, Hkv, G, D, bs, S, starts = 2, 2, 4, 64, 16, 64, [100, 20]
+    d = make_prefill(B, Hkv, G, D, bs, S, starts, seed=8)
+    span = d["block_table"].shape[1] * bs
+    g = torch.Generator().manual_seed(1)
+    pm = (torch.rand([B, span], generator=g) > 0.4).to(torch.bfloat16)
+    pm[:, 0] = 1
+    check(run_gpu(d, causal=True, mask=pm), run_oracle(d, causal=True, mask=pm))
+
+
+def test_prefill_chunked_equals_single_pass():
+    """Two chunks of 64 tokens in a row give the same output rows as one
+    128-token pass: the second call reads back what the first one wrote."""
+    d = make_prefill(1, 2, 4, 128, 16, 128, [0], seed=9)
+    full = run_gpu(d, causal=True)
+    d1 = dict(d, q=d["q"][:, :, :, :64].contiguous(), k=d["k"][:, :, :, :64].contiguous(),
+              v=d["v"][:, :, :, :64].contiguous())
+    x1 = run_gpu(d1, causal=True)
+    d2 = dict(d, q=d["q"][:, :, :, 64:].contiguous(), k=d["k"][:, :, :, 64:].contiguous(),
+              v=d["v"][:, :, :, 64:].contiguous(), kcache=x1[1], vcache=x1[2],
+              seq=torch.tensor([[64]], dtype=torch.int32))
+    x2 = run_gpu(d2, causal=True)
+    torch.testing.assert_close(torch.cat([x1[0], x2[0]], dim=3).float(), full[0].float(), rtol=0, atol=0)
+    assert torch.equal(x2[1], full[1]) and torch.equal(x2[2], full[2])
+
+
+def test_prefill_larger_context():
+    """Chunked prefill at the workload's per-sequence shape (512 new tokens,
+    32/8 heads, D=128, bs=16) on two sequences with cached context."""
+    d = make_prefill(2, 8, 4, 128, 16, 512, [1500, 3333], seed=10)
+    check(run_gpu(d, causal=True), run_oracle(d, causal=True))

@@ -1,0 +1,766 @@
+// Flash-attention forward on the sm_100a tensor cores (tcgen05 + TMEM + TMA),
+// shared by the paged chunked-prefill ops and dense SDPA.
+//
+// Reference semantics:
+//   rbln_custom_ops::paged_causal_attn_prefill / paged_attn_prefill
+//     (test/rbln/test_custom_kernel.py:31-92, 262-343): write the chunk's new
+//     k/v rows at positions [seq[b], seq[b] + S_q), then attend; generalised
+//     to a real block table and to a causal mask offset by seq[b];
+//   aten::_scaled_dot_product_fused_attention_overrideable
+//     (torch_rbln/_internal/kernels/sdpa.py:670-751 with the math of
+//     _sdpa_cpu_fallback, sdpa.py:244-289): softmax(Q K^T * scale + mask) V,
+//     GQA by head ratio, top-left causal.
+//
+// One CTA computes a 128-row query tile: the G query heads that share a KV
+// head are stacked into the M dimension (rows = G heads x 128/G tokens), so
+// each K/V tile fetched from HBM feeds all G heads. Warp roles:
+//   warp 0     TMA producer: Q once; K and V tiles of 128 keys into a
+//              2-stage ring of 128B-swizzled shared-memory panels. Paged K/V
+//              are fetched block by block through the block table (4-D tensor
+//              map over [num_blocks, Hkv, block_size, D]); a block outside the
+//              table or the pool is fetched at an out-of-range coordinate,
+//              which the TMA unit fills with zeros.
+//   warp 1     TMEM owner and MMA issuer (one thread): S = Q K^T into one of
+//              two TMEM buffers (128 fp32 columns each), O += P V into a third.
+//   warps 2-5  softmax: thread = query row (TMEM lane), fp32 online softmax
+//              in the log2 domain with lazy rescaling of O (only when the
+//              running max grows by more than 8), P written to shared memory
+//              as bf16/f16 in the operand layout of the PV MMA; epilogue.
+// The QK MMA of tile j+1 is issued before the PV MMA of tile j, so the tensor
+// cores work while the softmax warps process the previous tile.
+// Every mbarrier wait is bounded (sm100.cuh); on timeout the CTA raises
+// RBLN_DEVERR_TIMEOUT, drains its copies and MMAs, frees TMEM and returns.
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace rbln {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;                 // query rows per CTA
+constexpr int BN = 128;                 // keys per KV tile
+constexpr int kThreads = 192;           // 6 warps
+constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes
+
+enum MaskMode : int {
+  MM_CAUSAL = 0,  // key <= seq_off + s
+  MM_NONE = 1,    // every written key (paged: < seq_off + S_q; dense: < S)
+  MM_KEEP = 2,    // keep-mask value > 0 (paged_attn_prefill)
+};
+
+struct AttnArgs {
+  // output rows [B, Hkv, G, S_q, D]; strides in bytes
+  char* out;
+  int64_t os_b, os_h, os_g, os_s;
+  float* lse;  // optional [B, Hkv, G, S_q] (natural-log logsumexp), element strides
+  int64_t ls_b, ls_h, ls_g, ls_s;
+  const int32_t* seq;  // per-sequence start offset (nullptr = 0)
+  int64_t seq_stride;
+  const void* bt;  // block table (nullptr = dense: block id = b)
+  int bt_dtype;
+  int64_t bt_stride;
+  int max_blocks;
+  int num_blocks;  // pool size (dense: B)
+  int bs;          // tokens per block (dense: S rounded up to 128)
+  int span;        // addressable keys per sequence
+  int kv_extra;    // dense: number of keys S
+  int B, Hkv, G, S_q, QT, q_tiles;
+  int mask_mode;
+  const void* mask;  // keep-mask (paged) or SDPA mask
+  int mask_dtype;
+  int mask_additive;  // 1: add mask * log2e to scores (SDPA float mask)
+  int mask_len;
+  int64_t m_b, m_h, m_s;  // element strides (h indexes query heads h*G+g); key stride 1
+  const void* pmask;      // optional position keep-mask [B, L]
+  int pmask_dtype;
+  int pmask_len;
+  int64_t pm_b;
+  float scale;
+  const float* scale_dev;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ float mask_value(const void* base, int dt, int64_t i) {
+  switch (dt) {
+    case RBLN_DT_F32: return static_cast<const float*>(base)[i];
+    case RBLN_DT_F16: return __half2float(static_cast<const __half*>(base)[i]);
+    case RBLN_DT_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+    default: return static_cast<const uint8_t*>(base)[i] ? 1.f : 0.f;
+  }
+}
+
+// Keys this CTA must visit, [0, kv_end).
+__device__ __forceinline__ int cta_kv_end(const AttnArgs& a, int s0, int seq_off) {
+  const int s_hi = min(s0 + a.QT, a.S_q);  // exclusive
+  int end;
+  if (a.mask_mode == MM_KEEP) {
+    end = min(a.span, a.mask_len);
+  } else if (a.mask_mode == MM_CAUSAL) {
+    end = seq_off + s_hi;
+  } else {
+    end = (a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q;
+  }
+  if (a.bt == nullptr) end = min(end, a.kv_extra);
+  return max(0, min(end, a.span));
+}
+
+template <int D>
+struct SmemLayout {
+  static constexpr int NP = D / 64;                    // 64-element panels along D
+  static constexpr int Q = 0;                          // NP panels
+  static constexpr int K0 = Q + NP * kPanelBytes;      // stage s: K0 + s*NP*panel
+  static constexpr int V0 = K0 + 2 * NP * kPanelBytes;
+  static constexpr int P = V0 + 2 * NP * kPanelBytes;  // 2 panels (128 keys)
+  static constexpr int BAR = P + 2 * kPanelBytes;      // mbarriers
+  static constexpr int TMEM_SLOT = BAR + 16 * 8;
+  static constexpr int ABORT = TMEM_SLOT + 8;
+  static constexpr int TOTAL = ABORT + 8;
+  // + alignment slack; at least 120 KB so that only one CTA (which holds all
+  // 512 TMEM columns) is resident per SM
+  static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
+};
+
+enum Bar { B_Q = 0, B_KF0, B_KF1, B_VF0, B_VF1, B_KE0, B_KE1, B_SF0, B_SF1, B_SR0, B_SR1, B_PF, B_PV, B_DONE, B_COUNT };
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  using L = SmemLayout<D>;
+  constexpr int NP = L::NP;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  volatile int* abort = reinterpret_cast<volatile int*>(sgen + L::ABORT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::TMEM_SLOT);
+  auto bar = [&](int i) { return sbase + L::BAR + 8u * i; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int s0 = qtile * a.QT;
+  const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
+  const int kv_end = (seq_off < 0) ? 0 : cta_kv_end(a, s0, seq_off);
+  const int ntiles = (kv_end + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    *abort = 0;
+    for (int i = 0; i < B_COUNT; ++i) {
+      const uint32_t cnt = (i == B_SR0 || i == B_SR1 || i == B_PF) ? 4u : 1u;
+      mbar_init(bar(i), cnt);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        // the Q box holds QT x G rows (fewer than 128 when G does not divide 128)
+        mbar_arrive_expect_tx(bar(B_Q), NP * a.QT * a.G * 128);
+        for (int p = 0; p < NP; ++p)
+          tma_load_5d(sbase + L::Q + p * kPanelBytes, &tm_q, bar(B_Q), p * 64, s0, 0, h, b);
+      }
+      const int rpb = min(a.bs, BN);
+      const int nbox = BN / rpb;
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1, abort)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar(B_KF0 + st), NP * kPanelBytes);
+          mbar_arrive_expect_tx(bar(B_VF0 + st), NP * kPanelBytes);
+        }
+        __syncwarp();
+        const int t0 = j * BN;
+        for (int i = lane; i < nbox; i += 32) {
+          const int key = t0 + i * rpb;
+          int blk = a.num_blocks;  // out of range -> zero fill
+          int row = 0;
+          if (key < kv_end) {
+            if (a.bt == nullptr) {
+              blk = b;
+              row = key;
+            } else {
+              const int bi = key / a.bs;
+              row = key - bi * a.bs;
+              if (bi < a.max_blocks) {
+                const int64_t v = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+                if (v >= 0 && v < a.num_blocks) {
+                  blk = (int)v;
+                } else if (a.err) {
+                  atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+                }
+              }
+            }
+          }
+          const uint32_t koff = sbase + L::K0 + st * NP * kPanelBytes + i * rpb * 128;
+          const uint32_t voff = sbase + L::V0 + st * NP * kPanelBytes + i * rpb * 128;
+          for (int p = 0; p < NP; ++p) {
+            tma_load_4d(koff + p * kPanelBytes, &tm_k, bar(B_KF0 + st), p * 64, row, h, blk);
+            tma_load_4d(voff + p * kPanelBytes, &tm_v, bar(B_VF0 + st), p * 64, row, h, blk);
+          }
+        }
+        issued = j + 1;
+      }
+      if (*abort) {
+        // let the copies already issued land before the CTA's memory goes away
+        for (int j = max(0, issued - 2); j < issued; ++j) {
+          const int st = j & 1;
+          const long long t0c = clock64();
+          while (!mbar_try_wait(bar(B_KF0 + st), (j >> 1) & 1) && clock64() - t0c < 2000000) {
+          }
+          while (!mbar_try_wait(bar(B_VF0 + st), (j >> 1) & 1) && clock64() - t0c < 4000000) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t id_qk = idesc_f16(BF16, BM, BN, false);
+      const uint32_t id_pv = idesc_f16(BF16, BM, D, true);
+      auto issue_pv = [&](int jj) -> bool {
+        const int sp = jj & 1;
+        if (!mbar_wait(bar(B_PF), jj & 1, abort)) return false;
+        if (!mbar_wait(bar(B_VF0 + sp), (jj >> 1) & 1, abort)) return false;
+        tc_fence_after();
+        const uint32_t vb = sbase + L::V0 + sp * NP * kPanelBytes;
+        const uint32_t pb = sbase + L::P;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t ad = sw128_desc(pb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(vb + kk * 16 * 128, kPanelBytes, 1024);
+          umma_f16_ss(t_o, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(B_PV));
+        umma_commit(bar(B_KE0 + sp));
+        return true;
+      };
+      bool ok = mbar_wait(bar(B_Q), 0, abort);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(bar(B_KF0 + st), (j >> 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        if (j >= 2 && !mbar_wait(bar(B_SR0 + st), ((j >> 1) - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = sbase + L::K0 + st * NP * kPanelBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = sw128_desc(sbase + L::Q + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(kb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+          umma_f16_ss(t_s[st], ad, bd, id_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(B_SF0 + st));
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) ok = issue_pv(ntiles - 1);
+      if (!ok) {
+        // abort: let the MMAs already issued finish before TMEM is freed
+        umma_commit(bar(B_DONE));
+        const long long t0c = clock64();
+        while (!mbar_try_wait(bar(B_DONE), 0) && clock64() - t0c < 4000000) {
+        }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int g = r / a.QT, i = r - g * a.QT;
+    const int s = s0 + i;
+    const bool row_ok = (g < a.G) && (s < a.S_q);
+    const int qpos = seq_off + s;  // absolute position of this query
+    const int none_limit = (a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const float qk_mult = scale * kLog2e;
+    float m_run = neg_inf(), l_run = 0.f;
+    const int64_t mrow = a.mask ? (b * a.m_b + (int64_t)(h * a.G + g) * a.m_h + (int64_t)s * a.m_s) : 0;
+    bool ok = true;
+
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(bar(B_SF0 + st), (j >> 1) & 1, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t tmp[32];
+        tmem_ld32(t_s[st] + lane_off + c * 32, tmp);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(tmp[e]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_SR0 + st));
+
+      const int t0 = j * BN;
+      const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN - 1 <= seq_off + s0) && (t0 + BN <= kv_end)
+                                                       : (a.mask_mode == MM_NONE && t0 + BN <= kv_end);
+      float mt = neg_inf();
+      if (interior && row_ok && a.mask == nullptr && a.pmask == nullptr) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          x[c] *= qk_mult;
+          mt = fmaxf(mt, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int key = t0 + c;
+          bool keep = row_ok && key < kv_end;
+          if (a.mask_mode == MM_CAUSAL) keep = keep && key <= qpos;
+          if (a.mask_mode == MM_NONE) keep = keep && key < none_limit;
+          float add = 0.f;
+          if (keep && a.mask) {
+            const float mv = mask_value(a.mask, a.mask_dtype, mrow + key);
+            if (a.mask_additive) add = mv * kLog2e;
+            else keep = mv > 0.f;
+          }
+          if (keep && a.pmask)
+            keep = key < a.pmask_len && mask_value(a.pmask, a.pmask_dtype, b * a.pm_b + key) > 0.f;
+          x[c] = keep ? fmaf(x[c], qk_mult, add) : neg_inf();
+          mt = fmaxf(mt, x[c]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mt);
+      const bool grow = m_new > m_run + 8.f;
+      float factor = 1.f;
+      if (grow) {
+        factor = exp2_approx(m_run - m_new);  // 0 when m_run = -inf
+        l_run *= factor;
+        m_run = m_new;
+      }
+      const float mu = (m_run == neg_inf()) ? 0.f : m_run;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        x[c] = exp2_approx(x[c] - mu);
+        lsum += x[c];
+      }
+      l_run += lsum;
+
+      // O and the P buffer are free once the PV MMA of tile j-1 completed
+      if (j >= 1 && !mbar_wait(bar(B_PV), (j - 1) & 1, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + lane_off + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          tmem_st32(t_o + lane_off + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      // P row -> shared memory, K-major 128B-swizzled (two 64-key panels)
+      uint8_t* prow = sgen + L::P + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
+        uint4 v;
+        v.x = pack2<BF16>(x[ch * 8 + 0], x[ch * 8 + 1]);
+        v.y = pack2<BF16>(x[ch * 8 + 2], x[ch * 8 + 3]);
+        v.z = pack2<BF16>(x[ch * 8 + 4], x[ch * 8 + 5]);
+        v.w = pack2<BF16>(x[ch * 8 + 6], x[ch * 8 + 7]);
+        const int pan = ch >> 3, c16 = (ch & 7) ^ (r & 7);
+        *reinterpret_cast<uint4*>(prow + pan * kPanelBytes + c16 * 16) = v;
+      }
+      // keys past kv_end in the last tile may hold unwritten memory: zero their V rows
+      if (j == ntiles - 1 && t0 + BN > kv_end) {
+        if (!mbar_wait(bar(B_VF0 + st), (j >> 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        if (t0 + r >= kv_end) {
+          uint8_t* vrow = sgen + L::V0 + st * NP * kPanelBytes + r * 128;
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c16 = 0; c16 < 8; ++c16)
+              *reinterpret_cast<uint4*>(vrow + p * kPanelBytes + c16 * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_PF));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (ok && ntiles > 0 && !mbar_wait(bar(B_PV), (ntiles - 1) & 1, abort)) ok = false;
+    tc_fence_after();
+    if (ok && row_ok) {
+      const float inv = 1.f / l_run;  // l_run == 0 -> inf -> NaN (all keys masked)
+      char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (ntiles > 0) {
+          tmem_ld32(t_o + lane_off + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 v;
+          v.x = pack2<BF16>(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+          v.y = pack2<BF16>(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+          v.z = pack2<BF16>(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+          v.w = pack2<BF16>(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + (c * 32 + q4 * 8) * 2) = v;
+        }
+      }
+      if (a.lse) {
+        const float v =
+            (m_run == neg_inf() || l_run == 0.f) ? neg_inf() : (m_run + __log2f(l_run)) * 0.6931471805599453f;
+        a.lse[b * a.ls_b + h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Writes the chunk's new k/v rows into the paged cache at [seq[b], seq[b]+S_q).
+// One warp per token: lanes 0-15 copy the K row, lanes 16-31 the V row.
+template <int D>
+__global__ void __launch_bounds__(256)
+    paged_append_kernel(const char* k_new, const char* v_new, int64_t kn_b, int64_t kn_h, int64_t kn_s, int64_t vn_b,
+                        int64_t vn_h, int64_t vn_s, char* kcache, char* vcache, int64_t cs_block, int64_t cs_head,
+                        int64_t cs_tok, const int32_t* seq, int64_t seq_stride, const void* bt, int bt_dtype,
+                        int64_t bt_stride, int bs, int span, int num_blocks, int S_q, uint32_t* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * 8 + warp;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (tok >= S_q) return;
+  const int s0 = seq[b * seq_stride];
+  const int pos = s0 + tok;
+  if (s0 < 0 || pos >= span) {
+    if (lane == 0 && err) atomicOr(err, RBLN_DEVERR_SEQ_RANGE);
+    return;
+  }
+  const int64_t blk = load_index(bt, bt_dtype, b * bt_stride + pos / bs);
+  if (blk < 0 || blk >= num_blocks) {
+    if (lane == 0 && err) atomicOr(err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    return;
+  }
+  const int64_t row = (blk * cs_block + h * cs_head + (int64_t)(pos % bs) * cs_tok) * 2;
+  const int part = lane >> 4, j = lane & 15;
+  if (j < D / 8) {
+    const char* src = part == 0 ? k_new + b * kn_b + h * kn_h + tok * kn_s : v_new + b * vn_b + h * vn_h + tok * vn_s;
+    char* dst = (part == 0 ? kcache : vcache) + row;
+    *reinterpret_cast<uint4*>(dst + j * 16) = *reinterpret_cast<const uint4*>(src + j * 16);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// rank-N tiled map, innermost dim first; strides in bytes for dims 1..N-1.
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
+              const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
+  return fn(m, dt, rank, base, d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct TcLaunch {
+  CUtensorMap tq, tk, tv;
+  AttnArgs a;
+  int D;
+  bool bf16;
+};
+
+template <int D, bool BF16>
+int launch_tc(const TcLaunch& Lc, cudaStream_t st) {
+  using SL = SmemLayout<D>;
+  // per-device attribute: set on every launch (cheap, host-side only)
+  if (cudaFuncSetAttribute(attn_fwd_tc_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SL::ALLOC) !=
+      cudaSuccess)
+    return RBLN_ERR_LAUNCH;
+  dim3 grid(Lc.a.q_tiles, Lc.a.Hkv, Lc.a.B);
+  attn_fwd_tc_kernel<D, BF16><<<grid, kThreads, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+int launch_tc_any(const TcLaunch& Lc, cudaStream_t st) {
+  if (Lc.D == 128) return Lc.bf16 ? launch_tc<128, true>(Lc, st) : launch_tc<128, false>(Lc, st);
+  return Lc.bf16 ? launch_tc<64, true>(Lc, st) : launch_tc<64, false>(Lc, st);
+}
+
+CUtensorMapDataType tmap_dtype(int dt) {
+  return dt == RBLN_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// q [B, Hkv, G, S, D] (element strides b, hkv, g, s) -> 5-D map, box {64, QT, G, 1, 1}
+bool map_q(CUtensorMap* m, const void* q, int dt, int B, int Hkv, int G, int S, int D, const int64_t* qs, int QT) {
+  uint64_t dims[5] = {(uint64_t)D, (uint64_t)S, (uint64_t)G, (uint64_t)Hkv, (uint64_t)B};
+  uint64_t str[4] = {(uint64_t)qs[3] * 2, (uint64_t)qs[2] * 2, (uint64_t)qs[1] * 2, (uint64_t)qs[0] * 2};
+  uint32_t box[5] = {64, (uint32_t)QT, (uint32_t)G, 1, 1};
+  return make_map(m, tmap_dtype(dt), 5, const_cast<void*>(q), dims, str, box);
+}
+
+// cache [NB, Hkv, rows, D] (element strides block, head, row) -> 4-D map, box {64, rpb, 1, 1}
+bool map_kv(CUtensorMap* m, const void* c, int dt, int NB, int Hkv, int rows, int D, int64_t s_blk, int64_t s_head,
+            int64_t s_row, int rpb) {
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)Hkv, (uint64_t)NB};
+  uint64_t str[3] = {(uint64_t)s_row * 2, (uint64_t)s_head * 2, (uint64_t)s_blk * 2};
+  uint32_t box[4] = {64, (uint32_t)rpb, 1, 1};
+  return make_map(m, tmap_dtype(dt), 4, const_cast<void*>(c), dims, str, box);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_mask_op) {
+  if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 || p->max_blocks <= 0 ||
+      p->num_blocks <= 0 || p->q_len < 0)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->head_dim != 64 && p->head_dim != 128) return RBLN_ERR_UNSUPPORTED;
+  if (p->q_dtype != RBLN_DT_BF16 && p->q_dtype != RBLN_DT_F16) return RBLN_ERR_UNSUPPORTED;
+  if (p->kv_dtype != p->q_dtype) return RBLN_ERR_UNSUPPORTED;
+  if (p->group > BM) return RBLN_ERR_UNSUPPORTED;
+  const int bs = p->block_size;
+  // TMA boxes of min(bs, 128) rows must start on 1 KB (8-row) swizzle atoms
+  if (!((bs >= 8 && bs <= BN && BN % bs == 0) || (bs >= BN && bs % BN == 0))) return RBLN_ERR_UNSUPPORTED;
+  if (keep_mask_op && !p->mask) return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->batch == 0 || p->q_len == 0) return RBLN_OK;
+  if (!p->q || !p->out || !p->kcache || !p->vcache || !p->seq || !p->block_table) return RBLN_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->q) || !aligned16(p->out) || !aligned16(p->kcache) || !aligned16(p->vcache))
+    return RBLN_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 4; ++i)
+    if ((p->q_stride[i] * 2) % 16 || (p->out_stride[i] * 2) % 16) return RBLN_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 3; ++i)
+    if ((p->cache_stride[i] * 2) % 16) return RBLN_ERR_INVALID_ARGUMENT;
+  const int64_t span64 = (int64_t)p->max_blocks * bs;
+  if (span64 > (1 << 30)) return RBLN_ERR_UNSUPPORTED;
+  const int D = p->head_dim, G = p->group;
+  const int QT = BM / G;
+  const int q_tiles = (p->q_len + QT - 1) / QT;
+  if (q_tiles > 65535 || p->num_kv_heads > 65535 || p->batch > 65535) return RBLN_ERR_UNSUPPORTED;
+
+  // 1) write the chunk's k/v rows into the cache
+  if (p->k_new) {
+    if (!p->v_new || !aligned16(p->k_new) || !aligned16(p->v_new)) return RBLN_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < 3; ++i)
+      if ((p->k_new_stride[i] * 2) % 16 || (p->v_new_stride[i] * 2) % 16) return RBLN_ERR_INVALID_ARGUMENT;
+    dim3 grid((p->q_len + 7) / 8, p->num_kv_heads, p->batch);
+    auto* kn = static_cast<const char*>(p->k_new);
+    auto* vn = static_cast<const char*>(p->v_new);
+    if (D == 128)
+      paged_append_kernel<128><<<grid, 256, 0, st>>>(
+          kn, vn, p->k_new_stride[0] * 2, p->k_new_stride[1] * 2, p->k_new_stride[2] * 2, p->v_new_stride[0] * 2,
+          p->v_new_stride[1] * 2, p->v_new_stride[2] * 2, (char*)p->kcache, (char*)p->vcache, p->cache_stride[0],
+          p->cache_stride[1], p->cache_stride[2], p->seq, p->seq_stride, p->block_table, p->block_table_dtype,
+          p->block_table_stride, bs, (int)span64, p->num_blocks, p->q_len, p->error_flags);
+    else
+      paged_append_kernel<64><<<grid, 256, 0, st>>>(
+          kn, vn, p->k_new_stride[0] * 2, p->k_new_stride[1] * 2, p->k_new_stride[2] * 2, p->v_new_stride[0] * 2,
+          p->v_new_stride[1] * 2, p->v_new_stride[2] * 2, (char*)p->kcache, (char*)p->vcache, p->cache_stride[0],
+          p->cache_stride[1], p->cache_stride[2], p->seq, p->seq_stride, p->block_table, p->block_table_dtype,
+          p->block_table_stride, bs, (int)span64, p->num_blocks, p->q_len, p->error_flags);
+    if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
+  }
+
+  // 2) attention
+  TcLaunch Lc{};
+  Lc.D = D;
+  Lc.bf16 = p->q_dtype == RBLN_DT_BF16;
+  const int rpb = std::min(bs, BN);
+  if (!map_q(&Lc.tq, p->q, p->q_dtype, p->batch, p->num_kv_heads, G, p->q_len, D, p->q_stride, QT))
+    return RBLN_ERR_LAUNCH;
+  if (!map_kv(&Lc.tk, p->kcache, p->kv_dtype, p->num_blocks, p->num_kv_heads, bs, D, p->cache_stride[0],
+              p->cache_stride[1], p->cache_stride[2], rpb))
+    return RBLN_ERR_LAUNCH;
+  if (!map_kv(&Lc.tv, p->vcache, p->kv_dtype, p->num_blocks, p->num_kv_heads, bs, D, p->cache_stride[0],
+              p->cache_stride[1], p->cache_stride[2], rpb))
+    return RBLN_ERR_LAUNCH;
+  AttnArgs& a = Lc.a;
+  a.out = (char*)p->out;
+  a.os_b = p->out_stride[0] * 2;
+  a.os_h = p->out_stride[1] * 2;
+  a.os_g = p->out_stride[2] * 2;
+  a.os_s = p->out_stride[3] * 2;
+  a.seq = p->seq;
+  a.seq_stride = p->seq_stride;
+  a.bt = p->block_table;
+  a.bt_dtype = p->block_table_dtype;
+  a.bt_stride = p->block_table_stride;
+  a.max_blocks = p->max_blocks;
+  a.num_blocks = p->num_blocks;
+  a.bs = bs;
+  a.span = (int)span64;
+  a.kv_extra = 0;
+  a.B = p->batch;
+  a.Hkv = p->num_kv_heads;
+  a.G = G;
+  a.S_q = p->q_len;
+  a.QT = QT;
+  a.q_tiles = q_tiles;
+  if (keep_mask_op) {
+    a.mask_mode = MM_KEEP;
+    a.mask = p->mask;
+    a.mask_dtype = p->mask_dtype;
+    a.mask_len = p->mask_len;
+    a.m_b = p->mask_stride[0];
+    a.m_h = 0;
+    a.m_s = p->mask_stride[1];
+  } else {
+    a.mask_mode = p->causal ? MM_CAUSAL : MM_NONE;
+    if (p->mask) {  // optional position mask [B, L]
+      a.pmask = p->mask;
+      a.pmask_dtype = p->mask_dtype;
+      a.pmask_len = p->mask_len;
+      a.pm_b = p->mask_stride[0];
+    }
+  }
+  a.scale = p->scale;
+  a.scale_dev = p->scale_dev;
+  a.err = p->error_flags;
+  return launch_tc_any(Lc, st);
+}
+
+}  // namespace
+
+// Dense attention on the same kernel (used by rbln_sdpa_fwd, sdpa.cu).
+// q [B, Hkv, G, L, D] by element strides qs = {b, hkv, g, l}; k/v [B, Hkv, S, D]
+// by strides {b, h, s}; mask [B|1, Hq|1, L, S] by strides {b, hq, l} (key stride 1).
+int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os, float* lse, const int64_t* ls,
+                  const void* k, const void* v, const int64_t* ks, const int64_t* vs, int dtype, int B, int Hkv,
+                  int G, int L, int S, int D, int causal, const void* mask, int mask_dtype, int mask_additive,
+                  const int64_t* ms, float scale, uint32_t* err, cudaStream_t st) {
+  if (D != 64 && D != 128) return RBLN_ERR_UNSUPPORTED;
+  if (G > BM || S <= 0) return RBLN_ERR_UNSUPPORTED;
+  TcLaunch Lc{};
+  Lc.D = D;
+  Lc.bf16 = dtype == RBLN_DT_BF16;
+  const int QT = BM / G;
+  const int q_tiles = (L + QT - 1) / QT;
+  if (q_tiles > 65535 || Hkv > 65535 || B > 65535) return RBLN_ERR_UNSUPPORTED;
+  if (!map_q(&Lc.tq, q, dtype, B, Hkv, G, L, D, qs, QT)) return RBLN_ERR_LAUNCH;
+  // k [B, Hkv, S, D] seen as a pool of B blocks of S rows, 128-row boxes
+  if (!map_kv(&Lc.tk, k, dtype, B, Hkv, S, D, ks[0], ks[1], ks[2], BN)) return RBLN_ERR_LAUNCH;
+  if (!map_kv(&Lc.tv, v, dtype, B, Hkv, S, D, vs[0], vs[1], vs[2], BN)) return RBLN_ERR_LAUNCH;
+  AttnArgs& a = Lc.a;
+  a.out = (char*)out;
+  a.os_b = os[0] * 2;
+  a.os_h = os[1] * 2;
+  a.os_g = os[2] * 2;
+  a.os_s = os[3] * 2;
+  a.lse = lse;
+  if (lse) {
+    a.ls_b = ls[0];
+    a.ls_h = ls[1];
+    a.ls_g = ls[2];
+    a.ls_s = ls[3];
+  }
+  a.seq = nullptr;
+  a.bt = nullptr;
+  a.max_blocks = 1;
+  a.num_blocks = B;
+  a.bs = ((S + BN - 1) / BN) * BN;
+  a.span = a.bs;
+  a.kv_extra = S;
+  a.B = B;
+  a.Hkv = Hkv;
+  a.G = G;
+  a.S_q = L;
+  a.QT = QT;
+  a.q_tiles = q_tiles;
+  a.mask_mode = causal ? MM_CAUSAL : MM_NONE;
+  if (mask) {
+    a.mask = mask;
+    a.mask_dtype = mask_dtype;
+    a.mask_additive = mask_additive;
+    a.mask_len = S;
+    a.m_b = ms[0];
+    a.m_h = ms[1];
+    a.m_s = ms[2];
+  }
+  a.scale = scale;
+  a.err = err;
+  return launch_tc_any(Lc, st);
+}
+
+}  // namespace rbln
+
+extern "C" {
+
+int rbln_paged_causal_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  return rbln::run_prefill(p, stream, /*keep_mask_op=*/false);
+}
+
+int rbln_paged_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  return rbln::run_prefill(p, stream, /*keep_mask_op=*/true);
+}
+
+}  // extern "C"

@@ -553,10 +553,10 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
     const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);
-    if (smem > 48 * 1024) {
-      cudaFuncSetAttribute(paged_decode_merge_kernel<D, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-    }
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(paged_decode_merge_kernel<D, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return RBLN_ERR_LAUNCH;
     paged_decode_merge_kernel<D, QB><<<dim3(a.Hkv, a.B), kThreads, smem, st>>>(a);
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;

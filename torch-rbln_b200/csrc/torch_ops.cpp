@@ -10,10 +10,16 @@
 // on purpose: the output dtype is q.dtype (not forced fp16), the caller's
 // scale is honoured, batch > 1 prefill is allowed.
 #include <ATen/ATen.h>
+#include <ATen/Context.h>
+#include <ATen/SDPBackend.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/ops/_fused_sdp_choice_native.h>
+#include <c10/core/GradMode.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <atomic>
+#include <cmath>
 #include <cstdlib>
 #include <string>
 
@@ -159,8 +165,8 @@ void fill_paged(Common& c, const char* op, const at::Tensor& q_in, const at::Ten
     p.mask_len = (int32_t)std::min<int64_t>(c.mask.size(-1), (int64_t)p.max_blocks * block_size);
     // batch stride: the mask's leading dim is the batch (or broadcast 1)
     p.mask_stride[0] = c.mask.size(0) == 1 ? 0 : c.mask.stride(0);
-    // query-row stride for prefill masks [B, 1, 1, S_q, L] / [B, S_q, L]
-    p.mask_stride[1] = (c.mask.dim() >= 2 && c.mask.size(-2) == S && S > 1) ? c.mask.stride(-2) : 0;
+    // query-row stride for prefill keep-masks [B, 1, 1, S_q, L]
+    p.mask_stride[1] = (c.mask.dim() >= 2 && c.mask.size(-2) == S) ? c.mask.stride(-2) : 0;
   }
 
   if (scale.is_cuda()) {
@@ -255,7 +261,202 @@ at::Tensor paged_causal_attn_decode_kvfp8_cuda(const at::Tensor& q, const at::Te
   return run_decode(c, kcache, op, false);
 }
 
+at::Tensor run_prefill(Common& c, const char* op, bool keep_mask) {
+  c10::cuda::CUDAGuard guard(c.q.device());
+  auto stream = at::cuda::getCurrentCUDAStream(c.q.device().index());
+  const int rc = keep_mask ? rbln_paged_attn_prefill(&c.p, stream.stream())
+                           : rbln_paged_causal_attn_prefill(&c.p, stream.stream());
+  check_rc(rc, op);
+  check_device_flags(c, op);
+  return c.out;
+}
+
+// rbln_custom_ops::paged_attn_prefill (register_custom_ops.py:175-229)
+at::Tensor paged_attn_prefill_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                   const at::Tensor& mask, at::Tensor& kcache, at::Tensor& vcache,
+                                   const at::Tensor& seq, const at::Tensor& scale, const at::Tensor& block_table,
+                                   int64_t block_size) {
+  const char* op = "paged_attn_prefill";
+  TORCH_CHECK(kcache.scalar_type() == q.scalar_type(), op, ": cache dtype must equal q dtype");
+  Common c;
+  fill_paged(c, op, q, k, v, kcache, vcache, seq, scale, block_table, block_size, mask, false);
+  return run_prefill(c, op, true);
+}
+
+// rbln_custom_ops::paged_causal_attn_prefill (register_custom_ops.py:324-379)
+at::Tensor paged_causal_attn_prefill_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                          at::Tensor& kcache, at::Tensor& vcache, const at::Tensor& seq,
+                                          const at::Tensor& scale, const at::Tensor& block_table, int64_t block_size,
+                                          bool is_bidirectional, const std::optional<at::Tensor>& mask) {
+  const char* op = "paged_causal_attn_prefill";
+  TORCH_CHECK(kcache.scalar_type() == q.scalar_type(), op, ": cache dtype must equal q dtype");
+  Common c;
+  fill_paged(c, op, q, k, v, kcache, vcache, seq, scale, block_table, block_size, mask, false);
+  c.p.causal = is_bidirectional ? 0 : 1;
+  return run_prefill(c, op, false);
+}
+
+// ---------------------------------------------------------------------------
+// SDPA: aten::_scaled_dot_product_fused_attention_overrideable on CUDA, and
+// the backend choice that routes F.scaled_dot_product_attention to it
+// (mirrors _fused_sdp_choice_privateuse1, aten/src/ATen/native/
+// RBLNRegisterOps.cpp:89-102, which picks "overrideable" for 4-D inputs).
+// ---------------------------------------------------------------------------
+std::atomic<bool> g_sdpa_route{[] {
+  const char* e = std::getenv("RBLN_ATTN_SDPA");
+  return !(e && std::string(e) == "0");
+}()};
+
+bool sm100_device(const at::Tensor& t) {
+  if (!t.is_cuda()) return false;
+  const auto* prop = at::cuda::getDeviceProperties(t.device().index());
+  return prop->major == 10;
+}
+
+// The inputs the CUDA kernels here take; anything else goes to torch's own
+// CUDA backends.
+bool sdpa_supported(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                    const std::optional<at::Tensor>& mask, double dropout_p) {
+  if (q.dim() != 4 || k.dim() != 4 || v.dim() != 4) return false;
+  if (q.is_nested() || k.is_nested() || v.is_nested()) return false;
+  const auto dt = q.scalar_type();
+  if (dt != at::kBFloat16 && dt != at::kHalf && dt != at::kFloat) return false;
+  if (k.scalar_type() != dt || v.scalar_type() != dt) return false;
+  if (k.device() != q.device() || v.device() != q.device() || !sm100_device(q)) return false;
+  const int64_t D = q.size(3);
+  if ((D != 64 && D != 128) || k.size(3) != D || v.size(3) != D) return false;
+  if (k.size(0) != q.size(0) || v.size(0) != q.size(0) || k.size(1) != v.size(1) || k.size(2) != v.size(2))
+    return false;
+  if (k.size(1) == 0 || q.size(1) % k.size(1) != 0) return false;
+  if (q.numel() == 0 || k.numel() == 0) return false;
+  if (dropout_p > 0.0) return false;
+  if (c10::GradMode::is_enabled() && (q.requires_grad() || k.requires_grad() || v.requires_grad())) return false;
+  if (mask.has_value() && mask->defined()) {
+    const auto& m = *mask;
+    if (m.dim() < 2 || m.dim() > 4 || m.device() != q.device()) return false;
+    if (m.scalar_type() != at::kBool && !at::isFloatingType(m.scalar_type())) return false;
+    if (m.requires_grad() && c10::GradMode::is_enabled()) return false;
+  }
+  return true;
+}
+
+int64_t fused_sdp_choice_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                              const std::optional<at::Tensor>& mask, double dropout_p, bool is_causal,
+                              std::optional<double> scale, bool enable_gqa) {
+  if (g_sdpa_route.load() && at::globalContext().userEnabledOverrideableSDP() &&
+      sdpa_supported(q, k, v, mask, dropout_p))
+    return static_cast<int64_t>(at::SDPBackend::overrideable);
+  return at::native::_fused_sdp_choice_cuda(q, k, v, mask, dropout_p, is_causal, scale, enable_gqa);
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::SymInt, c10::SymInt, at::Tensor, at::Tensor,
+           at::Tensor>
+sdpa_overrideable_cuda(const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                       const std::optional<at::Tensor>& attn_bias, double dropout_p, bool is_causal,
+                       bool return_debug_mask, std::optional<double> scale) {
+  // input validation as in the reference (sdpa.py:85-119): ValueError
+  TORCH_CHECK_VALUE(query.scalar_type() == key.scalar_type() && query.scalar_type() == value.scalar_type(),
+                    "Expected query, key, and value to have the same dtype, but got query.dtype: ",
+                    query.scalar_type(), ", key.dtype: ", key.scalar_type(), ", and value.dtype: ",
+                    value.scalar_type(), " instead.");
+  TORCH_CHECK_VALUE(query.device() == key.device() && query.device() == value.device(),
+                    "Expected query, key, and value to have the same device type, but got query.device: ",
+                    query.device(), ", key.device: ", key.device(), ", and value.device: ", value.device(),
+                    " instead.");
+  if (attn_bias.has_value() && attn_bias->defined()) {
+    TORCH_CHECK_VALUE(attn_bias->scalar_type() == at::kBool || at::isFloatingType(attn_bias->scalar_type()),
+                      "Expected attn_mask to have dtype bool or floating point, but got attn_mask.dtype: ",
+                      attn_bias->scalar_type(), " instead.");
+    TORCH_CHECK_VALUE(attn_bias->device() == query.device(),
+                      "Expected attn_mask to have the same device as query, but got attn_mask.device: ",
+                      attn_bias->device(), " and query.device: ", query.device(), " instead.");
+  }
+  TORCH_CHECK(sdpa_supported(query, key, value, attn_bias, dropout_p),
+              "_scaled_dot_product_fused_attention_overrideable (CUDA, sm_100a): unsupported inputs "
+              "(need 4-D bf16/f16/f32 q/k/v with head_dim 64 or 128, Hq % Hkv == 0, no dropout, no grad)");
+  c10::cuda::CUDAGuard guard(query.device());
+  auto inner = [](const at::Tensor& t) { return t.stride(-1) == 1 ? t : t.contiguous(); };
+  at::Tensor q = inner(query), k = inner(key), v = inner(value);
+  const int64_t B = q.size(0), H = q.size(1), L = q.size(2), D = q.size(3);
+  const int64_t Hkv = k.size(1), S = k.size(2);
+  at::Tensor out = at::empty({B, H, L, D}, q.options());
+  at::Tensor lse = at::empty({B, H, L}, q.options().dtype(at::kFloat));
+  rbln_sdpa_params_t p{};
+  p.batch = (int32_t)B;
+  p.num_heads = (int32_t)H;
+  p.num_kv_heads = (int32_t)Hkv;
+  p.q_len = (int32_t)L;
+  p.kv_len = (int32_t)S;
+  p.head_dim = (int32_t)D;
+  p.dtype = to_rbln_dtype(q.scalar_type());
+  p.q = q.data_ptr();
+  p.k = k.data_ptr();
+  p.v = v.data_ptr();
+  p.out = out.data_ptr();
+  for (int i = 0; i < 3; ++i) {
+    p.q_stride[i] = q.stride(i);
+    p.k_stride[i] = k.stride(i);
+    p.v_stride[i] = v.stride(i);
+    p.out_stride[i] = out.stride(i);
+    p.lse_stride[i] = lse.stride(i);
+  }
+  p.lse = lse.data_ptr<float>();
+  at::Tensor m;
+  if (attn_bias.has_value() && attn_bias->defined()) {
+    m = *attn_bias;
+    if (m.scalar_type() != at::kBool && m.scalar_type() != at::kFloat && m.scalar_type() != at::kHalf &&
+        m.scalar_type() != at::kBFloat16)
+      m = m.to(at::kFloat);
+    while (m.dim() < 4) m = m.unsqueeze(0);
+    m = m.expand({B, H, L, S});
+    if (m.stride(3) != 1 && q.scalar_type() != at::kFloat) m = m.contiguous();
+    p.mask = m.data_ptr();
+    p.mask_dtype = to_rbln_dtype(m.scalar_type());
+    p.mask_additive = m.scalar_type() == at::kBool ? 0 : 1;
+    for (int i = 0; i < 4; ++i) p.mask_stride[i] = m.stride(i);
+  }
+  p.causal = is_causal ? 1 : 0;
+  p.scale = (float)(scale.has_value() ? *scale : 1.0 / std::sqrt((double)D));
+  at::Tensor err;
+  if (debug_checks()) {
+    err = at::zeros({1}, q.options().dtype(at::kInt));
+    p.error_flags = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  }
+  auto stream = at::cuda::getCurrentCUDAStream(q.device().index());
+  check_rc(rbln_sdpa_fwd(&p, stream.stream()), "_scaled_dot_product_fused_attention_overrideable");
+  if (err.defined()) {
+    const int flags = err.item<int>();
+    TORCH_CHECK(flags == 0, "_scaled_dot_product_fused_attention_overrideable: device error flags 0x", std::hex,
+                flags);
+  }
+  at::Tensor debug = return_debug_mask ? at::empty({B, H, L, S}, q.options().dtype(at::kFloat))
+                                       : at::empty({0}, q.options().dtype(at::kFloat));
+  at::Tensor cum_q = at::empty({0}, q.options().dtype(at::kLong));
+  at::Tensor cum_k = at::empty({0}, q.options().dtype(at::kLong));
+  at::Tensor seed = at::empty({}, at::TensorOptions().dtype(at::kLong).device(at::kCPU));
+  at::Tensor offset = at::empty({}, at::TensorOptions().dtype(at::kLong).device(at::kCPU));
+  return {out, lse, cum_q, cum_k, c10::SymInt(L), c10::SymInt(S), seed, offset, debug};
+}
+
+void set_sdpa_route(bool enabled) { g_sdpa_route.store(enabled); }
+bool sdpa_route_enabled() { return g_sdpa_route.load(); }
+
 }  // namespace
+
+TORCH_LIBRARY(rbln_attn, m) {
+  m.def("set_sdpa_route(bool enabled) -> ()");
+  m.def("sdpa_route_enabled() -> bool");
+}
+
+TORCH_LIBRARY_IMPL(rbln_attn, CompositeExplicitAutograd, m) {
+  m.impl("set_sdpa_route", &set_sdpa_route);
+  m.impl("sdpa_route_enabled", &sdpa_route_enabled);
+}
+
+TORCH_LIBRARY_IMPL(aten, CUDA, m) {
+  m.impl("_fused_sdp_choice", &fused_sdp_choice_cuda);
+  m.impl("_scaled_dot_product_fused_attention_overrideable", &sdpa_overrideable_cuda);
+}
 
 TORCH_LIBRARY(rbln_custom_ops, m) {
   m.def(
@@ -278,6 +479,8 @@ TORCH_LIBRARY(rbln_custom_ops, m) {
 }
 
 TORCH_LIBRARY_IMPL(rbln_custom_ops, CUDA, m) {
+  m.impl("paged_attn_prefill", &paged_attn_prefill_cuda);
+  m.impl("paged_causal_attn_prefill", &paged_causal_attn_prefill_cuda);
   m.impl("paged_attn_decode", &paged_attn_decode_cuda);
   m.impl("paged_causal_attn_decode", &paged_causal_attn_decode_cuda);
   m.impl("paged_causal_attn_decode_kvfp8", &paged_causal_attn_decode_kvfp8_cuda);

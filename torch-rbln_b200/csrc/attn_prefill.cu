@@ -184,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1, abort)) break;
+        // warp-uniform decision: every lane of the producer warp waits, all break together
+        if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1, abort))) break;
         if (lane == 0) {
           mbar_arrive_expect_tx(bar(B_KF0 + st), NP * kPanelBytes);
           mbar_arrive_expect_tx(bar(B_VF0 + st), NP * kPanelBytes);
@@ -307,12 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(bar(B_SF0 + st), (j >> 1) & 1, abort)) {
+      // tcgen05.ld below is .sync.aligned: the whole warp must take the same path
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF0 + st), (j >> 1) & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
       float x[BN];
+      __syncwarp();
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t tmp[32];
@@ -372,12 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run += lsum;
 
       // O and the P buffer are free once the PV MMA of tile j-1 completed
-      if (j >= 1 && !mbar_wait(bar(B_PV), (j - 1) & 1, abort)) {
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(B_PV), (j - 1) & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
+        __syncwarp();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // keys past kv_end in the last tile may hold unwritten memory: zero their V rows
       if (j == ntiles - 1 && t0 + BN > kv_end) {
-        if (!mbar_wait(bar(B_VF0 + st), (j >> 1) & 1, abort)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(B_VF0 + st), (j >> 1) & 1, abort))) {
           ok = false;
           break;
         }
@@ -423,32 +427,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
-    if (ok && ntiles > 0 && !mbar_wait(bar(B_PV), (ntiles - 1) & 1, abort)) ok = false;
+    // warp-uniform from here: the TMEM loads are .sync.aligned; only the
+    // global stores depend on the lane's row
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PV), (ntiles - 1) & 1, abort));
     tc_fence_after();
-    if (ok && row_ok) {
+    if (ok) {
       const float inv = 1.f / l_run;  // l_run == 0 -> inf -> NaN (all keys masked)
       char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         if (ntiles > 0) {
+          __syncwarp();
           tmem_ld32(t_o + lane_off + c * 32, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
+        if (row_ok) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 v;
-          v.x = pack2<BF16>(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
-          v.y = pack2<BF16>(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
-          v.z = pack2<BF16>(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
-          v.w = pack2<BF16>(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + (c * 32 + q4 * 8) * 2) = v;
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 v;
+            v.x = pack2<BF16>(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+            v.y = pack2<BF16>(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+            v.z = pack2<BF16>(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+            v.w = pack2<BF16>(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + (c * 32 + q4 * 8) * 2) = v;
+          }
         }
       }
-      if (a.lse) {
+      if (row_ok && a.lse) {
         const float v =
             (m_run == neg_inf() || l_run == 0.f) ? neg_inf() : (m_run + __log2f(l_run)) * 0.6931471805599453f;
         a.lse[b * a.ls_b + h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;

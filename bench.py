@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (paged decode by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|decode_fp8|decode_long]
+                    [--workload decode|decode_fp8|decode_long|prefill|sdpa|sdpa_bf16]
 
 Default workload (N = 1): paged-attention decode, bf16, batch 64, 32 query /
 8 KV heads, head_dim 128, block_size 16, context length per sequence
@@ -461,19 +461,313 @@ def run_reference(args, wl_name):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# compute-bound workloads: chunked prefill and SDPA
+# ---------------------------------------------------------------------------
+COMPUTE = {
+    "prefill": dict(kind="prefill", B=8, Hkv=8, G=4, D=128, bs=16, S=512, cmin=0, cmax=8192,
+                    desc="paged chunked prefill bf16 B=8 Hq=32 Hkv=8 D=128 S_q=512 new tokens, "
+                         "cached ctx~U[0,8192], bs=16, causal"),
+    # profiling case for ncu --set full (same per-CTA work, fewer sequences)
+    "prefill_small": dict(kind="prefill", B=2, Hkv=8, G=4, D=128, bs=16, S=512, cmin=2048, cmax=6144,
+                          desc="paged chunked prefill bf16 B=2 Hq=32 Hkv=8 D=128 S_q=512 ctx~U[2048,6144]"),
+    "sdpa": dict(kind="sdpa", B=1, Hq=32, Hkv=8, L=512, D=64, dtype=torch.float32,
+                 desc="SDPA causal GQA fp32 B=1 Hq=32 Hkv=8 L=S=512 D=64 (Llama-3.2-1B attention shape)"),
+    "sdpa_bf16": dict(kind="sdpa", B=4, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
+                      desc="SDPA causal GQA bf16 B=4 Hq=32 Hkv=8 L=S=4096 D=128"),
+}
+
+
+def build_prefill(wl, device, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    B, Hkv, G, D, bs, S = wl["B"], wl["Hkv"], wl["G"], wl["D"], wl["bs"], wl["S"]
+    ctx = torch.randint(wl["cmin"], wl["cmax"] + 1, (B,), generator=g)
+    nb = [int(math.ceil((int(c) + S) / bs)) for c in ctx]
+    max_blocks = max(nb)
+    pool = sum(nb) + B
+    perm = torch.randperm(pool, generator=g)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    cur = 0
+    for b in range(B):
+        bt[b, :nb[b]] = perm[cur:cur + nb[b]].to(torch.int32)
+        cur += nb[b]
+    q = torch.randn([B, Hkv, G, S, D], generator=g).to(torch.bfloat16)
+    k = torch.randn([B, Hkv, 1, S, D], generator=g).to(torch.bfloat16)
+    v = torch.randn([B, Hkv, 1, S, D], generator=g).to(torch.bfloat16)
+    gd = torch.Generator(device=device).manual_seed(seed + 1)
+    shape = [pool, Hkv, 1, bs, D]
+    kc = torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16)
+    vc = torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16)
+    Hq = Hkv * G
+    flops = sum(4 * D * Hq * (S * int(c) + S * (S + 1) // 2) for c in ctx)
+    return dict(q=q, k=k, v=v, kcache=kc, vcache=vc, seq=ctx.to(torch.int32).reshape(B, 1), bt=bt, bs=bs,
+                ctx=ctx, flops=flops, scale=1.0 / math.sqrt(D), B=B, Hkv=Hkv, G=G, D=D, S=S)
+
+
+def build_sdpa(wl, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    B, Hq, Hkv, L, D = wl["B"], wl["Hq"], wl["Hkv"], wl["L"], wl["D"]
+    q = torch.randn([B, Hq, L, D], generator=g).to(wl["dtype"])
+    k = torch.randn([B, Hkv, L, D], generator=g).to(wl["dtype"])
+    v = torch.randn([B, Hkv, L, D], generator=g).to(wl["dtype"])
+    flops = 4 * D * Hq * B * (L * (L + 1) // 2)
+    return dict(q=q, k=k, v=v, flops=flops, scale=1.0 / math.sqrt(D))
+
+
+def _timed_kernel_loop(args, stream, step, flush):
+    """Per-iteration CUDA events around `step` (which records the kernel
+    events itself), with an L2 flush outside the timed window."""
+    op_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    k_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for pair in op_ev + k_ev:
+        pair[0].record(stream)
+        pair[1].record(stream)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        op_ev[i][0].record(stream)
+        step(*k_ev[i])
+        op_ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    op_ms = statistics.mean(a.elapsed_time(b) for a, b in op_ev)
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+    return op_ms, k_ms
+
+
+def run_compute_ours(args, wl_name):
+    import ctypes
+
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    import torch_rbln_b200  # noqa: F401
+    from torch_rbln_b200 import cabi
+
+    wl = COMPUTE[wl_name]
+    stream = torch.cuda.current_stream(dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
+    L = cabi.lib()
+    if wl["kind"] == "prefill":
+        d = build_prefill(wl, dev, seed=1000 * rank)
+        q, k, v, seq, bt = (d[x].to(dev) for x in ("q", "k", "v", "seq", "bt"))
+        kc, vc = d["kcache"], d["vcache"]
+        p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
+        pref = ctypes.byref(p)
+        scale_t = torch.tensor(d["scale"])
+
+        def step(e0=None, e1=None):
+            p.prof_events[0] = e0.cuda_event if e0 is not None else None
+            p.prof_events[1] = e1.cuda_event if e1 is not None else None
+            rc = L.rbln_paged_causal_attn_prefill(pref, sh)
+            if rc != 0:
+                raise RuntimeError(f"rbln_paged_causal_attn_prefill failed: {rc}")
+
+        def op_call(qq, kk, vv, ss, bb):
+            return torch.ops.rbln_custom_ops.paged_causal_attn_prefill(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"],
+                                                                       False)
+
+        host_inputs = [d["q"], d["k"], d["v"], d["seq"], d["bt"]]
+        out_shape, out_dtype = q.shape, q.dtype
+        metric = "paged chunked prefill TFLOP/s"
+        launches = 2
+        kernel = "attn_fwd_tc_kernel<128, bf16> (tcgen05/TMEM/TMA)"
+        dtype = "bf16"
+        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
+    else:
+        d = build_sdpa(wl, seed=0)
+        q, k, v = (d[x].to(dev) for x in ("q", "k", "v"))
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+        sp = cabi.sdpa_params(q, k, v, out, lse, causal=True, scale=d["scale"])
+        spref = ctypes.byref(sp)
+
+        def step(e0=None, e1=None):
+            if e0 is not None:
+                e0.record(stream)
+            rc = L.rbln_sdpa_fwd(spref, sh)
+            if e1 is not None:
+                e1.record(stream)
+            if rc != 0:
+                raise RuntimeError(f"rbln_sdpa_fwd failed: {rc}")
+
+        import torch.nn.functional as F
+
+        def op_call(qq, kk, vv):
+            return F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=d["scale"], enable_gqa=True)
+
+        host_inputs = [d["q"], d["k"], d["v"]]
+        out_shape, out_dtype = q.shape, q.dtype
+        metric = "SDPA TFLOP/s"
+        launches = 1
+        kernel = ("sdpa_f32_kernel<64> (exact-fp32 SIMT; tensor cores have no fp32 mode)"
+                  if wl["dtype"] == torch.float32 else "attn_fwd_tc_kernel<128, bf16> (tcgen05/TMEM/TMA)")
+        dtype = "f32" if wl["dtype"] == torch.float32 else "bf16"
+        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        op_ms, k_ms = _timed_kernel_loop(args, stream, step, flush)
+    if ws > 1:
+        dist.barrier()
+
+    # e2e through the public torch API with host buffers
+    pinned = [t.cpu().pin_memory() for t in host_inputs]
+    hout = torch.empty(out_shape, dtype=out_dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        o = op_call(*[t.to(dev, non_blocking=True) for t in pinned])
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        tt = torch.tensor([op_ms, e2e_ms, k_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        op_ms, e2e_ms, k_ms = tt.tolist()
+
+    hbm_peak, tf_peak, peak_src = load_peaks()
+    flops = d["flops"]
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    line = {
+        "metric": metric, "value": round(ws * flops / (op_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(op_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded N(0,1) inputs" + (", seeded cached lengths and block-table permutation)"
+                                                     if wl["kind"] == "prefill" else ")"),
+        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}", "l2": l2, "flops_per_step": flops},
+        "e2e": {"value": round(ws * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": ("torch.ops.rbln_custom_ops.paged_causal_attn_prefill" if wl["kind"] == "prefill"
+                        else "torch.nn.functional.scaled_dot_product_attention")},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_peak, 4), "traffic": _traffic_from_profiles(wl_name),
+                     "kernel": kernel, "kernel_ms": round(k_ms, 4),
+                     "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peak_src == "measured"
+                                     else "fallback 1.59 PFLOP/s")},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_compute(wl, d, args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _cpu_prefill_sample(d, b):
+    """Sequence b gathered into the reference layout, plus its keep-mask."""
+    bs, S, D = d["bs"], d["S"], d["D"]
+    ctx = int(d["ctx"][b])
+    nblk = int(math.ceil((ctx + S) / bs))
+    blocks = d["bt"][b, :nblk].long()
+    kb = d["kcache"][blocks.to(d["kcache"].device)].cpu()
+    vb = d["vcache"][blocks.to(d["vcache"].device)].cpu()
+    part = nblk * bs
+    kc = kb.permute(1, 2, 0, 3, 4).reshape(1, d["Hkv"], 1, part, D).contiguous()
+    vc = vb.permute(1, 2, 0, 3, 4).reshape(1, d["Hkv"], 1, part, D).contiguous()
+    t = torch.arange(part).reshape(1, part)
+    qi = torch.arange(S).reshape(S, 1) + ctx
+    mask = (t <= qi).to(torch.bfloat16).reshape(1, 1, 1, S, part)
+    flops = 4 * D * d["Hkv"] * d["G"] * (S * ctx + S * (S + 1) // 2)
+    return d["q"][b:b + 1], d["k"][b:b + 1], d["v"][b:b + 1], kc, vc, ctx, mask, flops
+
+
+def _cpu_compute_times(wl, d, reps, budget_s):
+    from oracle import paged_attention as opa
+    from oracle import sdpa as osd
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    if wl["kind"] == "prefill":
+        # the sequence with the median context stands for the workload
+        b = int(torch.argsort(d["ctx"])[len(d["ctx"]) // 2])
+        q, k, v, kc, vc, ctx, mask, flops = _cpu_prefill_sample(d, b)
+        sc = torch.tensor(d["scale"])
+        fn = lambda: opa.mock_prefill_contiguous(q, k, v, kc.clone(), vc.clone(), ctx, sc, mask)
+        sample = (f"1 of {d['B']} sequences (median cached context {ctx}, 512 new tokens), reference CPU "
+                  f"algorithm (oracle.paged_attention.mock_prefill_contiguous, bf16, per-sequence layout)")
+    else:
+        q, k, v = d["q"], d["k"], d["v"]
+        flops = d["flops"]
+        fn = lambda: osd.sdpa_reference(q, k, v, None, 0.0, True, d["scale"])
+        sample = "the full workload, reference CPU path (oracle.sdpa.sdpa_reference: repeat_kv + torch CPU SDPA)"
+    fn()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for _ in range(reps):
+        t = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t)
+        if time.perf_counter() > t_end:
+            break
+    return statistics.median(times), flops, sample, len(times)
+
+
+def cpu_baseline_compute(wl, d, budget_s):
+    med, flops, sample, n = _cpu_compute_times(wl, d, 5, budget_s)
+    return {"value": round(flops / med / 1e12, 5), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": sample + f", median of {n} runs, {med * 1e3:.1f} ms", "ms_per_sample": round(med * 1e3, 2)}
+
+
+def run_reference_compute(args, wl_name):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    wl = COMPUTE[wl_name]
+    d = build_prefill(wl, torch.device("cpu"), seed=0) if wl["kind"] == "prefill" else build_sdpa(wl, seed=0)
+    for _ in range(args.warmup):
+        _cpu_compute_times(wl, d, 1, 1e9)
+    med, flops, sample, n = _cpu_compute_times(wl, d, args.steps, 120.0)
+    val = flops / med / 1e12
+    unit = "TFLOP/s"
+    line = {"impl": "reference", "metric": "paged chunked prefill TFLOP/s" if wl["kind"] == "prefill"
+            else "SDPA TFLOP/s", "value": round(val, 5), "unit": unit, "n_gpus": ws, "steps": n,
+            "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if wl["kind"] == "sdpa" and wl["dtype"] == torch.float32 else "bf16",
+            "data": "synthetic (seeded)", "config": {"workload": wl["desc"]},
+            "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(COMPUTE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload in COMPUTE:
+        (run_reference_compute if args.impl == "reference" else run_compute_ours)(args, args.workload)
+    elif args.impl == "reference":
         run_reference(args, args.workload)
     else:
         run_ours(args, args.workload)

@@ -240,3 +240,22 @@ def mock_decode_contiguous(q, k, v, kcache, vcache, seq, scale, mask=None):
         w = torch.softmax(w + add, dim=-1, dtype=torch.float32).to(q.dtype)
         outs.append(torch.matmul(w, vs).view(Hkv, G, 1, D))
     return torch.stack(outs, 0)
+
+
+def mock_prefill_contiguous(q, k, v, kcache, vcache, s, scale, keep_mask):
+    """The reference's CPU prefill on its own layout, op for op
+    (test_custom_kernel.py:72-92): one sequence, caches [1, Hkv, 1, max_seq, D],
+    new rows written at [s, s + S_q), keep_mask [1, 1, 1, S_q, max_seq].
+    Mutates the caches; returns q.dtype. This is the CPU path the benchmark
+    times as the prefill baseline."""
+    partition = kcache.size(-2)
+    S = q.size(-2)
+    D = k.size(-1)
+    kcache[0].unsqueeze(0)[:, :, :, s:s + S, :D].copy_(k[:, :, :, :, :D])
+    vcache[0].unsqueeze(0)[:, :, :, s:s + S, :D].copy_(v[:, :, :, :, :D])
+    ks = kcache[0].unsqueeze(0)[..., :D]
+    vs = vcache[0].unsqueeze(0)[..., :D]
+    w = torch.matmul(q, ks.transpose(3, 4)) * scale
+    w = w + torch.where(keep_mask[:, :, :, :, :partition] > 0, 0.0, -float("inf"))
+    w = torch.softmax(w, dim=-1, dtype=torch.float32).to(q.dtype)
+    return torch.matmul(w, vs)

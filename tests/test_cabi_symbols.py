@@ -114,3 +114,25 @@ def test_cpu_tensors_are_rejected_no_fallback():
         torch.ops.rbln_custom_ops.paged_causal_attn_decode(
             q, k, k, kc, kc, torch.zeros(1, 1, dtype=torch.int32), torch.tensor(0.125),
             torch.zeros(1, 2, dtype=torch.int32), 16)
+
+
+def test_sdpa_struct_field_offsets_match_c():
+    from torch_rbln_b200 import cabi
+
+    fields = [f for f, _ in cabi.SdpaParams._fields_]
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"rbln_attn.h\"\nint main(void){\n"
+    for f in fields:
+        src += f'  printf("%zu\\n", offsetof(rbln_sdpa_params_t, {f}));\n'
+    src += '  printf("%zu\\n", sizeof(rbln_sdpa_params_t));\n  return 0;\n}\n'
+    with tempfile.TemporaryDirectory() as td:
+        c = os.path.join(td, "off.c")
+        exe = os.path.join(td, "off")
+        open(c, "w").write(src)
+        cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+        r = subprocess.run(["gcc", c, "-o", exe, "-I", os.path.join(ROOT, "include"), "-I", cuda_inc],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            pytest.skip("gcc or CUDA headers unavailable: " + r.stderr[-200:])
+        vals = [int(x) for x in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    got = [getattr(cabi.SdpaParams, f).offset for f in fields] + [ctypes.sizeof(cabi.SdpaParams)]
+    assert vals == got

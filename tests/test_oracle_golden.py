@@ -187,3 +187,18 @@ def test_contiguous_mock_restatement_matches_reference(idx, op):
     out = opa.mock_decode_contiguous(c["q"], c["k"], c["v"], kc, vc, c["ctx"], torch.tensor(1.0 / math.sqrt(c["D"])),
                                      mask)
     assert torch.equal(out, exp["out"])
+
+
+@pytest.mark.parametrize("idx", range(len(PREFILL)))
+def test_contiguous_prefill_restatement_matches_reference(idx):
+    """The prefill CPU-baseline restatement equals the reference bit for bit."""
+    c = PREFILL[idx]
+    exp = c["results"]["paged_attn_prefill_s1"]
+    D, S, ms, dt, s1 = c["D"], c["S"], c["max_seq"], c["dtype"], c["s1"]
+    kc = torch.zeros([1, c["Hkv"], 1, ms, D], dtype=dt)
+    vc = torch.zeros_like(kc)
+    kc[:, :, :, :s1], vc[:, :, :, :s1] = c["kpre"], c["vpre"]
+    mask = torch.ones([1, S, ms], dtype=dt).tril(diagonal=s1).view(1, 1, 1, S, ms)
+    out = opa.mock_prefill_contiguous(c["q"], c["k"], c["v"], kc, vc, s1, torch.tensor(1.0 / math.sqrt(D)), mask)
+    assert torch.equal(out, exp["out"])
+    assert _sha(kc) == exp["kc"] and _sha(vc) == exp["vc"]

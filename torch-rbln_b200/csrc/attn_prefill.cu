@@ -696,7 +696,10 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.scale = p->scale;
   a.scale_dev = p->scale_dev;
   a.err = p->error_flags;
-  return launch_tc_any(Lc, st);
+  if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
+  const int rc = launch_tc_any(Lc, st);
+  if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
+  return rc;
 }
 
 }  // namespace

@@ -64,6 +64,21 @@ class PagedAttnParams(ctypes.Structure):
     ]
 
 
+class SdpaParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_i32), ("num_heads", c_i32), ("num_kv_heads", c_i32), ("q_len", c_i32), ("kv_len", c_i32),
+        ("head_dim", c_i32), ("dtype", c_i32),
+        ("q", c_vp), ("q_stride", c_i64 * 3),
+        ("k", c_vp), ("k_stride", c_i64 * 3),
+        ("v", c_vp), ("v_stride", c_i64 * 3),
+        ("out", c_vp), ("out_stride", c_i64 * 3),
+        ("lse", c_vp), ("lse_stride", c_i64 * 3),
+        ("mask", c_vp), ("mask_dtype", c_i32), ("mask_additive", c_i32), ("mask_stride", c_i64 * 4),
+        ("causal", c_i32), ("scale", ctypes.c_float),
+        ("error_flags", c_vp),
+    ]
+
+
 # entry points: (name, restype, argtypes)
 ENTRY_POINTS = {
     "rbln_attn_abi_version": (ctypes.c_int, []),
@@ -72,6 +87,9 @@ ENTRY_POINTS = {
                                                         ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_paged_causal_attn_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
+    "rbln_paged_causal_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
+    "rbln_paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
+    "rbln_sdpa_fwd": (ctypes.c_int, [ctypes.POINTER(SdpaParams), c_vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -157,6 +175,26 @@ def attach_workspace(p: PagedAttnParams, device, keep: dict) -> None:
         ws = torch.empty(n.value, dtype=torch.uint8, device=device)
         keep["ws"] = ws
         p.workspace, p.workspace_bytes = ws.data_ptr(), n.value
+
+
+def sdpa_params(q, k, v, out, lse=None, causal=True, scale=None):
+    """Fills SdpaParams for q [B, Hq, L, D], k/v [B, Hkv, S, D] (inner dim contiguous)."""
+    p = SdpaParams()
+    p.batch, p.num_heads, p.q_len, p.head_dim = q.shape
+    p.num_kv_heads, p.kv_len = k.shape[1], k.shape[2]
+    p.dtype = _DT[q.dtype]
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        setattr(p, name, t.data_ptr())
+        st = getattr(p, name + "_stride")
+        for i in range(3):
+            st[i] = t.stride(i)
+    if lse is not None:
+        p.lse = lse.data_ptr()
+        for i in range(3):
+            p.lse_stride[i] = lse.stride(i)
+    p.causal = 1 if causal else 0
+    p.scale = scale if scale is not None else 1.0 / (q.shape[-1] ** 0.5)
+    return p
 
 
 def call(name: str, p: PagedAttnParams, stream: Optional[torch.cuda.Stream] = None) -> int:

@@ -60,14 +60,16 @@ WORKLOADS = {
     # profiling case for ncu --set full: inputs still larger than L2, ~0.35 GB on the device
     "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
                          B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False),
+    # long context, KV heads sharded over the ranks + one NCCL all-gather of head outputs
     "decode_long": dict(desc="paged decode bf16 B=32 Hq=64 Hkv=8 D=128 bs=16 L=32768 pool=65536",
-                        B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False),
+                        B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False,
+                        shard="heads"),
 }
 
 
-def build_decode(wl: dict, device, seed: int = 0):
+def build_decode(wl: dict, device, seed: int = 0, pool_seed: int = None):
     """Seeded synthetic decode inputs. Lengths / block table on the CPU
-    generator; the KV pool is drawn on the device (same seed) for speed."""
+    generator; the KV pool is drawn on the device (seed + 1, or pool_seed)."""
     g = torch.Generator().manual_seed(seed)
     B, Hkv, G, D, bs = wl["B"], wl["Hkv"], wl["G"], wl["D"], wl["bs"]
     lens = torch.randint(wl["lmin"], wl["lmax"] + 1, (B,), generator=g)
@@ -86,7 +88,7 @@ def build_decode(wl: dict, device, seed: int = 0):
     k = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
     v = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
     seq = (lens - 1).to(torch.int32).reshape(B, 1)
-    gd = torch.Generator(device=device).manual_seed(seed + 1)
+    gd = torch.Generator(device=device).manual_seed(seed + 1 if pool_seed is None else pool_seed)
     shape = [nblk, Hkv, 1, bs, D]
     if wl["fp8"]:
         kc, ks = _fp8_pool(shape, gd, device)
@@ -213,7 +215,17 @@ def run_ours(args, wl_name):
     from torch_rbln_b200 import cabi
 
     wl = WORKLOADS[wl_name]
-    d = build_decode(wl, dev, seed=1000 * rank)
+    head_shard = wl.get("shard") == "heads" and ws > 1
+    if head_shard:
+        # every rank sees the same sequences and block table; it holds only its
+        # slice of the KV heads (and their query heads)
+        from torch_rbln_b200 import sharding
+
+        sharding.kv_head_range(wl["Hkv"], rank, ws)
+        wl = dict(wl, Hkv=wl["Hkv"] // ws)
+        d = build_decode(wl, dev, seed=0, pool_seed=1 + rank)
+    else:
+        d = build_decode(wl, dev, seed=1000 * rank)
     q, k, v = d["q"].to(dev), d["k"].to(dev), d["v"].to(dev)
     seq, bt = d["seq"].to(dev), d["bt"].to(dev)
     kc, vc = d["kcache"], d["vcache"]
@@ -225,7 +237,8 @@ def run_ours(args, wl_name):
     def op_call(qq, kk, vv, ss, bb):
         if d["fp8"]:
             return ops.paged_causal_attn_decode_kvfp8(qq, kk, vv, kc, vc, ks, vs, ss, scale_t, bb, d["bs"])
-        return ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
+        o = ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
+        return sharding.all_gather_heads(o, ws) if head_shard else o
 
     # C-ABI parameter block with the timing hook around the main kernel
     p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs)
@@ -245,6 +258,8 @@ def run_ours(args, wl_name):
         rc = entry(pref, sh)
         if rc != 0:
             raise RuntimeError(f"rbln_paged_causal_attn_decode failed: {rc}")
+        if head_shard:
+            sharding.all_gather_heads(keep["out"], ws)
 
     for _ in range(args.warmup):
         cabi_step()
@@ -275,7 +290,8 @@ def run_ours(args, wl_name):
     # ---- e2e: public torch op, host buffers, H2D + D2H inside the timed region
     pin = lambda t: t.cpu().pin_memory()
     hq, hk, hv, hs, hb = pin(d["q"]), pin(d["k"]), pin(d["v"]), pin(d["seq"]), pin(d["bt"])
-    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    out_heads = q.shape[1] * (ws if head_shard else 1)
+    hout = torch.empty((q.shape[0], out_heads) + tuple(q.shape[2:]), dtype=q.dtype).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs, hb))
     d2h = hout.numel() * hout.element_size()
     for _ in range(max(2, args.warmup)):
@@ -316,11 +332,13 @@ def run_ours(args, wl_name):
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if head_shard else "weak",
         "vs_baseline": None,
         "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
         "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
-        "config": {"workload": wl["desc"], "global_batch": d["B"] * ws, "parallelism": f"batch-sharded x{ws}",
+        "config": {"workload": WORKLOADS[wl_name]["desc"], "global_batch": d["B"] if head_shard else d["B"] * ws,
+                   "parallelism": (f"kv-head-sharded x{ws} + NCCL all-gather of head outputs" if head_shard
+                                   else f"batch-sharded x{ws}"),
                    "l2": "inputs larger than L2 (KV pool " + f"{kc.numel() * kc.element_size() * 2 / 1e9:.2f} GB)",
                    "bytes_per_step_per_gpu": nbytes},
         "e2e": {"value": round(ws * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -514,24 +532,21 @@ def build_sdpa(wl, seed=0):
     return dict(q=q, k=k, v=v, flops=flops, scale=1.0 / math.sqrt(D))
 
 
-def _timed_kernel_loop(args, stream, step, flush):
-    """Per-iteration CUDA events around `step` (which records the kernel
-    events itself), with an L2 flush outside the timed window."""
-    op_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    k_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for pair in op_ev + k_ev:
-        pair[0].record(stream)
-        pair[1].record(stream)
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        flush.zero_()
-        op_ev[i][0].record(stream)
-        step(*k_ev[i])
-        op_ev[i][1].record(stream)
-    torch.cuda.synchronize()
-    op_ms = statistics.mean(a.elapsed_time(b) for a, b in op_ev)
-    k_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
-    return op_ms, k_ms
+def _timed_kernel_loop(args, stream, step, kernel_step, flush):
+    """Per-iteration CUDA events on the launch stream around the whole op
+    (`step`) and, in separate iterations, around the main kernel alone
+    (`kernel_step`), each preceded by an L2 flush outside the timed window."""
+    def timed(fn):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+    return timed(step), timed(kernel_step)
 
 
 def run_compute_ours(args, wl_name):
@@ -559,13 +574,18 @@ def run_compute_ours(args, wl_name):
         q, k, v, seq, bt = (d[x].to(dev) for x in ("q", "k", "v", "seq", "bt"))
         kc, vc = d["kcache"], d["vcache"]
         p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
-        pref = ctypes.byref(p)
+        # the same call without new rows to append launches the attention kernel alone
+        pk, keepk = cabi.paged_params(q, None, None, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
+        pref, pkref = ctypes.byref(p), ctypes.byref(pk)
         scale_t = torch.tensor(d["scale"])
 
-        def step(e0=None, e1=None):
-            p.prof_events[0] = e0.cuda_event if e0 is not None else None
-            p.prof_events[1] = e1.cuda_event if e1 is not None else None
+        def step():
             rc = L.rbln_paged_causal_attn_prefill(pref, sh)
+            if rc != 0:
+                raise RuntimeError(f"rbln_paged_causal_attn_prefill failed: {rc}")
+
+        def kernel_step():
+            rc = L.rbln_paged_causal_attn_prefill(pkref, sh)
             if rc != 0:
                 raise RuntimeError(f"rbln_paged_causal_attn_prefill failed: {rc}")
 
@@ -588,14 +608,12 @@ def run_compute_ours(args, wl_name):
         sp = cabi.sdpa_params(q, k, v, out, lse, causal=True, scale=d["scale"])
         spref = ctypes.byref(sp)
 
-        def step(e0=None, e1=None):
-            if e0 is not None:
-                e0.record(stream)
+        def step():
             rc = L.rbln_sdpa_fwd(spref, sh)
-            if e1 is not None:
-                e1.record(stream)
             if rc != 0:
                 raise RuntimeError(f"rbln_sdpa_fwd failed: {rc}")
+
+        kernel_step = step  # one kernel per call
 
         import torch.nn.functional as F
 
@@ -617,7 +635,7 @@ def run_compute_ours(args, wl_name):
     if ws > 1:
         dist.barrier()
     with ClockSampler(local) as clk:
-        op_ms, k_ms = _timed_kernel_loop(args, stream, step, flush)
+        op_ms, k_ms = _timed_kernel_loop(args, stream, step, kernel_step, flush)
     if ws > 1:
         dist.barrier()
 

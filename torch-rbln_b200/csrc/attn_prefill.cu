@@ -475,6 +475,419 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two-tile variant for the mask-free paths (causal / bidirectional), the hot
+// path of chunked prefill and SDPA.
+//
+// A CTA owns two 128-row query tiles (A: tokens [s0, s0+QT), B: the next QT
+// tokens) and streams 64-key K/V tiles through a 3-stage ring. Each query
+// tile has its own softmax warpgroup and its own TMEM buffers (S double
+// buffered, 64 columns each; O up to 128 columns), so while one warpgroup
+// turns S into P the tensor core runs the other tile's MMAs:
+//   warp 0       TMA producer          warp 1   MMA issuer / TMEM owner
+//   warps 2-5    softmax, tile A       warps 6-9 softmax, tile B
+// Per KV tile j the MMA thread issues QK_A(j), QK_B(j), then PV_A(j-1),
+// PV_B(j-1). Shared memory: Q 2x32 KB, K/V 3x32 KB, P 2x16 KB (D = 128).
+// A quarter of the softmax exponentials are evaluated on the FMA pipe with a
+// polynomial (exp2_fma) so the SFU is not the bottleneck.
+// ---------------------------------------------------------------------------
+constexpr int BN2 = 64;          // keys per KV tile
+constexpr int kStages2 = 3;
+constexpr int kThreads2 = 320;   // 10 warps
+constexpr int kPanel64 = 64 * 128;  // 64 rows x 128 bytes
+
+// 2^x for x <= 8 on the FMA pipe: x = n + f, f in [0,1); 2^f by a cubic
+// least-squares fit at Chebyshev nodes (max relative error 7.7e-5, 2^-13.7),
+// 2^n by adding n to the exponent field. Inputs below -126 (masked scores
+// are -inf) give exactly 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float n = floorf(xc);
+  const float f = xc - n;
+  float p = fmaf(0.07790716737508774f, f, 0.22623319923877716f);
+  p = fmaf(p, f, 0.6957771182060242f);
+  p = fmaf(p, f, 0.999927818775177f);
+  const float r = __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+  return x < -126.f ? 0.f : r;
+}
+
+template <int D>
+struct SmemLayout2 {
+  static constexpr int NP = D / 64;
+  static constexpr int QA = 0;                                  // NP panels of 128 rows
+  static constexpr int QB = QA + NP * kPanelBytes;
+  static constexpr int K0 = QB + NP * kPanelBytes;              // stage s: K0 + s*NP*kPanel64
+  static constexpr int V0 = K0 + kStages2 * NP * kPanel64;
+  static constexpr int PA = V0 + kStages2 * NP * kPanel64;      // one 128-row panel (64 keys)
+  static constexpr int PB = PA + kPanelBytes;
+  static constexpr int BAR = PB + kPanelBytes;
+  static constexpr int TMEM_SLOT = BAR + 32 * 8;
+  static constexpr int ABORT = TMEM_SLOT + 8;
+  static constexpr int TOTAL = ABORT + 8;
+  static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
+};
+
+enum Bar2 {
+  C_Q = 0,
+  C_KF0, C_KF1, C_KF2,
+  C_VF0, C_VF1, C_VF2,
+  C_KE0, C_KE1, C_KE2,
+  C_SFA0, C_SFA1, C_SFB0, C_SFB1,
+  C_SRA0, C_SRA1, C_SRB0, C_SRB1,
+  C_PFA, C_PFB, C_PVA, C_PVB, C_DONE, C_COUNT
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  using L = SmemLayout2<D>;
+  constexpr int NP = L::NP;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  volatile int* abort = reinterpret_cast<volatile int*>(sgen + L::ABORT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::TMEM_SLOT);
+  auto bar = [&](int i) { return sbase + L::BAR + 8u * i; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heaviest query tiles (latest positions, most keys under the causal mask) first
+  const int qtile = a.q_tiles - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int s0 = qtile * 2 * a.QT;
+  const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
+  // keys for both tiles: the CTA spans 2*QT query tokens
+  int kv_end = 0;
+  if (seq_off >= 0) {
+    const int s_hi = min(s0 + 2 * a.QT, a.S_q);
+    int end = (a.mask_mode == MM_CAUSAL) ? seq_off + s_hi : ((a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q);
+    if (a.bt == nullptr) end = min(end, a.kv_extra);
+    kv_end = max(0, min(end, a.span));
+  }
+  const int ntiles = (kv_end + BN2 - 1) / BN2;
+
+  if (threadIdx.x == 0) {
+    *abort = 0;
+    for (int i = 0; i < C_COUNT; ++i) {
+      const bool four = (i >= C_SRA0 && i <= C_SRB1) || i == C_PFA || i == C_PFB;
+      mbar_init(bar(i), four ? 4u : 1u);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S_A[2] 0/64, S_B[2] 128/192, O_A 256, O_B 384
+  auto t_s = [&](int x, int sb) { return tmem + x * 128 + sb * 64; };
+  auto t_o = [&](int x) { return tmem + 256 + x * 128; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        mbar_arrive_expect_tx(bar(C_Q), 2 * NP * a.QT * a.G * 128);
+        for (int p = 0; p < NP; ++p) {
+          tma_load_5d(sbase + L::QA + p * kPanelBytes, &tm_q, bar(C_Q), p * 64, s0, 0, h, b);
+          tma_load_5d(sbase + L::QB + p * kPanelBytes, &tm_q, bar(C_Q), p * 64, s0 + a.QT, 0, h, b);
+        }
+      }
+      const int rpb = min(a.bs, BN2);
+      const int nbox = BN2 / rpb;
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % kStages2;
+        if (j >= kStages2 &&
+            !__all_sync(0xffffffffu, mbar_wait(bar(C_KE0 + st), ((j / kStages2) - 1) & 1, abort)))
+          break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar(C_KF0 + st), NP * kPanel64);
+          mbar_arrive_expect_tx(bar(C_VF0 + st), NP * kPanel64);
+        }
+        __syncwarp();
+        const int t0 = j * BN2;
+        for (int i = lane; i < nbox; i += 32) {
+          const int key = t0 + i * rpb;
+          int blk = a.num_blocks;  // out of range -> zero fill
+          int row = 0;
+          if (key < kv_end) {
+            if (a.bt == nullptr) {
+              blk = b;
+              row = key;
+            } else {
+              const int bi = key / a.bs;
+              row = key - bi * a.bs;
+              if (bi < a.max_blocks) {
+                const int64_t v = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+                if (v >= 0 && v < a.num_blocks) {
+                  blk = (int)v;
+                } else if (a.err) {
+                  atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+                }
+              }
+            }
+          }
+          const uint32_t koff = sbase + L::K0 + st * NP * kPanel64 + i * rpb * 128;
+          const uint32_t voff = sbase + L::V0 + st * NP * kPanel64 + i * rpb * 128;
+          for (int p = 0; p < NP; ++p) {
+            tma_load_4d(koff + p * kPanel64, &tm_k, bar(C_KF0 + st), p * 64, row, h, blk);
+            tma_load_4d(voff + p * kPanel64, &tm_v, bar(C_VF0 + st), p * 64, row, h, blk);
+          }
+        }
+        issued = j + 1;
+      }
+      if (*abort) {
+        for (int j = max(0, issued - kStages2); j < issued; ++j) {
+          const int st = j % kStages2;
+          const long long t0c = clock64();
+          while (!mbar_try_wait(bar(C_KF0 + st), (j / kStages2) & 1) && clock64() - t0c < 2000000) {
+          }
+          while (!mbar_try_wait(bar(C_VF0 + st), (j / kStages2) & 1) && clock64() - t0c < 4000000) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t id_qk = idesc_f16(BF16, 128, BN2, false);
+      const uint32_t id_pv = idesc_f16(BF16, 128, D, true);
+      auto issue_pv = [&](int jj) -> bool {
+        const int stp = jj % kStages2;
+        const uint32_t vb = sbase + L::V0 + stp * NP * kPanel64;
+        if (!mbar_wait(bar(C_VF0 + stp), (jj / kStages2) & 1, abort)) return false;
+        for (int x = 0; x < 2; ++x) {
+          if (!mbar_wait(bar(x == 0 ? C_PFA : C_PFB), jj & 1, abort)) return false;
+          tc_fence_after();
+          const uint32_t pb = sbase + (x == 0 ? L::PA : L::PB);
+#pragma unroll
+          for (int kk = 0; kk < BN2 / 16; ++kk) {
+            const uint64_t ad = sw128_desc(pb + kk * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(vb + kk * 16 * 128, kPanel64, 1024);
+            umma_f16_ss(t_o(x), ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bar(x == 0 ? C_PVA : C_PVB));
+        }
+        umma_commit(bar(C_KE0 + stp));
+        return true;
+      };
+      bool ok = mbar_wait(bar(C_Q), 0, abort);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j % kStages2, sb = j & 1;
+        if (!mbar_wait(bar(C_KF0 + st), (j / kStages2) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        const uint32_t kb = sbase + L::K0 + st * NP * kPanel64;
+        for (int x = 0; x < 2 && ok; ++x) {
+          if (j >= 2 && !mbar_wait(bar((x == 0 ? C_SRA0 : C_SRB0) + sb), ((j >> 1) - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qb = sbase + (x == 0 ? L::QA : L::QB);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = sw128_desc(qb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(kb + (kk >> 2) * kPanel64 + (kk & 3) * 32, 16, 1024);
+            umma_f16_ss(t_s(x, sb), ad, bd, id_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar((x == 0 ? C_SFA0 : C_SFB0) + sb));
+        }
+        if (ok && j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok) ok = issue_pv(ntiles - 1);
+      if (!ok) {
+        umma_commit(bar(C_DONE));
+        const long long t0c = clock64();
+        while (!mbar_try_wait(bar(C_DONE), 0) && clock64() - t0c < 4000000) {
+        }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- softmax
+    const int x = (warp >= 6) ? 1 : 0;  // query tile
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int g = r / a.QT, i = r - g * a.QT;
+    const int s = s0 + x * a.QT + i;
+    const bool row_ok = (g < a.G) && (s < a.S_q);
+    const int qpos = seq_off + s;
+    const int none_limit = (a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q;
+    // first key any row of this tile may not see (tile-uniform bound for the fast path)
+    const int tile_first_q = seq_off + s0 + x * a.QT;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const float qk_mult = scale * kLog2e;
+    const int bar_sf = x == 0 ? C_SFA0 : C_SFB0, bar_sr = x == 0 ? C_SRA0 : C_SRB0;
+    const int bar_pf = x == 0 ? C_PFA : C_PFB, bar_pv = x == 0 ? C_PVA : C_PVB;
+    uint8_t* pbuf = sgen + (x == 0 ? L::PA : L::PB);
+    float m_run = neg_inf(), l_run = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(bar_sf + sb), (j >> 1) & 1, abort))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float xv[BN2];
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < BN2 / 32; ++c) {
+        uint32_t tmp[32];
+        tmem_ld32(t_s(x, sb) + lane_off + c * 32, tmp);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) xv[c * 32 + e] = __uint_as_float(tmp[e]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(bar_sr + sb));
+
+      const int t0 = j * BN2;
+      const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN2 - 1 <= tile_first_q) && (t0 + BN2 <= kv_end)
+                                                       : (t0 + BN2 <= kv_end);
+      float mt = neg_inf();
+      if (interior && row_ok) {
+#pragma unroll
+        for (int c = 0; c < BN2; ++c) {
+          xv[c] *= qk_mult;
+          mt = fmaxf(mt, xv[c]);
+        }
+      } else {
+        const int lim = (a.mask_mode == MM_CAUSAL) ? min(qpos + 1, kv_end) : min(none_limit, kv_end);
+#pragma unroll
+        for (int c = 0; c < BN2; ++c) {
+          const bool keep = row_ok && (t0 + c < lim);
+          xv[c] = keep ? xv[c] * qk_mult : neg_inf();
+          mt = fmaxf(mt, xv[c]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mt);
+      const bool grow = m_new > m_run + 8.f;
+      float factor = 1.f;
+      if (grow) {
+        factor = exp2_approx(m_run - m_new);
+        l_run *= factor;
+        m_run = m_new;
+      }
+      const float mu = (m_run == neg_inf()) ? 0.f : m_run;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN2; ++c) {
+        const float e = ((c & 3) == 3) ? exp2_fma(xv[c] - mu) : exp2_approx(xv[c] - mu);
+        xv[c] = e;
+        lsum += e;
+      }
+      l_run += lsum;
+
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(bar_pv), (j - 1) & 1, abort))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o(x) + lane_off + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          tmem_st32(t_o(x) + lane_off + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      uint8_t* prow = pbuf + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < BN2 / 8; ++ch) {
+        uint4 v;
+        v.x = pack2<BF16>(xv[ch * 8 + 0], xv[ch * 8 + 1]);
+        v.y = pack2<BF16>(xv[ch * 8 + 2], xv[ch * 8 + 3]);
+        v.z = pack2<BF16>(xv[ch * 8 + 4], xv[ch * 8 + 5]);
+        v.w = pack2<BF16>(xv[ch * 8 + 6], xv[ch * 8 + 7]);
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) * 16)) = v;
+      }
+      // keys past kv_end in the last tile may hold unwritten memory: tile A's
+      // warpgroup zeroes their V rows before its P is released (both PV MMAs
+      // of this tile come after that release)
+      if (x == 0 && j == ntiles - 1 && t0 + BN2 > kv_end) {
+        const int st = j % kStages2;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(C_VF0 + st), (j / kStages2) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        if (r < BN2 && t0 + r >= kv_end) {
+          uint8_t* vrow = sgen + L::V0 + st * NP * kPanel64 + r * 128;
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c16 = 0; c16 < 8; ++c16)
+              *reinterpret_cast<uint4*>(vrow + p * kPanel64 + c16 * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(bar_pf));
+    }
+
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(bar_pv), (ntiles - 1) & 1, abort));
+    tc_fence_after();
+    if (ok) {
+      const float inv = 1.f / l_run;
+      char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (ntiles > 0) {
+          __syncwarp();
+          tmem_ld32(t_o(x) + lane_off + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 v;
+            v.x = pack2<BF16>(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+            v.y = pack2<BF16>(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+            v.z = pack2<BF16>(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+            v.w = pack2<BF16>(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + (c * 32 + q4 * 8) * 2) = v;
+          }
+        }
+      }
+      if (row_ok && a.lse) {
+        const float v =
+            (m_run == neg_inf() || l_run == 0.f) ? neg_inf() : (m_run + __log2f(l_run)) * 0.6931471805599453f;
+        a.lse[b * a.ls_b + h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // Writes the chunk's new k/v rows into the paged cache at [seq[b], seq[b]+S_q).
 // One warp per token: lanes 0-15 copy the K row, lanes 16-31 the V row.
 template <int D>
@@ -563,6 +976,30 @@ int launch_tc(const TcLaunch& Lc, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
+template <int D, bool BF16>
+int launch_tc2(const TcLaunch& Lc, cudaStream_t st) {
+  using SL = SmemLayout2<D>;
+  if (cudaFuncSetAttribute(attn_fwd_tc2_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SL::ALLOC) !=
+      cudaSuccess)
+    return RBLN_ERR_LAUNCH;
+  dim3 grid(Lc.a.q_tiles, Lc.a.Hkv, Lc.a.B);
+  attn_fwd_tc2_kernel<D, BF16><<<grid, kThreads2, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+int launch_tc2_any(const TcLaunch& Lc, cudaStream_t st) {
+  if (Lc.D == 128) return Lc.bf16 ? launch_tc2<128, true>(Lc, st) : launch_tc2<128, false>(Lc, st);
+  return Lc.bf16 ? launch_tc2<64, true>(Lc, st) : launch_tc2<64, false>(Lc, st);
+}
+
+// The two-tile kernel serves mask-free causal/bidirectional attention whose
+// block size gives 1 KB-aligned 64-row boxes.
+bool use_tc2(const AttnArgs& a) {
+  if (a.mask || a.pmask || a.mask_mode == MM_KEEP) return false;
+  if (a.bt == nullptr) return true;
+  return (a.bs >= 8 && a.bs <= BN2 && BN2 % a.bs == 0) || (a.bs >= BN2 && a.bs % BN2 == 0);
+}
+
 int launch_tc_any(const TcLaunch& Lc, cudaStream_t st) {
   if (Lc.D == 128) return Lc.bf16 ? launch_tc<128, true>(Lc, st) : launch_tc<128, false>(Lc, st);
   return Lc.bf16 ? launch_tc<64, true>(Lc, st) : launch_tc<64, false>(Lc, st);
@@ -645,7 +1082,8 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   TcLaunch Lc{};
   Lc.D = D;
   Lc.bf16 = p->q_dtype == RBLN_DT_BF16;
-  const int rpb = std::min(bs, BN);
+  const bool two_tile = !keep_mask_op && !p->mask && ((bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0));
+  const int rpb = std::min(bs, two_tile ? BN2 : BN);
   if (!map_q(&Lc.tq, p->q, p->q_dtype, p->batch, p->num_kv_heads, G, p->q_len, D, p->q_stride, QT))
     return RBLN_ERR_LAUNCH;
   if (!map_kv(&Lc.tk, p->kcache, p->kv_dtype, p->num_blocks, p->num_kv_heads, bs, D, p->cache_stride[0],
@@ -675,7 +1113,7 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.G = G;
   a.S_q = p->q_len;
   a.QT = QT;
-  a.q_tiles = q_tiles;
+  a.q_tiles = two_tile ? (p->q_len + 2 * QT - 1) / (2 * QT) : q_tiles;
   if (keep_mask_op) {
     a.mask_mode = MM_KEEP;
     a.mask = p->mask;
@@ -697,7 +1135,7 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.scale_dev = p->scale_dev;
   a.err = p->error_flags;
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
-  const int rc = launch_tc_any(Lc, st);
+  const int rc = two_tile ? launch_tc2_any(Lc, st) : launch_tc_any(Lc, st);
   if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
   return rc;
 }
@@ -720,9 +1158,11 @@ int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os
   const int q_tiles = (L + QT - 1) / QT;
   if (q_tiles > 65535 || Hkv > 65535 || B > 65535) return RBLN_ERR_UNSUPPORTED;
   if (!map_q(&Lc.tq, q, dtype, B, Hkv, G, L, D, qs, QT)) return RBLN_ERR_LAUNCH;
-  // k [B, Hkv, S, D] seen as a pool of B blocks of S rows, 128-row boxes
-  if (!map_kv(&Lc.tk, k, dtype, B, Hkv, S, D, ks[0], ks[1], ks[2], BN)) return RBLN_ERR_LAUNCH;
-  if (!map_kv(&Lc.tv, v, dtype, B, Hkv, S, D, vs[0], vs[1], vs[2], BN)) return RBLN_ERR_LAUNCH;
+  const bool two_tile = (mask == nullptr);
+  const int rows_per_box = two_tile ? BN2 : BN;
+  // k [B, Hkv, S, D] seen as a pool of B blocks of S rows
+  if (!map_kv(&Lc.tk, k, dtype, B, Hkv, S, D, ks[0], ks[1], ks[2], rows_per_box)) return RBLN_ERR_LAUNCH;
+  if (!map_kv(&Lc.tv, v, dtype, B, Hkv, S, D, vs[0], vs[1], vs[2], rows_per_box)) return RBLN_ERR_LAUNCH;
   AttnArgs& a = Lc.a;
   a.out = (char*)out;
   a.os_b = os[0] * 2;
@@ -761,6 +1201,10 @@ int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os
   }
   a.scale = scale;
   a.err = err;
+  if (two_tile) {
+    a.q_tiles = (L + 2 * QT - 1) / (2 * QT);
+    return launch_tc2_any(Lc, st);
+  }
   return launch_tc_any(Lc, st);
 }
 

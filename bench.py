@@ -597,7 +597,7 @@ def run_compute_ours(args, wl_name):
         out_shape, out_dtype = q.shape, q.dtype
         metric = "paged chunked prefill TFLOP/s"
         launches = 2
-        kernel = "attn_fwd_tc_kernel<128, bf16> (tcgen05/TMEM/TMA)"
+        kernel = "attn_fwd_tc2_kernel<128, bf16> (tcgen05/TMEM/TMA, two query tiles per CTA)"
         dtype = "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
     else:
@@ -625,7 +625,8 @@ def run_compute_ours(args, wl_name):
         metric = "SDPA TFLOP/s"
         launches = 1
         kernel = ("sdpa_f32_kernel<64> (exact-fp32 SIMT; tensor cores have no fp32 mode)"
-                  if wl["dtype"] == torch.float32 else "attn_fwd_tc_kernel<128, bf16> (tcgen05/TMEM/TMA)")
+                  if wl["dtype"] == torch.float32
+                  else "attn_fwd_tc2_kernel<128, bf16> (tcgen05/TMEM/TMA, two query tiles per CTA)")
         dtype = "f32" if wl["dtype"] == torch.float32 else "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
 

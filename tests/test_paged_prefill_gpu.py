@@ -136,7 +136,8 @@ def test_prefill_keep_mask_matches_causal():
     got_keep = run_gpu(d, op="keep", mask=keep)
     check(got_keep, run_oracle(d, op="keep", mask=keep))
     got_causal = run_gpu(d, causal=True)
-    torch.testing.assert_close(got_keep[0].float(), got_causal[0].float(), rtol=0, atol=0)
+    # different kernels (masked vs mask-free) round differently: same tolerance
+    torch.testing.assert_close(got_keep[0].float(), got_causal[0].float(), rtol=RTOL, atol=ATOL)
 
 
 def test_prefill_position_mask():
@@ -150,8 +151,9 @@ def test_prefill_position_mask():
 
 
 def test_prefill_chunked_equals_single_pass():
-    """Two chunks of 64 tokens in a row give the same output rows as one
-    128-token pass: the second call reads back what the first one wrote."""
+    """Two chunks of 64 tokens in a row give the same output rows (within
+    tolerance) and the same cache as one 128-token pass: the second call
+    reads back what the first one wrote."""
     d = make_prefill(1, 2, 4, 128, 16, 128, [0], seed=9)
     full = run_gpu(d, causal=True)
     d1 = dict(d, q=d["q"][:, :, :, :64].contiguous(), k=d["k"][:, :, :, :64].contiguous(),
@@ -161,7 +163,8 @@ def test_prefill_chunked_equals_single_pass():
               v=d["v"][:, :, :, 64:].contiguous(), kcache=x1[1], vcache=x1[2],
               seq=torch.tensor([[64]], dtype=torch.int32))
     x2 = run_gpu(d2, causal=True)
-    torch.testing.assert_close(torch.cat([x1[0], x2[0]], dim=3).float(), full[0].float(), rtol=0, atol=0)
+    # tile boundaries differ between the two schedules, so compare at the stated tolerance
+    torch.testing.assert_close(torch.cat([x1[0], x2[0]], dim=3).float(), full[0].float(), rtol=RTOL, atol=ATOL)
     assert torch.equal(x2[1], full[1]) and torch.equal(x2[2], full[2])
 
 

@@ -576,6 +576,8 @@ def run_compute_ours(args, wl_name):
         p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
         # the same call without new rows to append launches the attention kernel alone
         pk, keepk = cabi.paged_params(q, None, None, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
+        cabi.attach_workspace(p, dev, keep, prefill=True)
+        cabi.attach_workspace(pk, dev, keepk, prefill=True)
         pref, pkref = ctypes.byref(p), ctypes.byref(pk)
         scale_t = torch.tensor(d["scale"])
 
@@ -596,7 +598,7 @@ def run_compute_ours(args, wl_name):
         host_inputs = [d["q"], d["k"], d["v"], d["seq"], d["bt"]]
         out_shape, out_dtype = q.shape, q.dtype
         metric = "paged chunked prefill TFLOP/s"
-        launches = 2
+        launches = 3  # schedule pre-pass, append, attention
         kernel = "attn_fwd_tc2_kernel<128, bf16> (tcgen05/TMEM/TMA, two query tiles per CTA)"
         dtype = "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"

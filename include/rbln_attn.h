@@ -146,6 +146,12 @@ int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_
  * p->mask is required. */
 int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream);
 
+/* Optional scratch for the prefill entry points: when p->workspace holds
+ * this many bytes, a pre-pass orders the (sequence, query-tile) work items
+ * longest first before the attention kernel runs; without it the kernel
+ * uses a fixed order. 0 when no pre-pass applies. */
+int rbln_paged_prefill_workspace_size(const rbln_paged_attn_params_t* p, size_t* bytes);
+
 /* rbln_custom_ops::paged_causal_attn_prefill
  * (reference frontend register_custom_ops.py:324-379,
  *  CPU semantics test_custom_kernel.py:262-343).

@@ -173,3 +173,27 @@ def test_prefill_larger_context():
     32/8 heads, D=128, bs=16) on two sequences with cached context."""
     d = make_prefill(2, 8, 4, 128, 16, 512, [1500, 3333], seed=10)
     check(run_gpu(d, causal=True), run_oracle(d, causal=True))
+
+
+def test_prefill_schedule_pre_pass_is_order_only():
+    """With and without the longest-first pre-pass (workspace given or not),
+    the C-ABI call computes the same result bit for bit: only the order in
+    which CTAs start changes."""
+    import ctypes
+
+    from torch_rbln_b200 import cabi
+
+    d = make_prefill(4, 2, 4, 128, 16, 200, [3000, 5, 900, 40], seed=12)
+    outs = []
+    for use_ws in (False, True):
+        x = {k: (v.to(DEV) if isinstance(v, torch.Tensor) and k != "scale" else v) for k, v in d.items()}
+        p, keep = cabi.paged_params(x["q"], x["k"], x["v"], x["kcache"], x["vcache"], x["seq"], x["block_table"],
+                                    16, float(x["scale"]), causal=1)
+        if use_ws:
+            cabi.attach_workspace(p, DEV, keep, prefill=True)
+            assert p.workspace_bytes > 0
+        assert cabi.call("rbln_paged_causal_attn_prefill", p) == cabi.OK
+        torch.cuda.synchronize()
+        outs.append(keep["out"].cpu())
+    assert torch.equal(outs[0], outs[1])
+    check((outs[1], None, None)[:1] + (torch.zeros(1), torch.zeros(1)), (run_oracle(d)[0], torch.zeros(1), torch.zeros(1)))

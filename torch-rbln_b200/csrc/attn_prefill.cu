@@ -84,6 +84,7 @@ struct AttnArgs {
   float scale;
   const float* scale_dev;
   uint32_t* err;
+  const int* work;  // optional: items (b * q_tiles + tile) in launch order, longest first
 };
 
 __device__ __forceinline__ float mask_value(const void* base, int dt, int64_t i) {
@@ -488,8 +489,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   warps 2-5    softmax, tile A       warps 6-9 softmax, tile B
 // Per KV tile j the MMA thread issues QK_A(j), QK_B(j), then PV_A(j-1),
 // PV_B(j-1). Shared memory: Q 2x32 KB, K/V 3x32 KB, P 2x16 KB (D = 128).
-// A quarter of the softmax exponentials are evaluated on the FMA pipe with a
-// polynomial (exp2_fma) so the SFU is not the bottleneck.
+// Half of the softmax exponentials are evaluated on the FMA pipe with a
+// polynomial (exp2_fma) so the SFU is not the bottleneck. CTAs take their
+// (sequence, query-tile) items longest-first from a list that
+// prefill_schedule_kernel sorts on the device by key count.
 // ---------------------------------------------------------------------------
 constexpr int BN2 = 64;          // keys per KV tile
 constexpr int kStages2 = 3;
@@ -551,9 +554,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
   auto bar = [&](int i) { return sbase + L::BAR + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // heaviest query tiles (latest positions, most keys under the causal mask) first
-  const int qtile = a.q_tiles - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
+  // 1-D grid over (item, KV head), items longest first: from the sorted list
+  // when there is one, else latest query tiles (most keys) first
+  const int item = (int)(blockIdx.x / a.Hkv), h = (int)(blockIdx.x % a.Hkv);
+  int b, qtile;
+  if (a.work) {
+    const int w = a.work[item];
+    b = w / a.q_tiles;
+    qtile = w - b * a.q_tiles;
+  } else {
+    b = item / a.q_tiles;
+    qtile = a.q_tiles - 1 - (item - b * a.q_tiles);
+  }
   const int s0 = qtile * 2 * a.QT;
   const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
   // keys for both tiles: the CTA spans 2*QT query tokens
@@ -784,7 +796,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       float lsum = 0.f;
 #pragma unroll
       for (int c = 0; c < BN2; ++c) {
-        const float e = ((c & 3) == 3) ? exp2_fma(xv[c] - mu) : exp2_approx(xv[c] - mu);
+        const float e = (c & 1) ? exp2_fma(xv[c] - mu) : exp2_approx(xv[c] - mu);
         xv[c] = e;
         lsum += e;
       }
@@ -888,6 +900,33 @@ __global__ void __launch_bounds__(kThreads2, 1)
   }
 }
 
+// Orders the (sequence, query-tile) items of a two-tile prefill launch by
+// the number of keys they attend, longest first (ties: lower index first),
+// so that the longest CTAs start in the first wave. One CTA; each thread
+// ranks items by counting the items that go before them.
+__global__ void __launch_bounds__(256) prefill_schedule_kernel(const int32_t* seq, int64_t seq_stride, int B,
+                                                               int q_tiles, int S_q, int tile_tokens, int span,
+                                                               int causal, int* work) {
+  extern __shared__ int cost[];
+  const int n = B * q_tiles;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int b = i / q_tiles, t = i - b * q_tiles;
+    const int off = max(0, seq[b * seq_stride]);
+    const int hi = min((t + 1) * tile_tokens, S_q);
+    cost[i] = min(span, causal ? off + hi : off + S_q);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int ci = cost[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const int cj = cost[j];
+      rank += (cj > ci) || (cj == ci && j < i);
+    }
+    work[rank] = i;
+  }
+}
+
 // Writes the chunk's new k/v rows into the paged cache at [seq[b], seq[b]+S_q).
 // One warp per token: lanes 0-15 copy the K row, lanes 16-31 the V row.
 template <int D>
@@ -982,8 +1021,9 @@ int launch_tc2(const TcLaunch& Lc, cudaStream_t st) {
   if (cudaFuncSetAttribute(attn_fwd_tc2_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SL::ALLOC) !=
       cudaSuccess)
     return RBLN_ERR_LAUNCH;
-  dim3 grid(Lc.a.q_tiles, Lc.a.Hkv, Lc.a.B);
-  attn_fwd_tc2_kernel<D, BF16><<<grid, kThreads2, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
+  const long long n = (long long)Lc.a.q_tiles * Lc.a.B * Lc.a.Hkv;
+  if (n > 2147483647LL) return RBLN_ERR_UNSUPPORTED;
+  attn_fwd_tc2_kernel<D, BF16><<<(unsigned)n, kThreads2, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -1027,6 +1067,16 @@ bool map_kv(CUtensorMap* m, const void* c, int dt, int NB, int Hkv, int rows, in
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Items ranked by prefill_schedule_kernel (its shared memory holds one int each).
+constexpr int kMaxScheduledItems = 8192;
+
+int prefill_ws_bytes(const rbln_paged_attn_params_t* p) {
+  if (!p || p->group <= 0 || p->group > BM || p->batch <= 0 || p->q_len <= 0) return 0;
+  const int QT = BM / p->group;
+  const long long n = (long long)p->batch * ((p->q_len + 2 * QT - 1) / (2 * QT));
+  return n <= kMaxScheduledItems ? (int)(n * sizeof(int)) : 0;
+}
 
 int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_mask_op) {
   if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 || p->max_blocks <= 0 ||
@@ -1134,6 +1184,15 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.scale = p->scale;
   a.scale_dev = p->scale_dev;
   a.err = p->error_flags;
+  if (two_tile && p->workspace) {
+    const int n = p->batch * a.q_tiles;
+    if (n <= kMaxScheduledItems && p->workspace_bytes >= (size_t)n * sizeof(int)) {
+      prefill_schedule_kernel<<<1, 256, n * sizeof(int), st>>>(p->seq, p->seq_stride, p->batch, a.q_tiles, p->q_len,
+                                                               2 * QT, (int)span64, p->causal, (int*)p->workspace);
+      if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
+      a.work = static_cast<const int*>(p->workspace);
+    }
+  }
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
   const int rc = two_tile ? launch_tc2_any(Lc, st) : launch_tc_any(Lc, st);
   if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
@@ -1211,6 +1270,12 @@ int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os
 }  // namespace rbln
 
 extern "C" {
+
+int rbln_paged_prefill_workspace_size(const rbln_paged_attn_params_t* p, size_t* bytes) {
+  if (!p || !bytes) return RBLN_ERR_INVALID_ARGUMENT;
+  *bytes = (size_t)rbln::prefill_ws_bytes(p);
+  return RBLN_OK;
+}
 
 int rbln_paged_causal_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
   return rbln::run_prefill(p, stream, /*keep_mask_op=*/false);

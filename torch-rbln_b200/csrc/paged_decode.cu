@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -119,8 +120,9 @@ __device__ __forceinline__ int v_dim(int gid, int e) {
   return gid * C::VSEG + (e / C::VSEG) * 64 + (e % C::VSEG);
 }
 
-template <int D, int KV, bool Q_BF16, int NT>
-__global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_split_kernel(const DecodeArgs a) {
+template <int D, int KV, bool Q_BF16, int NT, int TPI>
+__global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1 && KV == KV_FP8) ? 3 : 2)
+    paged_decode_split_kernel(const DecodeArgs a) {
   using C = Cfg<D, KV>;
   constexpr bool MB = C::MMA_BF16;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -241,15 +243,24 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
 
   const char* kc = a.kcache;
   const char* vc = a.vcache;
-  const int tv0 = 2 * tig, tv1 = 2 * tig + 1, tv2 = 2 * tig + 8, tv3 = 2 * tig + 9;
+  const int tv[4] = {2 * tig, 2 * tig + 1, 2 * tig + 8, 2 * tig + 9};
 
-  for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile) {
-    // per-token row offsets: lane l (mod 16) resolves token ts + l
+  // One 16-token tile in flight: lane l (mod 16) resolves token ts + l
+  // through the block table; the row offsets reach the lanes that load them
+  // by shuffles; then the K rows gid / gid+8 and the V rows tv[] are loaded.
+  struct Tile {
+    uint4 kraw[2][C::KCH];
+    uint32_t vraw[4][C::NVW];
+    uint32_t vmask;
+    float ksc, vsc;
+  };
+  auto fetch = [&](int ts, Tile& T) {
     const int tpos = ts + (lane & 15);
     bool valid = tpos < t1;
     if (valid && a.mask) valid = load_keep(a.mask, a.mask_dtype, b * a.mask_stride + tpos);
     uint32_t off16 = 0;  // row byte offset / 16
-    float ksc = 1.f, vsc = 1.f;
+    T.ksc = 1.f;
+    T.vsc = 1.f;
     if (valid) {
       const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + tpos / a.bs);
       if (blk < 0 || blk >= a.num_blocks) {
@@ -258,49 +269,43 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
       } else {
         off16 = (uint32_t)(((blk * a.cs_block + h * a.cs_head + (tpos % a.bs) * a.cs_tok) * C::SZ) >> 4);
         if constexpr (KV == KV_FP8) {
-          ksc = a.k_scale[blk * a.ss_block + h * a.ss_head];
-          vsc = a.v_scale[blk * a.ss_block + h * a.ss_head];
+          T.ksc = a.k_scale[blk * a.ss_block + h * a.ss_head];
+          T.vsc = a.v_scale[blk * a.ss_block + h * a.ss_head];
         }
       }
     }
-    const uint32_t vmask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
-    if (vmask == 0) continue;
-
+    T.vmask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
+    if (T.vmask == 0) return;
     const uint32_t ok0 = __shfl_sync(0xffffffffu, off16, gid);
     const uint32_t ok1 = __shfl_sync(0xffffffffu, off16, gid + 8);
-    const bool vk0 = (vmask >> gid) & 1, vk1 = (vmask >> (gid + 8)) & 1;
-    uint32_t ov[4];
-    bool vv[4];
-    ov[0] = __shfl_sync(0xffffffffu, off16, tv0); vv[0] = (vmask >> tv0) & 1;
-    ov[1] = __shfl_sync(0xffffffffu, off16, tv1); vv[1] = (vmask >> tv1) & 1;
-    ov[2] = __shfl_sync(0xffffffffu, off16, tv2); vv[2] = (vmask >> tv2) & 1;
-    ov[3] = __shfl_sync(0xffffffffu, off16, tv3); vv[3] = (vmask >> tv3) & 1;
-
-    // K rows gid and gid+8, chunks 4i+tig
-    uint4 kraw[2][C::KCH];
+    const bool vk0 = (T.vmask >> gid) & 1, vk1 = (T.vmask >> (gid + 8)) & 1;
 #pragma unroll
     for (int i = 0; i < C::KCH; ++i) {
-      kraw[0][i] = vk0 ? ld_stream_v4(kc + (size_t)ok0 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
-      kraw[1][i] = vk1 ? ld_stream_v4(kc + (size_t)ok1 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
+      T.kraw[0][i] = vk0 ? ld_stream_v4(kc + (size_t)ok0 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
+      T.kraw[1][i] = vk1 ? ld_stream_v4(kc + (size_t)ok1 * 16 + (4 * i + tig) * 16) : make_uint4(0, 0, 0, 0);
     }
-    // V rows tv0..tv3, this lane's d segments
-    uint32_t vraw[4][C::NVW];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const char* rowp = vc + (size_t)ov[j] * 16;
+      const uint32_t ov = __shfl_sync(0xffffffffu, off16, tv[j]);
+      const bool vv = (T.vmask >> tv[j]) & 1;
+      const char* rowp = vc + (size_t)ov * 16;
       if constexpr (C::NVW >= 4) {
 #pragma unroll
         for (int sg = 0; sg < C::NVW / 4; ++sg) {
-          uint4 x = vv[j] ? ld_stream_v4(rowp + (gid * C::VSEG + sg * 64) * C::SZ) : make_uint4(0, 0, 0, 0);
-          vraw[j][4 * sg + 0] = x.x; vraw[j][4 * sg + 1] = x.y;
-          vraw[j][4 * sg + 2] = x.z; vraw[j][4 * sg + 3] = x.w;
+          uint4 x = vv ? ld_stream_v4(rowp + (gid * C::VSEG + sg * 64) * C::SZ) : make_uint4(0, 0, 0, 0);
+          T.vraw[j][4 * sg + 0] = x.x; T.vraw[j][4 * sg + 1] = x.y;
+          T.vraw[j][4 * sg + 2] = x.z; T.vraw[j][4 * sg + 3] = x.w;
         }
       } else {
-        uint2 x = vv[j] ? ld_stream_v2(rowp + gid * C::VSEG * C::SZ) : make_uint2(0, 0);
-        vraw[j][0] = x.x; vraw[j][1] = x.y;
+        uint2 x = vv ? ld_stream_v2(rowp + gid * C::VSEG * C::SZ) : make_uint2(0, 0);
+        T.vraw[j][0] = x.x; T.vraw[j][1] = x.y;
       }
     }
+  };
 
+  auto consume = [&](const Tile& T) {
+    if (T.vmask == 0) return;  // warp-uniform (ballot)
+    const bool vk0 = (T.vmask >> gid) & 1, vk1 = (T.vmask >> (gid + 8)) & 1;
     // S^T = K . Q^T
     float s[NT][4];
 #pragma unroll
@@ -309,8 +314,8 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const int i = kk >> 1, sgl = (kk & 1) * 2;
-        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&kraw[0][i]);
-        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&kraw[1][i]);
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&T.kraw[0][i]);
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&T.kraw[1][i]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
           mma16816<MB>(s[nt], r0[sgl], r1[sgl], r0[sgl + 1], r1[sgl + 1], qf[nt][2 * kk], qf[nt][2 * kk + 1]);
@@ -318,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
     } else {
 #pragma unroll
       for (int i = 0; i < C::KCH; ++i) {
-        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&kraw[0][i]);
-        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&kraw[1][i]);
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&T.kraw[0][i]);
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&T.kraw[1][i]);
 #pragma unroll
         for (int w = 0; w < 4; ++w) {  // kk = 4i + w uses chunk word w (4 fp8)
           const uint32_t a0 = e4m3x2_to_f16x2(r0[w] & 0xffffu), a2 = e4m3x2_to_f16x2(r0[w] >> 16);
@@ -336,10 +341,10 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
     float k0m = qk_mult, k1m = qk_mult;
     float vs0 = 1.f, vs1 = 1.f;
     if constexpr (KV == KV_FP8) {
-      k0m *= __shfl_sync(0xffffffffu, ksc, gid);
-      k1m *= __shfl_sync(0xffffffffu, ksc, gid + 8);
-      vs0 = __shfl_sync(0xffffffffu, vsc, gid);
-      vs1 = __shfl_sync(0xffffffffu, vsc, gid + 8);
+      k0m *= __shfl_sync(0xffffffffu, T.ksc, gid);
+      k1m *= __shfl_sync(0xffffffffu, T.ksc, gid + 8);
+      vs0 = __shfl_sync(0xffffffffu, T.vsc, gid);
+      vs1 = __shfl_sync(0xffffffffu, T.vsc, gid + 8);
     }
     uint32_t pb0[NT], pb1[NT];
 #pragma unroll
@@ -374,15 +379,15 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
     for (int mt = 0; mt < C::MT; ++mt) {
       uint32_t a0, a1, a2, a3;
       if constexpr (KV != KV_FP8) {
-        a0 = prmt(vraw[0][mt], vraw[1][mt], 0x5410);
-        a1 = prmt(vraw[0][mt], vraw[1][mt], 0x7632);
-        a2 = prmt(vraw[2][mt], vraw[3][mt], 0x5410);
-        a3 = prmt(vraw[2][mt], vraw[3][mt], 0x7632);
+        a0 = prmt(T.vraw[0][mt], T.vraw[1][mt], 0x5410);
+        a1 = prmt(T.vraw[0][mt], T.vraw[1][mt], 0x7632);
+        a2 = prmt(T.vraw[2][mt], T.vraw[3][mt], 0x5410);
+        a3 = prmt(T.vraw[2][mt], T.vraw[3][mt], 0x7632);
       } else {
         const int w = mt >> 1;
         const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
-        const uint32_t x = prmt(vraw[0][w], vraw[1][w], sel);
-        const uint32_t y = prmt(vraw[2][w], vraw[3][w], sel);
+        const uint32_t x = prmt(T.vraw[0][w], T.vraw[1][w], sel);
+        const uint32_t y = prmt(T.vraw[2][w], T.vraw[3][w], sel);
         a0 = e4m3x2_to_f16x2(x & 0xffffu);
         a1 = e4m3x2_to_f16x2(x >> 16);
         a2 = e4m3x2_to_f16x2(y & 0xffffu);
@@ -391,6 +396,16 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 ? 4 : 2)) paged_decode_spli
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma16816<MB>(o_acc[nt][mt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
     }
+  };
+
+  // TPI tiles of this warp in flight per iteration: all of their block-table
+  // lookups and loads are issued before the first one is consumed.
+  for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile * TPI) {
+    Tile T[TPI];
+#pragma unroll
+    for (int u = 0; u < TPI; ++u) fetch(ts + u * kWarps * kTile, T[u]);
+#pragma unroll
+    for (int u = 0; u < TPI; ++u) consume(T[u]);
   }
 
   // ---- combine the 4 warps of this CTA ------------------------------------
@@ -506,6 +521,11 @@ int dtype_bytes(int dt) {
 }
 
 int choose_chunk(const rbln_paged_attn_params_t* p, int span) {
+  static const int env_chunk = [] {
+    const char* e = std::getenv("RBLN_ATTN_DECODE_CHUNK");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (p->num_splits <= 0 && env_chunk >= 64) return std::min(std::max(64, env_chunk / 64 * 64), std::max(span, 64));
   if (p->num_splits > 0) {
     int c = (span + p->num_splits - 1) / p->num_splits;
     return std::max(64, (c + 63) / 64 * 64);
@@ -545,11 +565,26 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   return RBLN_OK;
 }
 
+// Tiles each warp keeps in flight: two for fp8 caches (so a warp has as many
+// bytes in flight as with a 16-bit cache), one otherwise; RBLN_ATTN_DECODE_TPI
+// overrides it (1 or 2).
+int decode_tpi(int kv_kind) {
+  static const int env = [] {
+    const char* e = std::getenv("RBLN_ATTN_DECODE_TPI");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (env == 1 || env == 2) return env;
+  return kv_kind == KV_FP8 ? 2 : 1;
+}
+
 template <int D, int KV, bool QB, int NT>
 int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
   dim3 grid(pl.max_splits, a.Hkv, a.B);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
-  paged_decode_split_kernel<D, KV, QB, NT><<<grid, kThreads, 0, st>>>(a);
+  if (decode_tpi(KV) == 2)
+    paged_decode_split_kernel<D, KV, QB, NT, 2><<<grid, kThreads, 0, st>>>(a);
+  else
+    paged_decode_split_kernel<D, KV, QB, NT, 1><<<grid, kThreads, 0, st>>>(a);
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
     const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);

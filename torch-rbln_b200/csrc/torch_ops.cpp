@@ -263,6 +263,14 @@ at::Tensor paged_causal_attn_decode_kvfp8_cuda(const at::Tensor& q, const at::Te
 
 at::Tensor run_prefill(Common& c, const char* op, bool keep_mask) {
   c10::cuda::CUDAGuard guard(c.q.device());
+  size_t ws = 0;
+  check_rc(rbln_paged_prefill_workspace_size(&c.p, &ws), op);
+  at::Tensor wst;
+  if (ws > 0) {
+    wst = at::empty({(int64_t)ws}, c.q.options().dtype(at::kByte));
+    c.p.workspace = wst.data_ptr();
+    c.p.workspace_bytes = ws;
+  }
   auto stream = at::cuda::getCurrentCUDAStream(c.q.device().index());
   const int rc = keep_mask ? rbln_paged_attn_prefill(&c.p, stream.stream())
                            : rbln_paged_causal_attn_prefill(&c.p, stream.stream());

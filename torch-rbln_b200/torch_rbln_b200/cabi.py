@@ -87,6 +87,8 @@ ENTRY_POINTS = {
                                                         ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_paged_causal_attn_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
+    "rbln_paged_prefill_workspace_size": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams),
+                                                         ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_paged_causal_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_sdpa_fwd": (ctypes.c_int, [ctypes.POINTER(SdpaParams), c_vp]),
@@ -166,9 +168,10 @@ def paged_params(q, k_new, v_new, kcache, vcache, seq, block_table, block_size, 
     return p, {"out": out}
 
 
-def attach_workspace(p: PagedAttnParams, device, keep: dict) -> None:
+def attach_workspace(p: PagedAttnParams, device, keep: dict, prefill: bool = False) -> None:
     n = ctypes.c_size_t(0)
-    rc = lib().rbln_paged_decode_workspace_size(ctypes.byref(p), ctypes.byref(n))
+    query = lib().rbln_paged_prefill_workspace_size if prefill else lib().rbln_paged_decode_workspace_size
+    rc = query(ctypes.byref(p), ctypes.byref(n))
     if rc != OK:
         raise RuntimeError(f"rbln_paged_decode_workspace_size failed: {rc}")
     if n.value:

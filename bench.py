@@ -61,6 +61,9 @@ WORKLOADS = {
     "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
                          B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False),
     # long context, KV heads sharded over the ranks + one NCCL all-gather of head outputs
+    # profiling case for the fp8 path (~0.6 GB of fp8 KV on the device)
+    "decode_fp8_small": dict(desc="paged decode fp8-e4m3 KV B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
+                             B=64, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
     "decode_long": dict(desc="paged decode bf16 B=32 Hq=64 Hkv=8 D=128 bs=16 L=32768 pool=65536",
                         B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False,
                         shard="heads"),

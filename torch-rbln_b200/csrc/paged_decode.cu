@@ -463,6 +463,9 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1
 // Combines the per-split partials of one (sequence, KV head).
 template <int D, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
+  // launched as a programmatic dependent of the split kernel: wait here until
+  // that grid has completed and its writes are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int pos, L, nsplit;
@@ -530,12 +533,13 @@ int choose_chunk(const rbln_paged_attn_params_t* p, int span) {
     int c = (span + p->num_splits - 1) / p->num_splits;
     return std::max(64, (c + 63) / 64 * 64);
   }
-  // Aim at roughly 16 CTAs per SM over the whole launch (the span is an
-  // upper bound of the real context), never below 256 tokens per split.
-  const int64_t target_ctas = 148LL * 16;
+  // About 24 CTAs per SM if every sequence used the whole span, with splits
+  // of 256..2048 tokens: short splits pay the per-CTA start-up and the merge,
+  // long ones leave a tail of unequal CTAs (measured on B200 over 256..8192).
+  const int64_t target_ctas = 148LL * 24;
   int64_t c = ((int64_t)span * p->batch * p->num_kv_heads + target_ctas - 1) / target_ctas;
   c = (c + 63) / 64 * 64;
-  c = std::max<int64_t>(c, 256);
+  c = std::min<int64_t>(std::max<int64_t>(c, 256), 2048);
   c = std::min<int64_t>(c, std::max(span, 64));
   return (int)((c + 63) / 64 * 64);
 }
@@ -592,7 +596,19 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
         cudaFuncSetAttribute(paged_decode_merge_kernel<D, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return RBLN_ERR_LAUNCH;
-    paged_decode_merge_kernel<D, QB><<<dim3(a.Hkv, a.B), kThreads, smem, st>>>(a);
+    // programmatic dependent launch: the merge grid is set up while the split
+    // kernel drains, and waits in-kernel (griddepcontrol.wait) for its completion
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.Hkv, a.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, paged_decode_merge_kernel<D, QB>, a) != cudaSuccess) return RBLN_ERR_LAUNCH;
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }

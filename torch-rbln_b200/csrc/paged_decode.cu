@@ -569,16 +569,15 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   return RBLN_OK;
 }
 
-// Tiles each warp keeps in flight: two for fp8 caches (so a warp has as many
-// bytes in flight as with a 16-bit cache), one otherwise; RBLN_ATTN_DECODE_TPI
-// overrides it (1 or 2).
-int decode_tpi(int kv_kind) {
+// Tiles each warp keeps in flight. One: on B200 two tiles per warp (more
+// registers, fewer resident warps) measured slower for both bf16 and fp8
+// caches. RBLN_ATTN_DECODE_TPI=2 selects the two-tile variant.
+int decode_tpi(int) {
   static const int env = [] {
     const char* e = std::getenv("RBLN_ATTN_DECODE_TPI");
     return e ? std::atoi(e) : 0;
   }();
-  if (env == 1 || env == 2) return env;
-  return kv_kind == KV_FP8 ? 2 : 1;
+  return env == 2 ? 2 : 1;
 }
 
 template <int D, int KV, bool QB, int NT>

@@ -266,3 +266,38 @@ def test_decode_error_contract():
         torch.ops.rbln_custom_ops.paged_causal_attn_decode(x["q"][..., :96].contiguous(), x["k"][..., :96].contiguous(),
                                                            x["v"][..., :96].contiguous(), bad, bad.clone(), x["seq"],
                                                            x["scale"], x["block_table"], 16)
+
+
+# --- balanced chunks (the default schedule) ----------------------------------
+def test_decode_balanced_chunks_span_many_sequences():
+    """Many short sequences: one chunk of the balanced schedule covers the end
+    of one sequence and several whole ones (one partial or one final output
+    per sequence it touches)."""
+    g = torch.Generator().manual_seed(21)
+    lens = torch.randint(1, 60, (300,), generator=g).tolist()
+    d = make_decode(300, 2, 4, 128, 16, lens, seed=21)
+    check(run_op(d), oracle(d))
+
+
+@pytest.mark.parametrize("G", [4, 16])
+def test_decode_balanced_one_long_sequence(G):
+    """One sequence spread over many chunks, next to short ones."""
+    d = make_decode(3, 2, G, 128, 16, [20000, 5, 300], seed=22)
+    check(run_op(d), oracle(d))
+
+
+def test_decode_negative_seq_sets_flag():
+    """seq[b] < 0: no visible position and nothing appended for that sequence,
+    its output is NaN and the device error word has DEVERR_SEQ_RANGE; the
+    other sequences are unaffected."""
+    d = make_decode(3, 2, 4, 128, 16, [100, 50, 700], seed=23)
+    d["seq"][1, 0] = -1
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    got = run_cabi(d, err=err)
+    assert int(err.item()) & cabi().DEVERR_SEQ_RANGE
+    assert torch.isnan(got[0][1].float()).all()
+    keep = torch.tensor([0, 2])
+    sub = dict(d, q=d["q"][keep], k=d["k"][keep], v=d["v"][keep], seq=d["seq"][keep],
+               block_table=d["block_table"][keep])
+    ref = oracle(sub)
+    check((got[0][keep], got[1], got[2]), ref)

@@ -25,13 +25,24 @@
 //  * fp8-e4m3 caches are converted exactly to f16 in registers
 //    (cvt.rn.f16x2.e4m3x2); the per-(block, head) K scale multiplies the
 //    scores and the V scale is folded into P before the PV product.
-//  * Splits write (O/l, log2-sum-exp) partials; a merge kernel combines them.
-//    A sequence that needs one split is written directly by its CTA.
+//  * Work is cut into equal chunks across the whole batch ("balanced"
+//    split-K): the sequences' lengths, each rounded up to 16, are laid end to
+//    end and CTA (c, h) takes tokens [c*W, (c+1)*W) of KV head h, whatever
+//    sequences they belong to. Each CTA computes that prefix itself from seq,
+//    so no host synchronisation is needed. One wave of CTAs (4 per SM) with
+//    equal work leaves no tail of long sequences.
+//  * A CTA writes one (O/l, log2-sum-exp) partial per sequence it touches; a
+//    merge kernel (launched as a programmatic dependent) combines them. A
+//    sequence held by one CTA is written directly by it.
+//  * A caller that fixes num_splits (or RBLN_ATTN_DECODE_SCHED=seq) gets the
+//    per-sequence grid (splits, Hkv, B) with a.chunk tokens per split.
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -78,8 +89,12 @@ struct DecodeArgs {
   int B, Hkv, G, num_blocks, bs, span;
   int chunk;
   int max_splits;
-  float* part_o;    // [B][Hkv][max_splits][G][D]
-  float* part_lse;  // [B][Hkv][max_splits][G]  (log2 domain)
+  int nchunk;       // balanced split: chunks per KV head (grid.x)
+  int min_w;        // balanced split: smallest chunk, in tokens
+  int* prefix;      // balanced split: [B + 1] padded-length prefix, then W
+  // per-sequence split: [B][Hkv][max_splits][G]; balanced: [Hkv][nchunk + B][G]
+  float* part_o;    // (.., D) floats per slot
+  float* part_lse;  // log2-sum-exp per slot
   uint32_t* err;
 };
 
@@ -120,55 +135,62 @@ __device__ __forceinline__ int v_dim(int gid, int e) {
   return gid * C::VSEG + (e / C::VSEG) * 64 + (e % C::VSEG);
 }
 
-template <int D, int KV, bool Q_BF16, int NT, int TPI>
-__global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1 && KV == KV_FP8) ? 3 : 2)
-    paged_decode_split_kernel(const DecodeArgs a) {
+// Writes the new token's k/v (bf16/f16 copy, or fp8 quantised with the
+// block's scale) at position `pos` of sequence b, KV head h. Threads 0..63
+// take K and 64..127 take V, 8 elements each. No barrier inside.
+template <int D, int KV, bool Q_BF16>
+__device__ __forceinline__ void append_token(const DecodeArgs& a, int b, int h, int pos) {
+  using C = Cfg<D, KV>;
+  const int tid = threadIdx.x;
+  const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + pos / a.bs);
+  if (blk < 0 || blk >= a.num_blocks) {
+    if (tid == 0) flag_error(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+  } else {
+    const int64_t row = (blk * a.cs_block + h * a.cs_head + (pos % a.bs) * a.cs_tok) * C::SZ;
+    const int part = tid >> 6;  // 0: K, 1: V
+    const int j = tid & 63;     // 8 elements per thread
+    if (j < D / 8) {
+      const char* src = (part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h
+                                   : a.v_new + b * a.vn_b + h * a.vn_h) + j * 16;
+      char* dst = (part == 0 ? a.kcache : a.vcache) + row;
+      const uint4 x = *reinterpret_cast<const uint4*>(src);
+      if constexpr (KV != KV_FP8) {
+        *reinterpret_cast<uint4*>(dst + j * 16) = x;
+      } else {
+        const float sc = (part == 0 ? a.k_scale : a.v_scale)[blk * a.ss_block + h * a.ss_head];
+        const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+        uint32_t o[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          float f[4];
+          float2 lo = unpack2<Q_BF16>(w[2 * k]), hi = unpack2<Q_BF16>(w[2 * k + 1]);
+          f[0] = lo.x / sc; f[1] = lo.y / sc; f[2] = hi.x / sc; f[3] = hi.y / sc;
+          __nv_fp8x2_storage_t p01 = __nv_cvt_float2_to_fp8x2(make_float2(f[0], f[1]), __NV_SATFINITE, __NV_E4M3);
+          __nv_fp8x2_storage_t p23 = __nv_cvt_float2_to_fp8x2(make_float2(f[2], f[3]), __NV_SATFINITE, __NV_E4M3);
+          o[k] = uint32_t(p01) | (uint32_t(p23) << 16);
+        }
+        *reinterpret_cast<uint2*>(dst + j * 8) = make_uint2(o[0], o[1]);
+      }
+    }
+  }
+}
+
+// Attention of the G query heads of KV head h of sequence b over the
+// context tokens [t0, t1): the CTA's 4 warps take 16-token tiles round-robin;
+// their (max, sum, O) are combined in shared memory and written as the final
+// output (whole = the CTA saw every token of the sequence) or as the
+// (O/l, log2-sum-exp) partial at part_o/part_lse index slot + g.
+template <int D, int KV, bool Q_BF16, int NT>
+__device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned char* dsm, int b, int h, int t0,
+                                               int t1, bool append, bool whole, int64_t slot) {
   using C = Cfg<D, KV>;
   constexpr bool MB = C::MMA_BF16;
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
 
-  int pos, L, nsplit;
-  decode_extent(a, b, pos, L, nsplit);
-  if (split >= nsplit) return;
-  if (pos < 0 && tid == 0 && split == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
-  const int t0 = split * a.chunk;
-  const int t1 = min(t0 + a.chunk, L);
-
   // ---- append the new token (write-then-read, like the reference) --------
-  if (a.k_new != nullptr && pos >= 0 && pos < a.span && min(pos / a.chunk, nsplit - 1) == split) {
-    const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + pos / a.bs);
-    if (blk < 0 || blk >= a.num_blocks) {
-      if (tid == 0) flag_error(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
-    } else {
-      const int64_t row = (blk * a.cs_block + h * a.cs_head + (pos % a.bs) * a.cs_tok) * C::SZ;
-      const int part = tid >> 6;  // 0: K, 1: V
-      const int j = tid & 63;     // 8 elements per thread
-      if (j < D / 8) {
-        const char* src = (part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h
-                                     : a.v_new + b * a.vn_b + h * a.vn_h) + j * 16;
-        char* dst = (part == 0 ? a.kcache : a.vcache) + row;
-        const uint4 x = *reinterpret_cast<const uint4*>(src);
-        if constexpr (KV != KV_FP8) {
-          *reinterpret_cast<uint4*>(dst + j * 16) = x;
-        } else {
-          const float sc = (part == 0 ? a.k_scale : a.v_scale)[blk * a.ss_block + h * a.ss_head];
-          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-          uint32_t o[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            float f[4];
-            float2 lo = unpack2<Q_BF16>(w[2 * k]), hi = unpack2<Q_BF16>(w[2 * k + 1]);
-            f[0] = lo.x / sc; f[1] = lo.y / sc; f[2] = hi.x / sc; f[3] = hi.y / sc;
-            __nv_fp8x2_storage_t p01 = __nv_cvt_float2_to_fp8x2(make_float2(f[0], f[1]), __NV_SATFINITE, __NV_E4M3);
-            __nv_fp8x2_storage_t p23 = __nv_cvt_float2_to_fp8x2(make_float2(f[2], f[3]), __NV_SATFINITE, __NV_E4M3);
-            o[k] = uint32_t(p01) | (uint32_t(p23) << 16);
-          }
-          *reinterpret_cast<uint2*>(dst + j * 8) = make_uint2(o[0], o[1]);
-        }
-      }
-    }
+  if (append && a.k_new != nullptr) {
+    append_token<D, KV, Q_BF16>(a, b, h, a.seq[b * a.seq_stride]);
     __syncthreads();
   }
 
@@ -398,20 +420,17 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1
     }
   };
 
-  // TPI tiles of this warp in flight per iteration: all of their block-table
-  // lookups and loads are issued before the first one is consumed.
-  for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile * TPI) {
-    Tile T[TPI];
-#pragma unroll
-    for (int u = 0; u < TPI; ++u) fetch(ts + u * kWarps * kTile, T[u]);
-#pragma unroll
-    for (int u = 0; u < TPI; ++u) consume(T[u]);
+  for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile) {
+    Tile T;
+    fetch(ts, T);
+    consume(T);
   }
 
   // ---- combine the 4 warps of this CTA ------------------------------------
   constexpr int GP = 8 * NT;
-  __shared__ float sO[kWarps][GP][D];
-  __shared__ float sM[kWarps][GP], sL[kWarps][GP];
+  auto sO = reinterpret_cast<float(*)[GP][D]>(dsm);
+  auto sM = reinterpret_cast<float(*)[GP]>(dsm + kWarps * GP * D * 4);
+  auto sL = reinterpret_cast<float(*)[GP]>(dsm + kWarps * GP * D * 4 + kWarps * GP * 4);
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const float l0 = warp_sum_xor_rows(l_run[nt][0]);
@@ -432,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1
   }
   __syncthreads();
 
-  const bool final_out = (nsplit == 1);
+  const bool final_out = whole;
   for (int idx = tid; idx < a.G * (D / 4); idx += kThreads) {
     const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
     float M = neg_inf();
@@ -453,27 +472,125 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && TPI == 1) ? 4 : (NT == 1
       char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
       *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
     } else {
-      const int64_t slot = ((int64_t)(b * a.Hkv + h) * a.max_splits + split) * a.G + g;
-      *reinterpret_cast<float4*>(a.part_o + slot * D + d4) = acc;
-      if (d4 == 0) a.part_lse[slot] = (M == neg_inf()) ? neg_inf() : M + __log2f(Lsum);
+      const int64_t ps = slot + g;
+      *reinterpret_cast<float4*>(a.part_o + ps * D + d4) = acc;
+      if (d4 == 0) a.part_lse[ps] = (M == neg_inf()) ? neg_inf() : M + __log2f(Lsum);
     }
+  }
+  __syncthreads();  // the combine area is reused by the CTA's next segment
+}
+
+// Bytes of the CTA combine area: per-warp O [kWarps][8*NT][D] and max/sum.
+template <int D, int NT>
+__host__ __device__ constexpr int combine_bytes() {
+  return (kWarps * 8 * NT * D + 2 * kWarps * 8 * NT) * 4;
+}
+
+// Context length seen by sequence b (see decode_extent).
+__device__ __forceinline__ int seq_len(const DecodeArgs& a, int b, int& pos) {
+  pos = a.seq[b * a.seq_stride];
+  return a.mask ? min(a.span, a.mask_len) : (pos < 0 ? 0 : min(pos + 1, a.span));
+}
+
+// One CTA per (context split, KV head, sequence): each sequence is cut into
+// splits of a.chunk tokens.
+template <int D, int KV, bool Q_BF16, int NT>
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_split_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  int pos, L, nsplit;
+  decode_extent(a, b, pos, L, nsplit);
+  if (split >= nsplit) return;
+  if (pos < 0 && threadIdx.x == 0 && split == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
+  const int t0 = split * a.chunk;
+  const int t1 = min(t0 + a.chunk, L);
+  const bool append = pos >= 0 && pos < a.span && min(pos / a.chunk, nsplit - 1) == split;
+  decode_segment<D, KV, Q_BF16, NT>(a, dsm, b, h, t0, t1, append, nsplit == 1,
+                                    ((int64_t)(b * a.Hkv + h) * a.max_splits + split) * a.G);
+}
+
+// Exclusive prefix P[0..B] of the sequences' lengths rounded up to 16, in
+// shared memory, and the balanced chunk size W (a multiple of 16). CTA (0, 0)
+// also stores P and W in the workspace for the merge kernel.
+__device__ __forceinline__ int balanced_prefix(const DecodeArgs& a, int* P) {
+  __shared__ int wsum[kWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (a.B + kThreads - 1) / kThreads;
+  const int first = tid * per;
+  int sum = 0, pos;
+  for (int i = 0; i < per; ++i)
+    if (first + i < a.B) sum += (seq_len(a, first + i, pos) + 15) & ~15;
+  int x = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int off = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) off += w < warp ? wsum[w] : 0;
+  int run = off + x - sum;
+  for (int i = 0; i < per; ++i)
+    if (first + i < a.B) {
+      P[first + i] = run;
+      run += (seq_len(a, first + i, pos) + 15) & ~15;
+    }
+  if (tid == kThreads - 1) P[a.B] = off + x;
+  __syncthreads();
+  const int T = P[a.B];
+  const int W = max(a.min_w, ((T + a.nchunk - 1) / a.nchunk + 15) & ~15);
+  if (blockIdx.x == 0 && blockIdx.y == 0) {
+    for (int i = tid; i <= a.B; i += kThreads) a.prefix[i] = P[i];
+    if (tid == 0) a.prefix[a.B + 1] = W;
+  }
+  return W;
+}
+
+// Balanced split: the batch's tokens, each sequence padded to a multiple of
+// 16, are cut into equal chunks of W tokens, so every CTA has the same work
+// however unequal the sequences are. CTA (c, h) takes chunk c of KV head h,
+// which may cover the end of one sequence and the start of the next ones: one
+// segment (and one partial, at slot c + b of head h) per sequence touched.
+template <int D, int KV, bool Q_BF16, int NT>
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanced_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  int* P = reinterpret_cast<int*>(dsm + combine_bytes<D, NT>());
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int W = balanced_prefix(a, P);
+  const int T = P[a.B];
+  int lo = c * W;
+  if (lo >= T) return;
+  const int hi = min(lo + W, T);
+  // last sequence whose padded range starts at or before lo (it is non-empty)
+  int bl = 0, bh = a.B - 1;
+  while (bl < bh) {
+    const int mid = (bl + bh + 1) >> 1;
+    if (P[mid] <= lo) bl = mid; else bh = mid - 1;
+  }
+  for (int b = bl; b < a.B && lo < hi; ++b) {
+    const int pb = P[b], pe = P[b + 1];
+    if (pe <= lo) continue;
+    const int seg_hi = min(hi, pe);
+    int pos;
+    const int L = seq_len(a, b, pos);
+    const int t0 = lo - pb, t1 = min(seg_hi - pb, L);
+    const int ap = min(pos, L - 1);
+    const bool append = pos >= 0 && pos < a.span && ap >= t0 && ap < t1;
+    decode_segment<D, KV, Q_BF16, NT>(a, dsm, b, h, t0, t1, append, lo == pb && seg_hi == pe,
+                                      ((int64_t)h * (a.nchunk + a.B) + c + b) * a.G);
+    lo = seg_hi;
   }
 }
 
-// Combines the per-split partials of one (sequence, KV head).
+// Weighted sum of `nsplit` partials (index (base + s) * G + g) of sequence b,
+// KV head h into the output. `sw` holds nsplit*G + G floats.
 template <int D, bool Q_BF16>
-__global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
-  // launched as a programmatic dependent of the split kernel: wait here until
-  // that grid has completed and its writes are visible
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int h = blockIdx.x, b = blockIdx.y;
+__device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h, int64_t base, int nsplit,
+                                               float* sw) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int pos, L, nsplit;
-  decode_extent(a, b, pos, L, nsplit);
-  if (nsplit <= 1) return;
-  extern __shared__ float sw[];  // [nsplit][G] weights, then [G] flags
-  float* s_lse = sw + nsplit * a.G;
-  const int64_t base = (int64_t)(b * a.Hkv + h) * a.max_splits;
+  float* s_inv = sw + nsplit * a.G;
   for (int g = warp; g < a.G; g += kWarps) {
     float M = neg_inf();
     for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, a.part_lse[(base + s) * a.G + g]);
@@ -488,7 +605,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const Deco
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    if (lane == 0) s_lse[g] = (M == neg_inf()) ? 0.f : 1.f / S;
+    if (lane == 0) s_inv[g] = (M == neg_inf()) ? 0.f : 1.f / S;
   }
   __syncthreads();
   for (int idx = tid; idx < a.G * (D / 4); idx += kThreads) {
@@ -501,12 +618,54 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const Deco
         acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
       }
     }
-    float inv = s_lse[g];
+    float inv = s_inv[g];
     if (inv == 0.f) inv = pos_nan();  // every position masked: NaN, as softmax of all -inf
     acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
     char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
     *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
   }
+}
+
+// Combines the per-split partials of one (sequence, KV head) of the
+// per-sequence split kernel.
+template <int D, bool Q_BF16>
+__global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
+  // launched as a programmatic dependent of the split kernel: wait here until
+  // that grid has completed and its writes are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int h = blockIdx.x, b = blockIdx.y;
+  int pos, L, nsplit;
+  decode_extent(a, b, pos, L, nsplit);
+  if (nsplit <= 1) return;
+  extern __shared__ float sw[];
+  merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, sw);
+}
+
+// Merge of the balanced kernel's partials for one (KV head, sequence). Also
+// finishes the sequences that no chunk covers (no visible position: the new
+// token is still appended and the output is NaN, as softmax of all -inf).
+template <int D, int KV, bool Q_BF16>
+__global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(const DecodeArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int h = blockIdx.x, b = blockIdx.y;
+  int pos;
+  const int L = seq_len(a, b, pos);
+  if (pos < 0 && h == 0 && threadIdx.x == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
+  if (L == 0) {
+    if (a.k_new != nullptr && pos >= 0 && pos < a.span) append_token<D, KV, Q_BF16>(a, b, h, pos);
+    for (int idx = threadIdx.x; idx < a.G * (D / 4); idx += kThreads) {
+      const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+      const float n = pos_nan();
+      char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n));
+    }
+    return;
+  }
+  const int W = a.prefix[a.B + 1];
+  const int cf = a.prefix[b] / W, cl = (a.prefix[b + 1] - 1) / W;
+  if (cf == cl) return;  // one chunk held the whole sequence and wrote the output
+  extern __shared__ float sw[];
+  merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw);
 }
 
 // ---------------------------------------------------------------------------
@@ -546,8 +705,30 @@ int choose_chunk(const rbln_paged_attn_params_t* p, int span) {
 
 struct Plan {
   int span, chunk, max_splits;
+  bool balanced;
+  int nchunk, min_w;
   size_t ws_bytes;
 };
+
+// Settings read once from the environment (timing sweeps):
+//   RBLN_ATTN_DECODE_SCHED=seq      per-sequence splits instead of balanced
+//   RBLN_ATTN_DECODE_WAVES=n        balanced: chunks per KV head fill n waves
+//   RBLN_ATTN_DECODE_MINW=t         balanced: smallest chunk in tokens
+struct DecodeEnv {
+  bool force_seq = false;
+  int waves = 0, min_w = 0;
+  DecodeEnv() {
+    if (const char* e = std::getenv("RBLN_ATTN_DECODE_SCHED")) force_seq = std::string(e) == "seq";
+    if (const char* e = std::getenv("RBLN_ATTN_DECODE_WAVES")) waves = std::atoi(e);
+    if (const char* e = std::getenv("RBLN_ATTN_DECODE_MINW")) min_w = std::atoi(e);
+  }
+};
+const DecodeEnv& decode_env() {
+  static const DecodeEnv env;
+  return env;
+}
+
+constexpr int kBalancedMaxBatch = 2048;
 
 int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 ||
@@ -561,53 +742,95 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   pl->chunk = choose_chunk(p, pl->span);
   pl->max_splits = (pl->span + pl->chunk - 1) / pl->chunk;
   if (pl->max_splits > 2048) return RBLN_ERR_UNSUPPORTED;
+  const DecodeEnv& env = decode_env();
+  // Balanced chunks unless the caller fixed the number of splits per sequence
+  // (num_splits > 0), the batch is too large for the in-CTA prefix, or the
+  // padded token total could overflow int32.
+  const int64_t padded_total = (int64_t)p->batch * ((span64 + 15) / 16 * 16);
+  pl->balanced = p->num_splits <= 0 && !env.force_seq && p->batch >= 1 && p->batch <= kBalancedMaxBatch &&
+                 padded_total < (int64_t(1) << 30);
+  pl->nchunk = 0;
+  pl->min_w = 0;
   pl->ws_bytes = 0;
-  if (pl->max_splits > 1) {
+  if (pl->balanced) {
+    // enough chunks per KV head to fill `waves` waves of resident CTAs (4 per
+    // SM for up to 8 query heads per KV head, 2 above), each of at least
+    // min_w tokens. One wave measured best on B200 (1..4 swept on the ragged
+    // B=64 bf16 and B=256 fp8 workloads and on 32 x 32768 tokens).
+    const int waves = env.waves > 0 ? env.waves : 1;
+    const int per_sm = p->group <= 8 ? 4 : 2;
+    pl->nchunk = std::max(1, (148 * per_sm * waves + p->num_kv_heads - 1) / p->num_kv_heads);
+    pl->min_w = env.min_w >= 16 ? env.min_w / 16 * 16 : 256;
+    const size_t slots = (size_t)p->num_kv_heads * (pl->nchunk + p->batch) * p->group;
+    pl->ws_bytes = ((size_t)(p->batch + 2) * sizeof(int) + 255) / 256 * 256 + slots * p->head_dim * sizeof(float) +
+                   slots * sizeof(float) + 256;
+  } else if (pl->max_splits > 1) {
     const size_t slots = (size_t)p->batch * p->num_kv_heads * pl->max_splits * p->group;
     pl->ws_bytes = slots * p->head_dim * sizeof(float) + slots * sizeof(float) + 256;
   }
   return RBLN_OK;
 }
 
-// Tiles each warp keeps in flight. One: on B200 two tiles per warp (more
-// registers, fewer resident warps) measured slower for both bf16 and fp8
-// caches. RBLN_ATTN_DECODE_TPI=2 selects the two-tile variant.
-int decode_tpi(int) {
-  static const int env = [] {
-    const char* e = std::getenv("RBLN_ATTN_DECODE_TPI");
-    return e ? std::atoi(e) : 0;
-  }();
-  return env == 2 ? 2 : 1;
+// Opts `kernel` into more than 48 KB of dynamic shared memory, once per
+// device; `done` is that kernel's own bitmask of devices already set.
+bool allow_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done) {
+  if (bytes <= 48 * 1024) return true;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_relaxed) & bit) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done.fetch_or(bit);
+  return true;
+}
+
+// Launches `kernel` as a programmatic dependent of the previous launch on
+// `st`: its grid is set up while that one drains and waits in-kernel
+// (griddepcontrol.wait) for its completion.
+int launch_dependent(void (*kernel)(DecodeArgs), dim3 grid, size_t smem, cudaStream_t st, const DecodeArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
 template <int D, int KV, bool QB, int NT>
 int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
-  dim3 grid(pl.max_splits, a.Hkv, a.B);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
-  if (decode_tpi(KV) == 2)
-    paged_decode_split_kernel<D, KV, QB, NT, 2><<<grid, kThreads, 0, st>>>(a);
-  else
-    paged_decode_split_kernel<D, KV, QB, NT, 1><<<grid, kThreads, 0, st>>>(a);
+  if (pl.balanced) {
+    const size_t smem = combine_bytes<D, NT>() + (size_t)(a.B + 1) * sizeof(int);
+    static std::atomic<uint64_t> done{0};
+    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_balanced_kernel<D, KV, QB, NT>), (int)smem, done))
+      return RBLN_ERR_LAUNCH;
+    paged_decode_balanced_kernel<D, KV, QB, NT><<<dim3(pl.nchunk, a.Hkv), kThreads, smem, st>>>(a);
+    if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
+    // a sequence spans at most nchunk + 1 chunks
+    const size_t msmem = ((size_t)(pl.nchunk + 1) * a.G + a.G) * sizeof(float);
+    static std::atomic<uint64_t> mdone{0};
+    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_balanced_kernel<D, KV, QB>), (int)msmem, mdone))
+      return RBLN_ERR_LAUNCH;
+    const int rc = launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B), msmem, st, a);
+    if (rc != RBLN_OK) return rc;
+    return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+  }
+  paged_decode_split_kernel<D, KV, QB, NT>
+      <<<dim3(pl.max_splits, a.Hkv, a.B), kThreads, combine_bytes<D, NT>(), st>>>(a);
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
     const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(paged_decode_merge_kernel<D, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+    static std::atomic<uint64_t> mdone{0};
+    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_kernel<D, QB>), (int)smem, mdone))
       return RBLN_ERR_LAUNCH;
-    // programmatic dependent launch: the merge grid is set up while the split
-    // kernel drains, and waits in-kernel (griddepcontrol.wait) for its completion
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.Hkv, a.B);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, paged_decode_merge_kernel<D, QB>, a) != cudaSuccess) return RBLN_ERR_LAUNCH;
+    const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B), smem, st, a);
+    if (rc != RBLN_OK) return rc;
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
@@ -660,7 +883,7 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
   }
   const int64_t cache_bytes_hint = ((int64_t)p->num_blocks * p->cache_stride[0]) * kv_sz;
   if (cache_bytes_hint / 16 > (int64_t)UINT32_MAX) return RBLN_ERR_UNSUPPORTED;
-  if (pl.max_splits > 1 && (!p->workspace || p->workspace_bytes < pl.ws_bytes)) return RBLN_ERR_WORKSPACE;
+  if (pl.ws_bytes > 0 && (!p->workspace || p->workspace_bytes < pl.ws_bytes)) return RBLN_ERR_WORKSPACE;
 
   DecodeArgs a{};
   a.q = static_cast<const char*>(p->q);
@@ -682,7 +905,16 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
   a.scale = p->scale; a.scale_dev = p->scale_dev;
   a.B = p->batch; a.Hkv = p->num_kv_heads; a.G = p->group; a.num_blocks = p->num_blocks;
   a.bs = p->block_size; a.span = pl.span; a.chunk = pl.chunk; a.max_splits = pl.max_splits;
-  if (pl.max_splits > 1) {
+  a.nchunk = pl.nchunk;
+  a.min_w = pl.min_w;
+  if (pl.balanced) {
+    uintptr_t w = (reinterpret_cast<uintptr_t>(p->workspace) + 255) & ~uintptr_t(255);
+    a.prefix = reinterpret_cast<int*>(w);
+    w += ((size_t)(p->batch + 2) * sizeof(int) + 255) / 256 * 256;
+    const size_t slots = (size_t)p->num_kv_heads * (pl.nchunk + p->batch) * p->group;
+    a.part_o = reinterpret_cast<float*>(w);
+    a.part_lse = a.part_o + slots * p->head_dim;
+  } else if (pl.max_splits > 1) {
     uintptr_t w = (reinterpret_cast<uintptr_t>(p->workspace) + 255) & ~uintptr_t(255);
     const size_t slots = (size_t)p->batch * p->num_kv_heads * pl.max_splits * p->group;
     a.part_o = reinterpret_cast<float*>(w);

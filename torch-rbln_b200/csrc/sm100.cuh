@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace rbln {
 namespace sm100 {
 
@@ -15,9 +17,7 @@ namespace sm100 {
 // gives up: the kernel raises an error flag and returns instead of hanging.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+using rbln::smem_u32;
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

@@ -63,10 +63,23 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
   return r;
 }
+__device__ __forceinline__ void sts64(uint32_t addr, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(addr), "r"(x), "r"(y) : "memory");
+}
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 r;
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(addr));
   return r;
+}
+
+// Bytes per element of an rbln_dtype_t.
+__host__ __device__ __forceinline__ int dtype_size(int dt) {
+  switch (dt) {
+    case RBLN_DT_F32: case RBLN_DT_I32: return 4;
+    case RBLN_DT_F16: case RBLN_DT_BF16: case RBLN_DT_I16: return 2;
+    case RBLN_DT_I64: return 8;
+    default: return 1;
+  }
 }
 
 // Scalar loads of a runtime-typed element, used for block tables and masks.

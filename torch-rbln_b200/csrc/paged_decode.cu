@@ -56,6 +56,7 @@ namespace rbln {
 namespace {
 
 constexpr int kWarps = 4;
+constexpr int kMaxDevices = 64;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 16;
 
@@ -180,7 +181,21 @@ __device__ __forceinline__ void append_token(const DecodeArgs& a, int b, int h, 
 // their (max, sum, O) are combined in shared memory and written as the final
 // output (whole = the CTA saw every token of the sequence) or as the
 // (O/l, log2-sum-exp) partial at part_o/part_lse index slot + g.
-template <int D, int KV, bool Q_BF16, int NT>
+// Bytes of the CTA combine area: per-warp O [kWarps][8*NT][D] and max/sum.
+template <int D, int NT>
+__host__ __device__ constexpr int combine_bytes() {
+  return (kWarps * 8 * NT * D + 2 * kWarps * 8 * NT) * 4;
+}
+// Dynamic shared memory of a split CTA (the balanced kernel adds B + 1 ints).
+template <int D, int NT>
+__host__ __device__ constexpr int segment_smem() {
+  return combine_bytes<D, NT>();
+}
+
+// LA (block-table lookahead): false = look up each tile's block where it is
+// fetched; true = load the next tile's entry into registers one tile early,
+// so that the lookup is off the tile's critical path.
+template <int D, int KV, bool Q_BF16, int NT, bool LA>
 __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned char* dsm, int b, int h, int t0,
                                                int t1, bool append, bool whole, int64_t slot) {
   using C = Cfg<D, KV>;
@@ -193,6 +208,22 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
     append_token<D, KV, Q_BF16>(a, b, h, a.seq[b * a.seq_stride]);
     __syncthreads();
   }
+
+  // Block id (-1 when outside [0, num_blocks)) and keep bit of token
+  // ts + (lane & 15) (lanes 16..31 repeat it).
+  struct TileEntry {
+    int blk;
+    bool keep;
+  };
+  auto bt_entry = [&](int ts, TileEntry& e) {
+    const int tpos = ts + (lane & 15);
+    const bool in = tpos < t1;
+    e.keep = in && (a.mask == nullptr || load_keep(a.mask, a.mask_dtype, b * a.mask_stride + tpos));
+    const int64_t blk = in ? load_index(a.bt, a.bt_dtype, b * a.bt_stride + tpos / a.bs) : -1;
+    e.blk = (blk >= 0 && blk < a.num_blocks) ? (int)blk : -1;
+  };
+  TileEntry ent;
+  if constexpr (LA) bt_entry(t0 + warp * kTile, ent);  // before the query loads: independent of them
 
   // ---- query fragments: B operand (k = head_dim, n = head) ---------------
   float scale = a.scale_dev ? *a.scale_dev : a.scale;
@@ -276,16 +307,17 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
     uint32_t vmask;
     float ksc, vsc;
   };
-  auto fetch = [&](int ts, Tile& T) {
+  // The tile's block-table entry and mask byte come from `ent`, loaded one
+  // tile earlier (bt_entry) so that the table lookup is off the critical path.
+  auto fetch = [&](int ts, Tile& T, const TileEntry& ent) {
     const int tpos = ts + (lane & 15);
-    bool valid = tpos < t1;
-    if (valid && a.mask) valid = load_keep(a.mask, a.mask_dtype, b * a.mask_stride + tpos);
+    bool valid = ent.keep;
     uint32_t off16 = 0;  // row byte offset / 16
     T.ksc = 1.f;
     T.vsc = 1.f;
     if (valid) {
-      const int64_t blk = load_index(a.bt, a.bt_dtype, b * a.bt_stride + tpos / a.bs);
-      if (blk < 0 || blk >= a.num_blocks) {
+      const int64_t blk = ent.blk;
+      if (blk < 0) {
         valid = false;
         flag_error(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
       } else {
@@ -422,7 +454,10 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
 
   for (int ts = t0 + warp * kTile; ts < t1; ts += kWarps * kTile) {
     Tile T;
-    fetch(ts, T);
+    if constexpr (!LA) bt_entry(ts, ent);
+    fetch(ts, T, ent);
+    // next tile's lookup overlaps this tile's loads and math
+    if constexpr (LA) bt_entry(ts + kWarps * kTile, ent);
     consume(T);
   }
 
@@ -480,11 +515,7 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
   __syncthreads();  // the combine area is reused by the CTA's next segment
 }
 
-// Bytes of the CTA combine area: per-warp O [kWarps][8*NT][D] and max/sum.
-template <int D, int NT>
-__host__ __device__ constexpr int combine_bytes() {
-  return (kWarps * 8 * NT * D + 2 * kWarps * 8 * NT) * 4;
-}
+
 
 // Context length seen by sequence b (see decode_extent).
 __device__ __forceinline__ int seq_len(const DecodeArgs& a, int b, int& pos) {
@@ -494,7 +525,7 @@ __device__ __forceinline__ int seq_len(const DecodeArgs& a, int b, int& pos) {
 
 // One CTA per (context split, KV head, sequence): each sequence is cut into
 // splits of a.chunk tokens.
-template <int D, int KV, bool Q_BF16, int NT>
+template <int D, int KV, bool Q_BF16, int NT, bool LA>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_split_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -505,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_split_
   const int t0 = split * a.chunk;
   const int t1 = min(t0 + a.chunk, L);
   const bool append = pos >= 0 && pos < a.span && min(pos / a.chunk, nsplit - 1) == split;
-  decode_segment<D, KV, Q_BF16, NT>(a, dsm, b, h, t0, t1, append, nsplit == 1,
+  decode_segment<D, KV, Q_BF16, NT, LA>(a, dsm, b, h, t0, t1, append, nsplit == 1,
                                     ((int64_t)(b * a.Hkv + h) * a.max_splits + split) * a.G);
 }
 
@@ -553,10 +584,10 @@ __device__ __forceinline__ int balanced_prefix(const DecodeArgs& a, int* P) {
 // however unequal the sequences are. CTA (c, h) takes chunk c of KV head h,
 // which may cover the end of one sequence and the start of the next ones: one
 // segment (and one partial, at slot c + b of head h) per sequence touched.
-template <int D, int KV, bool Q_BF16, int NT>
+template <int D, int KV, bool Q_BF16, int NT, bool LA>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanced_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  int* P = reinterpret_cast<int*>(dsm + combine_bytes<D, NT>());
+  int* P = reinterpret_cast<int*>(dsm + segment_smem<D, NT>());
   const int c = blockIdx.x, h = blockIdx.y;
   const int W = balanced_prefix(a, P);
   const int T = P[a.B];
@@ -578,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanc
     const int t0 = lo - pb, t1 = min(seg_hi - pb, L);
     const int ap = min(pos, L - 1);
     const bool append = pos >= 0 && pos < a.span && ap >= t0 && ap < t1;
-    decode_segment<D, KV, Q_BF16, NT>(a, dsm, b, h, t0, t1, append, lo == pb && seg_hi == pe,
+    decode_segment<D, KV, Q_BF16, NT, LA>(a, dsm, b, h, t0, t1, append, lo == pb && seg_hi == pe,
                                       ((int64_t)h * (a.nchunk + a.B) + c + b) * a.G);
     lo = seg_hi;
   }
@@ -714,10 +745,13 @@ struct Plan {
 //   RBLN_ATTN_DECODE_SCHED=seq      per-sequence splits instead of balanced
 //   RBLN_ATTN_DECODE_WAVES=n        balanced: chunks per KV head fill n waves
 //   RBLN_ATTN_DECODE_MINW=t         balanced: smallest chunk in tokens
+//   RBLN_ATTN_DECODE_LOOKAHEAD=0    fp8 caches: no block-table lookahead
 struct DecodeEnv {
   bool force_seq = false;
+  int lookahead = 1;
   int waves = 0, min_w = 0;
   DecodeEnv() {
+    if (const char* e = std::getenv("RBLN_ATTN_DECODE_LOOKAHEAD")) lookahead = std::atoi(e);
     if (const char* e = std::getenv("RBLN_ATTN_DECODE_SCHED")) force_seq = std::string(e) == "seq";
     if (const char* e = std::getenv("RBLN_ATTN_DECODE_WAVES")) waves = std::atoi(e);
     if (const char* e = std::getenv("RBLN_ATTN_DECODE_MINW")) min_w = std::atoi(e);
@@ -771,17 +805,24 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   return RBLN_OK;
 }
 
-// Opts `kernel` into more than 48 KB of dynamic shared memory, once per
-// device; `done` is that kernel's own bitmask of devices already set.
-bool allow_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done) {
+// Largest dynamic shared-memory size one kernel has been opted into, per
+// device (one instance per kernel instantiation).
+struct SmemOptIn {
+  std::atomic<int> bytes[kMaxDevices] = {};
+};
+
+// Opts `kernel` into `bytes` of dynamic shared memory when that is above
+// 48 KB and above what it was opted into before on this device.
+bool allow_smem(const void* kernel, int bytes, SmemOptIn& opt) {
   if (bytes <= 48 * 1024) return true;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done.load(std::memory_order_relaxed) & bit) return true;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+  if (opt.bytes[dev].load(std::memory_order_relaxed) >= bytes) return true;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return false;
-  done.fetch_or(bit);
+  int cur = opt.bytes[dev].load(std::memory_order_relaxed);
+  while (cur < bytes && !opt.bytes[dev].compare_exchange_weak(cur, bytes)) {
+  }
   return true;
 }
 
@@ -802,31 +843,35 @@ int launch_dependent(void (*kernel)(DecodeArgs), dim3 grid, size_t smem, cudaStr
   return cudaLaunchKernelEx(&cfg, kernel, a) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
-template <int D, int KV, bool QB, int NT>
+template <int D, int KV, bool QB, int NT, bool LA>
 int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
   if (pl.balanced) {
-    const size_t smem = combine_bytes<D, NT>() + (size_t)(a.B + 1) * sizeof(int);
-    static std::atomic<uint64_t> done{0};
-    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_balanced_kernel<D, KV, QB, NT>), (int)smem, done))
+    const size_t smem = segment_smem<D, NT>() + (size_t)(a.B + 1) * sizeof(int);
+    static SmemOptIn done;
+    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_balanced_kernel<D, KV, QB, NT, LA>), (int)smem, done))
       return RBLN_ERR_LAUNCH;
-    paged_decode_balanced_kernel<D, KV, QB, NT><<<dim3(pl.nchunk, a.Hkv), kThreads, smem, st>>>(a);
+    paged_decode_balanced_kernel<D, KV, QB, NT, LA><<<dim3(pl.nchunk, a.Hkv), kThreads, smem, st>>>(a);
     if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
     // a sequence spans at most nchunk + 1 chunks
     const size_t msmem = ((size_t)(pl.nchunk + 1) * a.G + a.G) * sizeof(float);
-    static std::atomic<uint64_t> mdone{0};
+    static SmemOptIn mdone;
     if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_balanced_kernel<D, KV, QB>), (int)msmem, mdone))
       return RBLN_ERR_LAUNCH;
     const int rc = launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B), msmem, st, a);
     if (rc != RBLN_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
   }
-  paged_decode_split_kernel<D, KV, QB, NT>
-      <<<dim3(pl.max_splits, a.Hkv, a.B), kThreads, combine_bytes<D, NT>(), st>>>(a);
+  static SmemOptIn sdone;
+  if (!allow_smem(reinterpret_cast<const void*>(paged_decode_split_kernel<D, KV, QB, NT, LA>), segment_smem<D, NT>(),
+                  sdone))
+    return RBLN_ERR_LAUNCH;
+  paged_decode_split_kernel<D, KV, QB, NT, LA>
+      <<<dim3(pl.max_splits, a.Hkv, a.B), kThreads, segment_smem<D, NT>(), st>>>(a);
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
     const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);
-    static std::atomic<uint64_t> mdone{0};
+    static SmemOptIn mdone;
     if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_kernel<D, QB>), (int)smem, mdone))
       return RBLN_ERR_LAUNCH;
     const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B), smem, st, a);
@@ -837,7 +882,14 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
 
 template <int D, int KV, bool QB>
 int launch_nt(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
-  return a.G <= 8 ? launch_typed<D, KV, QB, 1>(a, pl, st, ev) : launch_typed<D, KV, QB, 2>(a, pl, st, ev);
+  // Lookahead only where it fits the 128-register budget of 4 CTAs per SM
+  // and measured faster on B200: fp8 caches with up to 8 query heads per KV
+  // head (bf16/f16 tiles hold twice the registers and would spill).
+  if (a.G > 8) return launch_typed<D, KV, QB, 2, false>(a, pl, st, ev);
+  if constexpr (KV == KV_FP8) {
+    if (decode_env().lookahead != 0) return launch_typed<D, KV, QB, 1, true>(a, pl, st, ev);
+  }
+  return launch_typed<D, KV, QB, 1, false>(a, pl, st, ev);
 }
 
 template <int D>

@@ -32,6 +32,7 @@
 // RBLN_DEVERR_TIMEOUT, drains its copies and MMAs, frees TMEM and returns.
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -514,6 +515,60 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
+// Packed fp32 pairs (sm_100a f32x2 instructions): one issue slot for two
+// values.
+__device__ __forceinline__ void fma2(float& a, float& b, float m0, float m1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rm, rc;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rm, {%2, %3};\n\t"
+      "mov.b64 rc, {%4, %5};\n\tfma.rn.f32x2 ra, ra, rm, rc;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "f"(m0), "f"(m1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& a, float& b, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rc;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rc, {%2, %3};\n\t"
+      "add.rn.f32x2 ra, ra, rc;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void mul2(float& a, float& b, float m0, float m1) {
+  asm("{\n\t.reg .b64 ra, rm;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rm, {%2, %3};\n\t"
+      "mul.rn.f32x2 ra, ra, rm;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "f"(m0), "f"(m1));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 8 on the FMA pipe (no SFU or conversion-unit
+// instruction): x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the
+// rounding happens in the add), f in [-0.5, 0.5]; 2^f by a cubic with
+// minimax relative error 7.5e-5 (2^-13.7) on that interval; 2^n built as the
+// float with exponent field n + 127 by an integer multiply-add on the bits of
+// the shifted value. x is clamped to -127 first, where the scale is exactly
+// 0, so masked scores (-inf) give exactly 0.
+__device__ __forceinline__ void exp2_poly2(float& x0, float& x1) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -127.f);
+  x1 = fmaxf(x1, -127.f);
+  float t0 = x0, t1 = x1;
+  add2(t0, t1, kRound, kRound);
+  float f0 = t0, f1 = t1;
+  add2(f0, f1, -kRound, -kRound);        // round(x)
+  fma2(f0, f1, -1.f, -1.f, x0, x1);      // f = x - round(x)
+  float p0 = 0.05517132207751274f, p1 = 0.05517132207751274f;
+  fma2(p0, p1, f0, f1, 0.24261054396629333f, 0.24261054396629333f);
+  fma2(p0, p1, f0, f1, 0.6932609677314758f, 0.6932609677314758f);
+  fma2(p0, p1, f0, f1, 0.9999281167984009f, 0.9999281167984009f);
+  // bits(t) = 0x4B400000 + n, and 0x4B400000 * 2^23 = 0 (mod 2^32)
+  const float s0 = __uint_as_float(__float_as_uint(t0) * 0x800000u + 0x3F800000u);
+  const float s1 = __uint_as_float(__float_as_uint(t1) * 0x800000u + 0x3F800000u);
+  mul2(p0, p1, s0, s1);
+  x0 = p0;
+  x1 = p1;
+}
+
 template <int D>
 struct SmemLayout2 {
   static constexpr int NP = D / 64;
@@ -900,6 +955,429 @@ __global__ void __launch_bounds__(kThreads2, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 128-key kernel for the mask-free paths (causal / bidirectional), the hot
+// path of chunked prefill and SDPA.
+//
+// Same roles and two query tiles per CTA as the two-tile kernel above, with
+// KV tiles of 128 keys so that every QK MMA is 128 x 128 x 16 (an N = 64 MMA
+// occupies the tensor pipe about as long as an N = 128 one on B200). TMEM
+// holds one S buffer per query tile (128 columns) and one O (D columns):
+//   S_A 0..127, S_B 128..255, O_A 256.., O_B 384..
+// The softmax warpgroup of a tile reads S, writes P as bf16/f16 pairs over
+// the first 64 columns of the same buffer, and the PV MMA takes its A operand
+// from there, so P never goes through shared memory. The MMA thread issues,
+// per KV tile j,
+//   PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j)
+// so a query tile's S buffer is overwritten only after the PV that read its
+// P (tcgen05.mma executes in issue order), and while one warpgroup works on
+// its S the tensor core runs the other tile's PV and QK. The commit after
+// QK_x(j) tracks every earlier MMA too, so when S_x(j) is ready PV_x(j-1) has
+// completed and O_x may be rescaled. K and V have their own TMA rings, since
+// a K tile is released after the QKs and a V tile after the PVs one step
+// later. The softmax reads its row of S from TMEM twice, 32 columns at a
+// time (max, then exponentials), which keeps 10 warps within the register
+// file; its arithmetic uses packed f32x2 instructions, and every POLY-th pair
+// of exponentials runs on the FMA pipe (exp2_poly2) instead of the SFU.
+// Shared memory (D = 128): Q 2x32 KB, K 2x32 KB, V 2x32 KB.
+// ---------------------------------------------------------------------------
+constexpr int BN3 = 128;
+constexpr int kThreads3 = 320;  // 10 warps
+
+template <int D>
+struct SmemLayout3 {
+  static constexpr int NP = D / 64;
+  static constexpr int KS = D == 128 ? 2 : 3;  // K ring stages
+  static constexpr int VS = D == 128 ? 2 : 3;  // V ring stages
+  static constexpr int TILE = NP * kPanelBytes;  // 128 rows x D
+  static constexpr int QA = 0;
+  static constexpr int QB = QA + TILE;
+  static constexpr int K0 = QB + TILE;
+  static constexpr int V0 = K0 + KS * TILE;
+  static constexpr int BAR = V0 + VS * TILE;
+  static constexpr int TMEM_SLOT = BAR + 32 * 8;
+  static constexpr int ABORT = TMEM_SLOT + 8;
+  static constexpr int TOTAL = ABORT + 8;
+  static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
+};
+
+enum Bar3 {
+  E_Q = 0,
+  E_KF0, E_KF1, E_KF2, E_KE0, E_KE1, E_KE2,
+  E_VF0, E_VF1, E_VF2, E_VE0, E_VE1, E_VE2,
+  E_SFA, E_SFB,  // S of query tile A / B computed (and every earlier MMA done)
+  E_PFA, E_PFB,  // P of A / B written to TMEM (4 softmax warps each)
+  E_OA, E_OB,    // last PV of A / B complete
+  E_DONE, E_COUNT
+};
+
+template <int D, bool BF16, int POLY>
+__global__ void __launch_bounds__(kThreads3, 1)
+    attn_fwd_tc3_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  using L = SmemLayout3<D>;
+  constexpr int NP = L::NP, KS = L::KS, VS = L::VS;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  volatile int* abort = reinterpret_cast<volatile int*>(sgen + L::ABORT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::TMEM_SLOT);
+  auto bar = [&](int i) { return sbase + L::BAR + 8u * i; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1-D grid over (item, KV head), items longest first: from the sorted list
+  // when there is one, else latest query tiles (most keys) first
+  const int item = (int)(blockIdx.x / a.Hkv), h = (int)(blockIdx.x % a.Hkv);
+  int b, qtile;
+  if (a.work) {
+    const int w = a.work[item];
+    b = w / a.q_tiles;
+    qtile = w - b * a.q_tiles;
+  } else {
+    b = item / a.q_tiles;
+    qtile = a.q_tiles - 1 - (item - b * a.q_tiles);
+  }
+  const int s0 = qtile * 2 * a.QT;
+  const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
+  int kv_end = 0;
+  if (seq_off >= 0) {
+    const int s_hi = min(s0 + 2 * a.QT, a.S_q);
+    int end = (a.mask_mode == MM_CAUSAL) ? seq_off + s_hi : ((a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q);
+    if (a.bt == nullptr) end = min(end, a.kv_extra);
+    kv_end = max(0, min(end, a.span));
+  }
+  const int ntiles = (kv_end + BN3 - 1) / BN3;
+
+  if (threadIdx.x == 0) {
+    *abort = 0;
+    for (int i = 0; i < E_COUNT; ++i) mbar_init(bar(i), (i == E_PFA || i == E_PFB) ? 4u : 1u);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto t_s = [&](int x) { return tmem + x * 128; };
+  auto t_o = [&](int x) { return tmem + 256 + x * 128; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        mbar_arrive_expect_tx(bar(E_Q), 2 * NP * a.QT * a.G * 128);
+        for (int p = 0; p < NP; ++p) {
+          tma_load_5d(sbase + L::QA + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, s0, 0, h, b);
+          tma_load_5d(sbase + L::QB + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, s0 + a.QT, 0, h, b);
+        }
+      }
+      const int rpb = min(a.bs, BN3);
+      const int nbox = BN3 / rpb;  // <= 16 (block size >= 8)
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        // lane i < nbox fetches rows [i*rpb, (i+1)*rpb) of the tile
+        int blk = a.num_blocks;  // out of range -> zero fill
+        int row = 0;
+        const int key = j * BN3 + lane * rpb;
+        if (lane < nbox && key < kv_end) {
+          if (a.bt == nullptr) {
+            blk = b;
+            row = key;
+          } else {
+            const int bi = key / a.bs;
+            row = key - bi * a.bs;
+            if (bi < a.max_blocks) {
+              const int64_t v = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+              if (v >= 0 && v < a.num_blocks) {
+                blk = (int)v;
+              } else if (a.err) {
+                atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+              }
+            }
+          }
+        }
+        const int sk = j % KS;
+        if (j >= KS && !__all_sync(0xffffffffu, mbar_wait(bar(E_KE0 + sk), ((j / KS) - 1) & 1, abort))) break;
+        if (lane == 0) mbar_arrive_expect_tx(bar(E_KF0 + sk), NP * kPanelBytes);
+        __syncwarp();
+        if (lane < nbox)
+          for (int p = 0; p < NP; ++p)
+            tma_load_4d(sbase + L::K0 + sk * L::TILE + p * kPanelBytes + lane * rpb * 128, &tm_k, bar(E_KF0 + sk),
+                        p * 64, row, h, blk);
+        k_issued = j + 1;
+        const int sv = j % VS;
+        if (j >= VS && !__all_sync(0xffffffffu, mbar_wait(bar(E_VE0 + sv), ((j / VS) - 1) & 1, abort))) break;
+        if (lane == 0) mbar_arrive_expect_tx(bar(E_VF0 + sv), NP * kPanelBytes);
+        __syncwarp();
+        if (lane < nbox)
+          for (int p = 0; p < NP; ++p)
+            tma_load_4d(sbase + L::V0 + sv * L::TILE + p * kPanelBytes + lane * rpb * 128, &tm_v, bar(E_VF0 + sv),
+                        p * 64, row, h, blk);
+        v_issued = j + 1;
+      }
+      if (*abort) {
+        // let the copies in flight land before the CTA exits
+        const long long t0c = clock64();
+        for (int j = max(0, k_issued - KS); j < k_issued; ++j)
+          while (!mbar_try_wait(bar(E_KF0 + j % KS), (j / KS) & 1) && clock64() - t0c < 4000000) {
+          }
+        for (int j = max(0, v_issued - VS); j < v_issued; ++j)
+          while (!mbar_try_wait(bar(E_VF0 + j % VS), (j / VS) & 1) && clock64() - t0c < 8000000) {
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t id_qk = idesc_f16(BF16, 128, BN3, false);
+      const uint32_t id_pv = idesc_f16(BF16, 128, D, true);
+      bool ok = mbar_wait(bar(E_Q), 0, abort);
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles && !mbar_wait(bar(E_KF0 + j % KS), (j / KS) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        if (j >= 1 && !mbar_wait(bar(E_VF0 + (j - 1) % VS), ((j - 1) / VS) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        for (int x = 0; x < 2; ++x) {
+          if (j >= 1) {
+            // PV_x(j-1): A = P in S_x (TMEM), B = V tile j-1
+            if (!mbar_wait(bar(x == 0 ? E_PFA : E_PFB), (j - 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t vb = sbase + L::V0 + ((j - 1) % VS) * L::TILE;
+#pragma unroll
+            for (int kk = 0; kk < BN3 / 16; ++kk) {
+              const uint64_t bd = sw128_desc(vb + kk * 16 * 128, kPanelBytes, 1024);
+              umma_f16_ts(t_o(x), t_s(x) + kk * 8, bd, id_pv, (j > 1 || kk > 0) ? 1u : 0u);
+            }
+            if (j == ntiles) umma_commit(bar(x == 0 ? E_OA : E_OB));
+          } else {
+            tc_fence_after();
+          }
+          if (j < ntiles) {
+            // QK_x(j) into S_x
+            const uint32_t qb = sbase + (x == 0 ? L::QA : L::QB);
+            const uint32_t kb = sbase + L::K0 + (j % KS) * L::TILE;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t ad = sw128_desc(qb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = sw128_desc(kb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+              umma_f16_ss(t_s(x), ad, bd, id_qk, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(bar(x == 0 ? E_SFA : E_SFB));
+          }
+        }
+        if (!ok) break;
+        if (j < ntiles) umma_commit(bar(E_KE0 + j % KS));
+        if (j >= 1) umma_commit(bar(E_VE0 + (j - 1) % VS));
+      }
+      if (!ok) {
+        umma_commit(bar(E_DONE));
+        const long long t0c = clock64();
+        while (!mbar_try_wait(bar(E_DONE), 0) && clock64() - t0c < 4000000) {
+        }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- softmax
+    const int x = (warp >= 6) ? 1 : 0;  // query tile
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int g = r / a.QT, i = r - g * a.QT;
+    const int s = s0 + x * a.QT + i;
+    const bool row_ok = (g < a.G) && (s < a.S_q);
+    const int qpos = seq_off + s;
+    const int none_limit = (a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q;
+    // first key any row of this tile may not see (tile-uniform bound for the fast path)
+    const int tile_first_q = seq_off + s0 + x * a.QT;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const float qk_mult = scale * kLog2e;
+    const int bar_sf = x == 0 ? E_SFA : E_SFB, bar_pf = x == 0 ? E_PFA : E_PFB, bar_o = x == 0 ? E_OA : E_OB;
+    float m_run = neg_inf(), l_run = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < ntiles; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(bar_sf), j & 1, abort))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      __syncwarp();
+      const int t0 = j * BN3;
+      const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN3 - 1 <= tile_first_q) && (t0 + BN3 <= kv_end)
+                                                       : (t0 + BN3 <= kv_end);
+      const int lim = (a.mask_mode == MM_CAUSAL) ? min(qpos + 1, kv_end) : min(none_limit, kv_end);
+      // Scores stay unscaled until the exponent: the max is taken on raw
+      // scores (a positive multiplier keeps the order) and the scale is
+      // folded into the packed x*mult - m step.
+      const float mult = qk_mult > 0.f ? qk_mult : 1.f;
+      auto load_chunk = [&](int c4, float (&xc)[32]) {
+        uint32_t tmp[32];
+        tmem_ld32(t_s(x) + lane_off + c4 * 32, tmp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) xc[e] = __uint_as_float(tmp[e]);
+        if (!(qk_mult > 0.f)) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) mul2(xc[e], xc[e + 1], qk_mult, qk_mult);
+        }
+        if (!(interior && row_ok)) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!(row_ok && t0 + c4 * 32 + e < lim)) xc[e] = neg_inf();
+        }
+      };
+      float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
+#pragma unroll
+      for (int c4 = 0; c4 < BN3 / 32; ++c4) {
+        float xc[32];
+        load_chunk(c4, xc);
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          mx0 = max3(mx0, xc[e], xc[e + 1]);
+          mx1 = max3(mx1, xc[e + 2], xc[e + 3]);
+          mx2 = max3(mx2, xc[e + 4], xc[e + 5]);
+          mx3 = max3(mx3, xc[e + 6], xc[e + 7]);
+        }
+      }
+      const float mt = max3(mx0, mx1, fmaxf(mx2, mx3)) * mult;
+      const float m_new = fmaxf(m_run, mt);
+      const bool grow = m_new > m_run + 8.f;
+      float factor = 1.f;
+      if (grow) {
+        factor = exp2_approx(m_run - m_new);
+        l_run *= factor;
+        m_run = m_new;
+      }
+      // S_x(j) ready means PV_x(j-1) has completed: O may be rescaled now,
+      // before this tile's PV (which waits for this tile's P)
+      if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o(x) + lane_off + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          tmem_st32(t_o(x) + lane_off + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      const float nmu = (m_run == neg_inf()) ? 0.f : -m_run;
+      float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < BN3 / 32; ++c4) {
+        float xc[32];
+        load_chunk(c4, xc);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) fma2(xc[e], xc[e + 1], mult, mult, nmu, nmu);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          if (POLY > 0 && ((c4 * 32 + e) / 2) % POLY == POLY - 1) {
+            exp2_poly2(xc[e], xc[e + 1]);
+          } else {
+            xc[e] = exp2_approx(xc[e]);
+            xc[e + 1] = exp2_approx(xc[e + 1]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          add2(sa0, sa1, xc[e], xc[e + 1]);
+          add2(sb0, sb1, xc[e + 2], xc[e + 3]);
+        }
+        // P of these 32 keys into columns [16*c4, 16*c4 + 16) of S_x: the
+        // chunks those columns held have already been read
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = pack2<BF16>(xc[2 * e], xc[2 * e + 1]);
+        __syncwarp();
+        tmem_st16(t_s(x) + lane_off + c4 * 16, pk);
+      }
+      l_run += (sa0 + sa1) + (sb0 + sb1);
+      tmem_wait_st();
+      // keys past kv_end in the last tile may hold unwritten memory: tile A's
+      // warpgroup zeroes their V rows before its P is released (both PV MMAs
+      // of this tile come after that release)
+      if (x == 0 && j == ntiles - 1 && t0 + BN3 > kv_end) {
+        const int sv = j % VS;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(E_VF0 + sv), (j / VS) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        if (t0 + r >= kv_end) {
+          uint8_t* vrow = sgen + L::V0 + sv * L::TILE + r * 128;
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c16 = 0; c16 < 8; ++c16)
+              *reinterpret_cast<uint4*>(vrow + p * kPanelBytes + c16 * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(bar_pf));
+    }
+
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(bar_o), 0, abort));
+    tc_fence_after();
+    if (ok) {
+      const float inv = 1.f / l_run;
+      char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (ntiles > 0) {
+          __syncwarp();
+          tmem_ld32(t_o(x) + lane_off + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 v;
+            v.x = pack2<BF16>(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+            v.y = pack2<BF16>(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+            v.z = pack2<BF16>(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+            v.w = pack2<BF16>(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + (c * 32 + q4 * 8) * 2) = v;
+          }
+        }
+      }
+      if (row_ok && a.lse) {
+        const float v =
+            (m_run == neg_inf() || l_run == 0.f) ? neg_inf() : (m_run + __log2f(l_run)) * 0.6931471805599453f;
+        a.lse[b * a.ls_b + h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // Orders the (sequence, query-tile) items of a two-tile prefill launch by
 // the number of keys they attend, longest first (ties: lower index first),
 // so that the longest CTAs start in the first wave. One CTA; each thread
@@ -1032,6 +1510,55 @@ int launch_tc2_any(const TcLaunch& Lc, cudaStream_t st) {
   return Lc.bf16 ? launch_tc2<64, true>(Lc, st) : launch_tc2<64, false>(Lc, st);
 }
 
+template <int D, bool BF16, int POLY>
+int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
+  using SL = SmemLayout3<D>;
+  if (cudaFuncSetAttribute(attn_fwd_tc3_kernel<D, BF16, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SL::ALLOC) != cudaSuccess)
+    return RBLN_ERR_LAUNCH;
+  const long long n = (long long)Lc.a.q_tiles * Lc.a.B * Lc.a.Hkv;
+  if (n > 2147483647LL) return RBLN_ERR_UNSUPPORTED;
+  attn_fwd_tc3_kernel<D, BF16, POLY><<<(unsigned)n, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+// Share of the 128-key kernel's exponentials evaluated on the FMA pipe:
+// every POLY-th pair (0: none). RBLN_ATTN_PREFILL_POLY in {0, 2, 4, 8}
+// overrides the default.
+int prefill_poly() {
+  static const int v = [] {
+    const char* e = std::getenv("RBLN_ATTN_PREFILL_POLY");
+    const int x = e ? std::atoi(e) : -1;
+    return (x == 0 || x == 2 || x == 4 || x == 8) ? x : 0;
+  }();
+  return v;
+}
+
+template <int D, bool BF16>
+int launch_tc3_poly(const TcLaunch& Lc, cudaStream_t st) {
+  switch (prefill_poly()) {
+    case 2: return launch_tc3<D, BF16, 2>(Lc, st);
+    case 4: return launch_tc3<D, BF16, 4>(Lc, st);
+    case 8: return launch_tc3<D, BF16, 8>(Lc, st);
+    default: return launch_tc3<D, BF16, 0>(Lc, st);
+  }
+}
+
+int launch_tc3_any(const TcLaunch& Lc, cudaStream_t st) {
+  if (Lc.D == 128) return Lc.bf16 ? launch_tc3_poly<128, true>(Lc, st) : launch_tc3_poly<128, false>(Lc, st);
+  return Lc.bf16 ? launch_tc3_poly<64, true>(Lc, st) : launch_tc3_poly<64, false>(Lc, st);
+}
+
+// Kernel for the mask-free paths: 3 = 128-key tiles (default), 2 = 64-key
+// tiles (RBLN_ATTN_PREFILL_KERNEL=2).
+int mask_free_kernel() {
+  static const int v = [] {
+    const char* e = std::getenv("RBLN_ATTN_PREFILL_KERNEL");
+    return (e && std::atoi(e) == 2) ? 2 : 3;
+  }();
+  return v;
+}
+
 // The two-tile kernel serves mask-free causal/bidirectional attention whose
 // block size gives 1 KB-aligned 64-row boxes.
 bool use_tc2(const AttnArgs& a) {
@@ -1132,8 +1659,10 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   TcLaunch Lc{};
   Lc.D = D;
   Lc.bf16 = p->q_dtype == RBLN_DT_BF16;
-  const bool two_tile = !keep_mask_op && !p->mask && ((bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0));
-  const int rpb = std::min(bs, two_tile ? BN2 : BN);
+  const int mfk = mask_free_kernel();
+  const bool two_tile = !keep_mask_op && !p->mask &&
+                        (mfk == 3 || (bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0));
+  const int rpb = std::min(bs, (two_tile && mfk == 2) ? BN2 : BN);
   if (!map_q(&Lc.tq, p->q, p->q_dtype, p->batch, p->num_kv_heads, G, p->q_len, D, p->q_stride, QT))
     return RBLN_ERR_LAUNCH;
   if (!map_kv(&Lc.tk, p->kcache, p->kv_dtype, p->num_blocks, p->num_kv_heads, bs, D, p->cache_stride[0],
@@ -1194,7 +1723,7 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
     }
   }
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
-  const int rc = two_tile ? launch_tc2_any(Lc, st) : launch_tc_any(Lc, st);
+  const int rc = two_tile ? (mfk == 3 ? launch_tc3_any(Lc, st) : launch_tc2_any(Lc, st)) : launch_tc_any(Lc, st);
   if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
   return rc;
 }
@@ -1218,7 +1747,8 @@ int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os
   if (q_tiles > 65535 || Hkv > 65535 || B > 65535) return RBLN_ERR_UNSUPPORTED;
   if (!map_q(&Lc.tq, q, dtype, B, Hkv, G, L, D, qs, QT)) return RBLN_ERR_LAUNCH;
   const bool two_tile = (mask == nullptr);
-  const int rows_per_box = two_tile ? BN2 : BN;
+  const int mfk = mask_free_kernel();
+  const int rows_per_box = (two_tile && mfk == 2) ? BN2 : BN;
   // k [B, Hkv, S, D] seen as a pool of B blocks of S rows
   if (!map_kv(&Lc.tk, k, dtype, B, Hkv, S, D, ks[0], ks[1], ks[2], rows_per_box)) return RBLN_ERR_LAUNCH;
   if (!map_kv(&Lc.tv, v, dtype, B, Hkv, S, D, vs[0], vs[1], vs[2], rows_per_box)) return RBLN_ERR_LAUNCH;
@@ -1262,7 +1792,7 @@ int attn_tc_dense(const void* q, const int64_t* qs, void* out, const int64_t* os
   a.err = err;
   if (two_tile) {
     a.q_tiles = (L + 2 * QT - 1) / (2 * QT);
-    return launch_tc2_any(Lc, st);
+    return mfk == 3 ? launch_tc3_any(Lc, st) : launch_tc2_any(Lc, st);
   }
   return launch_tc_any(Lc, st);
 }

@@ -975,14 +975,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
 // QK_x(j) tracks every earlier MMA too, so when S_x(j) is ready PV_x(j-1) has
 // completed and O_x may be rescaled. K and V have their own TMA rings, since
 // a K tile is released after the QKs and a V tile after the PVs one step
-// later. The softmax reads its row of S from TMEM twice, 32 columns at a
-// time (max, then exponentials), which keeps 10 warps within the register
-// file; its arithmetic uses packed f32x2 instructions, and every POLY-th pair
+// later. The CTA has 12 warps; the producer/MMA warpgroup hands registers to
+// the two softmax warpgroups (setmaxnreg), so a softmax thread holds its
+// whole row of 128 scores (one TMEM round trip per tile); the softmax
+// arithmetic uses packed f32x2 instructions, and every POLY-th pair
 // of exponentials runs on the FMA pipe (exp2_poly2) instead of the SFU.
 // Shared memory (D = 128): Q 2x32 KB, K 2x32 KB, V 2x32 KB.
 // ---------------------------------------------------------------------------
 constexpr int BN3 = 128;
-constexpr int kThreads3 = 320;  // 10 warps
+constexpr int kThreads3 = 384;  // 12 warps: softmax A 0-3, softmax B 4-7, producer 8, MMA 9, 10-11 idle
+// Registers per thread after the split (launch: 168 each, 12 warps): the
+// softmax warpgroups hold a whole 128-score row, the third warpgroup little.
+constexpr uint32_t kRegsSoftmax3 = 200, kRegsOther3 = 96;
+static_assert(2 * 128 * kRegsSoftmax3 + 128 * kRegsOther3 <= 12 * 32 * 168, "register split exceeds the launch");
 
 template <int D>
 struct SmemLayout3 {
@@ -1053,7 +1058,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
     for (int i = 0; i < E_COUNT; ++i) mbar_init(bar(i), (i == E_PFA || i == E_PFB) ? 4u : 1u);
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -1064,7 +1069,11 @@ __global__ void __launch_bounds__(kThreads3, 1)
   auto t_s = [&](int x) { return tmem + x * 128; };
   auto t_o = [&](int x) { return tmem + 256 + x * 128; };
 
-  if (warp == 0) {
+  // Each warpgroup changes its register count at the top of its own branch,
+  // so the code of the branch is compiled for that count.
+  if (warp >= 8) {
+   setmaxnreg_dec<kRegsOther3>();
+   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (ntiles > 0) {
       if (lane == 0) {
@@ -1132,7 +1141,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
           }
       }
     }
-  } else if (warp == 1) {
+   } else if (warp == 9) {
     // ------------------------------------------------------------- MMA
     if (lane == 0 && ntiles > 0) {
       const uint32_t id_qk = idesc_f16(BF16, 128, BN3, false);
@@ -1189,9 +1198,11 @@ __global__ void __launch_bounds__(kThreads3, 1)
         }
       }
     }
+   }
   } else {
+    setmaxnreg_inc<kRegsSoftmax3>();
     // --------------------------------------------------------- softmax
-    const int x = (warp >= 6) ? 1 : 0;  // query tile
+    const int x = warp >> 2;  // query tile
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -1223,34 +1234,39 @@ __global__ void __launch_bounds__(kThreads3, 1)
       // scores (a positive multiplier keeps the order) and the scale is
       // folded into the packed x*mult - m step.
       const float mult = qk_mult > 0.f ? qk_mult : 1.f;
-      auto load_chunk = [&](int c4, float (&xc)[32]) {
-        uint32_t tmp[32];
-        tmem_ld32(t_s(x) + lane_off + c4 * 32, tmp);
+      // the row's 128 scores: four loads, one wait
+      float xv[BN3];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(t_s(x) + lane_off + 0, r0);
+        tmem_ld32(t_s(x) + lane_off + 32, r1);
+        tmem_ld32(t_s(x) + lane_off + 64, r2);
+        tmem_ld32(t_s(x) + lane_off + 96, r3);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) xc[e] = __uint_as_float(tmp[e]);
-        if (!(qk_mult > 0.f)) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) mul2(xc[e], xc[e + 1], qk_mult, qk_mult);
+        for (int e = 0; e < 32; ++e) {
+          xv[e] = __uint_as_float(r0[e]);
+          xv[32 + e] = __uint_as_float(r1[e]);
+          xv[64 + e] = __uint_as_float(r2[e]);
+          xv[96 + e] = __uint_as_float(r3[e]);
         }
-        if (!(interior && row_ok)) {
+      }
+      if (!(qk_mult > 0.f)) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (!(row_ok && t0 + c4 * 32 + e < lim)) xc[e] = neg_inf();
-        }
-      };
+        for (int e = 0; e < BN3; e += 2) mul2(xv[e], xv[e + 1], qk_mult, qk_mult);
+      }
+      if (!(interior && row_ok)) {
+#pragma unroll
+        for (int e = 0; e < BN3; ++e)
+          if (!(row_ok && t0 + e < lim)) xv[e] = neg_inf();
+      }
       float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
 #pragma unroll
-      for (int c4 = 0; c4 < BN3 / 32; ++c4) {
-        float xc[32];
-        load_chunk(c4, xc);
-#pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          mx0 = max3(mx0, xc[e], xc[e + 1]);
-          mx1 = max3(mx1, xc[e + 2], xc[e + 3]);
-          mx2 = max3(mx2, xc[e + 4], xc[e + 5]);
-          mx3 = max3(mx3, xc[e + 6], xc[e + 7]);
-        }
+      for (int e = 0; e < BN3; e += 8) {
+        mx0 = max3(mx0, xv[e], xv[e + 1]);
+        mx1 = max3(mx1, xv[e + 2], xv[e + 3]);
+        mx2 = max3(mx2, xv[e + 4], xv[e + 5]);
+        mx3 = max3(mx3, xv[e + 6], xv[e + 7]);
       }
       const float mt = max3(mx0, mx1, fmaxf(mx2, mx3)) * mult;
       const float m_new = fmaxf(m_run, mt);
@@ -1277,33 +1293,30 @@ __global__ void __launch_bounds__(kThreads3, 1)
         tmem_wait_st();
       }
       const float nmu = (m_run == neg_inf()) ? 0.f : -m_run;
+#pragma unroll
+      for (int e = 0; e < BN3; e += 2) fma2(xv[e], xv[e + 1], mult, mult, nmu, nmu);
+#pragma unroll
+      for (int e = 0; e < BN3; e += 2) {
+        if (POLY > 0 && (e / 2) % POLY == POLY - 1) {
+          exp2_poly2(xv[e], xv[e + 1]);
+        } else {
+          xv[e] = exp2_approx(xv[e]);
+          xv[e + 1] = exp2_approx(xv[e + 1]);
+        }
+      }
       float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
 #pragma unroll
+      for (int e = 0; e < BN3; e += 4) {
+        add2(sa0, sa1, xv[e], xv[e + 1]);
+        add2(sb0, sb1, xv[e + 2], xv[e + 3]);
+      }
+      // P of the row over the first 64 columns of S_x (all of S is in registers)
+      __syncwarp();
+#pragma unroll
       for (int c4 = 0; c4 < BN3 / 32; ++c4) {
-        float xc[32];
-        load_chunk(c4, xc);
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) fma2(xc[e], xc[e + 1], mult, mult, nmu, nmu);
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          if (POLY > 0 && ((c4 * 32 + e) / 2) % POLY == POLY - 1) {
-            exp2_poly2(xc[e], xc[e + 1]);
-          } else {
-            xc[e] = exp2_approx(xc[e]);
-            xc[e + 1] = exp2_approx(xc[e + 1]);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          add2(sa0, sa1, xc[e], xc[e + 1]);
-          add2(sb0, sb1, xc[e + 2], xc[e + 3]);
-        }
-        // P of these 32 keys into columns [16*c4, 16*c4 + 16) of S_x: the
-        // chunks those columns held have already been read
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack2<BF16>(xc[2 * e], xc[2 * e + 1]);
-        __syncwarp();
+        for (int e = 0; e < 16; ++e) pk[e] = pack2<BF16>(xv[32 * c4 + 2 * e], xv[32 * c4 + 2 * e + 1]);
         tmem_st16(t_s(x) + lane_off + c4 * 16, pk);
       }
       l_run += (sa0 + sa1) + (sb0 + sb1);
@@ -1372,7 +1385,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
   tc_fence_before();
   __syncthreads();
   if (*abort && threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1513,6 +1526,14 @@ int launch_tc2_any(const TcLaunch& Lc, cudaStream_t st) {
 template <int D, bool BF16, int POLY>
 int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
   using SL = SmemLayout3<D>;
+  // The warpgroups' setmaxnreg split assumes 168 registers per thread at
+  // launch; with fewer, a warpgroup raising its count would never be served.
+  static const bool regs_ok = [] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, attn_fwd_tc3_kernel<D, BF16, POLY>) == cudaSuccess &&
+           2 * 128 * kRegsSoftmax3 + 128 * kRegsOther3 <= (uint32_t)fa.numRegs * kThreads3;
+  }();
+  if (!regs_ok) return RBLN_ERR_LAUNCH;
   if (cudaFuncSetAttribute(attn_fwd_tc3_kernel<D, BF16, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            SL::ALLOC) != cudaSuccess)
     return RBLN_ERR_LAUNCH;
@@ -1523,13 +1544,13 @@ int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
 }
 
 // Share of the 128-key kernel's exponentials evaluated on the FMA pipe:
-// every POLY-th pair (0: none). RBLN_ATTN_PREFILL_POLY in {0, 2, 4, 8}
-// overrides the default.
+// every POLY-th pair (0: none). Default 8 (one in eight), best of 0/4/8 on
+// B200; RBLN_ATTN_PREFILL_POLY in {0, 2, 4, 8} overrides it.
 int prefill_poly() {
   static const int v = [] {
     const char* e = std::getenv("RBLN_ATTN_PREFILL_POLY");
     const int x = e ? std::atoi(e) : -1;
-    return (x == 0 || x == 2 || x == 4 || x == 8) ? x : 0;
+    return (x == 0 || x == 2 || x == 4 || x == 8) ? x : 8;
   }();
   return v;
 }

@@ -1338,8 +1338,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
             for (int c16 = 0; c16 < 8; ++c16)
               *reinterpret_cast<uint4*>(vrow + p * kPanelBytes + c16 * 16) = make_uint4(0, 0, 0, 0);
         }
+        fence_proxy_async_smem();  // the zeroed rows are read by the PV MMA (async proxy)
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(bar_pf));

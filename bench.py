@@ -349,7 +349,7 @@ def run_ours(args, wl_name):
                 "api": "torch.ops.rbln_custom_ops.paged_causal_attn_decode" + ("_kvfp8" if d["fp8"] else "")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": None,
-                     "kernel": "paged_decode_split_kernel", "kernel_ms": round(kmean, 4),
+                     "kernel": "paged_decode_balanced_kernel (equal token chunks over the batch, mma.sync)", "kernel_ms": round(kmean, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
                      else "fallback 6.65 TB/s"},
         "gpu_launches": launches_per_step * args.steps,
@@ -602,7 +602,7 @@ def run_compute_ours(args, wl_name):
         out_shape, out_dtype = q.shape, q.dtype
         metric = "paged chunked prefill TFLOP/s"
         launches = 3  # schedule pre-pass, append, attention
-        kernel = "attn_fwd_tc2_kernel<128, bf16> (tcgen05/TMEM/TMA, two query tiles per CTA)"
+        kernel = "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)"
         dtype = "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
     else:
@@ -631,7 +631,7 @@ def run_compute_ours(args, wl_name):
         launches = 1
         kernel = ("sdpa_f32_kernel<64> (exact-fp32 SIMT; tensor cores have no fp32 mode)"
                   if wl["dtype"] == torch.float32
-                  else "attn_fwd_tc2_kernel<128, bf16> (tcgen05/TMEM/TMA, two query tiles per CTA)")
+                  else "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)")
         dtype = "f32" if wl["dtype"] == torch.float32 else "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
 

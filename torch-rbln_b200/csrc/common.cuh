@@ -38,48 +38,9 @@ __device__ __forceinline__ uint2 ld_stream_v2(const void* p) {
   return r;
 }
 
-// Asynchronous global -> shared copies (cp.async), completed per thread by
-// commit/wait groups. `src_bytes` < size zero-fills the rest (0: no read).
+// 32-bit shared-state-space address of a shared-memory pointer.
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
-  return r;
-}
-__device__ __forceinline__ void sts64(uint32_t addr, uint32_t x, uint32_t y) {
-  asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(addr), "r"(x), "r"(y) : "memory");
-}
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 r;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(addr));
-  return r;
-}
-
-// Bytes per element of an rbln_dtype_t.
-__host__ __device__ __forceinline__ int dtype_size(int dt) {
-  switch (dt) {
-    case RBLN_DT_F32: case RBLN_DT_I32: return 4;
-    case RBLN_DT_F16: case RBLN_DT_BF16: case RBLN_DT_I16: return 2;
-    case RBLN_DT_I64: return 8;
-    default: return 1;
-  }
 }
 
 // Scalar loads of a runtime-typed element, used for block tables and masks.
@@ -152,14 +113,14 @@ __device__ __forceinline__ float2 unpack2(uint32_t v) {
   }
 }
 
-// Two e4m3 values (low byte -> low half) to an f16 pair. Exact: every e4m3
-// value is representable in f16.
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t lo16) {
-  uint32_t d;
-  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}"
-      : "=r"(d)
-      : "r"(lo16));
-  return d;
+// Four e4m3 values (bytes 0..3 of w) to two f16 pairs: lo = (b0, b1),
+// hi = (b2, b3); exact, every e4m3 value is representable in f16. The
+// 16-bit halves are taken as register halves, with no mask or shift.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

@@ -381,8 +381,9 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
         const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&T.kraw[1][i]);
 #pragma unroll
         for (int w = 0; w < 4; ++w) {  // kk = 4i + w uses chunk word w (4 fp8)
-          const uint32_t a0 = e4m3x2_to_f16x2(r0[w] & 0xffffu), a2 = e4m3x2_to_f16x2(r0[w] >> 16);
-          const uint32_t a1 = e4m3x2_to_f16x2(r1[w] & 0xffffu), a3 = e4m3x2_to_f16x2(r1[w] >> 16);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2x2(r0[w], a0, a2);
+          e4m3x4_to_f16x2x2(r1[w], a1, a3);
           const int kk = 4 * i + w;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
@@ -442,10 +443,8 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
         const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
         const uint32_t x = prmt(T.vraw[0][w], T.vraw[1][w], sel);
         const uint32_t y = prmt(T.vraw[2][w], T.vraw[3][w], sel);
-        a0 = e4m3x2_to_f16x2(x & 0xffffu);
-        a1 = e4m3x2_to_f16x2(x >> 16);
-        a2 = e4m3x2_to_f16x2(y & 0xffffu);
-        a3 = e4m3x2_to_f16x2(y >> 16);
+        e4m3x4_to_f16x2x2(x, a0, a1);
+        e4m3x4_to_f16x2x2(y, a2, a3);
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma16816<MB>(o_acc[nt][mt], a0, a1, a2, a3, pb0[nt], pb1[nt]);

@@ -86,6 +86,7 @@ struct AttnArgs {
   const float* scale_dev;
   uint32_t* err;
   const int* work;  // optional: items (b * q_tiles + tile) in launch order, longest first
+  int* counter;     // optional: next unit of a persistent launch (zeroed by the schedule pre-pass)
 };
 
 __device__ __forceinline__ float mask_value(const void* base, int dt, int64_t i) {
@@ -986,7 +987,7 @@ constexpr int BN3 = 128;
 constexpr int kThreads3 = 384;  // 12 warps: softmax A 0-3, softmax B 4-7, producer 8, MMA 9, 10-11 idle
 // Registers per thread after the split (launch: 168 each, 12 warps): the
 // softmax warpgroups hold a whole 128-score row, the third warpgroup little.
-constexpr uint32_t kRegsSoftmax3 = 200, kRegsOther3 = 96;
+constexpr uint32_t kRegsSoftmax3 = 216, kRegsOther3 = 64;
 static_assert(2 * 128 * kRegsSoftmax3 + 128 * kRegsOther3 <= 12 * 32 * 168, "register split exceeds the launch");
 
 template <int D>
@@ -1002,9 +1003,12 @@ struct SmemLayout3 {
   static constexpr int BAR = V0 + VS * TILE;
   static constexpr int TMEM_SLOT = BAR + 32 * 8;
   static constexpr int ABORT = TMEM_SLOT + 8;
-  static constexpr int TOTAL = ABORT + 8;
+  static constexpr int UNITS = ABORT + 8;  // ring of kUnitRing unit ids
+  static constexpr int TOTAL = UNITS + 4 * 4;
   static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
 };
+
+constexpr int kUnitRing = 4;
 
 enum Bar3 {
   E_Q = 0,
@@ -1012,14 +1016,60 @@ enum Bar3 {
   E_VF0, E_VF1, E_VF2, E_VE0, E_VE1, E_VE2,
   E_SFA, E_SFB,  // S of query tile A / B computed (and every earlier MMA done)
   E_PFA, E_PFB,  // P of A / B written to TMEM (4 softmax warps each)
-  E_OA, E_OB,    // last PV of A / B complete
-  E_DONE, E_COUNT
+  E_OA, E_OB,    // last PV of A / B of a unit complete
+  E_QE,          // every QK of a unit complete: Q may be reloaded
+  E_OEA, E_OEB,  // O of A / B read by the softmax (4 warps each)
+  E_UF0,         // kUnitRing barriers: unit id of a ring slot written (producer)
+  E_UE0 = E_UF0 + kUnitRing,  // kUnitRing barriers: slot read (MMA thread + 8 softmax warps)
+  E_DONE = E_UE0 + kUnitRing, E_COUNT
 };
 
+// Unit u of a launch of the 128-key kernel: (item, KV head), the item taken
+// from the longest-first list when there is one, else in reverse query-tile
+// order. Every role of a CTA derives the same units, in the same order.
+struct Unit3 {
+  int b, h, s0, seq_off, kv_end, ntiles;
+};
+__device__ __forceinline__ Unit3 unit3(const AttnArgs& a, int u) {
+  Unit3 t;
+  const int item = u / a.Hkv;
+  t.h = u - item * a.Hkv;
+  int qtile;
+  if (a.work) {
+    const int w = a.work[item];
+    t.b = w / a.q_tiles;
+    qtile = w - t.b * a.q_tiles;
+  } else {
+    t.b = item / a.q_tiles;
+    qtile = a.q_tiles - 1 - (item - t.b * a.q_tiles);
+  }
+  t.s0 = qtile * 2 * a.QT;
+  t.seq_off = a.seq ? a.seq[t.b * a.seq_stride] : 0;
+  t.kv_end = 0;
+  if (t.seq_off >= 0) {
+    const int s_hi = min(t.s0 + 2 * a.QT, a.S_q);
+    int end = (a.mask_mode == MM_CAUSAL) ? t.seq_off + s_hi : ((a.bt == nullptr) ? a.kv_extra : t.seq_off + a.S_q);
+    if (a.bt == nullptr) end = min(end, a.kv_extra);
+    t.kv_end = max(0, min(end, a.span));
+  }
+  t.ntiles = (t.kv_end + BN3 - 1) / BN3;
+  return t;
+}
+
+// Persistent: one CTA per SM. The producer takes the next unit from the
+// launch's counter (the units are in longest-first order, so a free CTA
+// takes the longest unit left) or, without one, every gridDim.x-th unit, and
+// passes its id to the MMA thread and the softmax warps through a small ring
+// in shared memory. Ring stages and barrier parities follow a running count
+// T of the CTA's KV tiles and `act` of its units with work, so the producer
+// loads the next unit's Q and K/V while the softmax finishes the previous
+// one. Q is reloaded after the previous unit's last QK (E_QE); a unit's
+// first PV overwrites O only after the softmax has read the previous O
+// (E_OEA/B).
 template <int D, bool BF16, int POLY>
 __global__ void __launch_bounds__(kThreads3, 1)
     attn_fwd_tc3_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+                        const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_units) {
   using L = SmemLayout3<D>;
   constexpr int NP = L::NP, KS = L::KS, VS = L::VS;
   extern __shared__ uint8_t smem_raw[];
@@ -1028,34 +1078,14 @@ __global__ void __launch_bounds__(kThreads3, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(sgen + L::ABORT);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::TMEM_SLOT);
   auto bar = [&](int i) { return sbase + L::BAR + 8u * i; };
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-D grid over (item, KV head), items longest first: from the sorted list
-  // when there is one, else latest query tiles (most keys) first
-  const int item = (int)(blockIdx.x / a.Hkv), h = (int)(blockIdx.x % a.Hkv);
-  int b, qtile;
-  if (a.work) {
-    const int w = a.work[item];
-    b = w / a.q_tiles;
-    qtile = w - b * a.q_tiles;
-  } else {
-    b = item / a.q_tiles;
-    qtile = a.q_tiles - 1 - (item - b * a.q_tiles);
-  }
-  const int s0 = qtile * 2 * a.QT;
-  const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
-  int kv_end = 0;
-  if (seq_off >= 0) {
-    const int s_hi = min(s0 + 2 * a.QT, a.S_q);
-    int end = (a.mask_mode == MM_CAUSAL) ? seq_off + s_hi : ((a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q);
-    if (a.bt == nullptr) end = min(end, a.kv_extra);
-    kv_end = max(0, min(end, a.span));
-  }
-  const int ntiles = (kv_end + BN3 - 1) / BN3;
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < E_COUNT; ++i) mbar_init(bar(i), (i == E_PFA || i == E_PFB) ? 4u : 1u);
+    for (int i = 0; i < E_COUNT; ++i)
+      mbar_init(bar(i), (i == E_PFA || i == E_PFB || i == E_OEA || i == E_OEB) ? 4u
+                        : (i >= E_UE0 && i < E_UE0 + kUnitRing)          ? 9u
+                                                                         : 1u);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -1068,6 +1098,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const uint32_t tmem = *tmem_slot;
   auto t_s = [&](int x) { return tmem + x * 128; };
   auto t_o = [&](int x) { return tmem + 256 + x * 128; };
+  volatile int* units = reinterpret_cast<volatile int*>(sgen + L::UNITS);
 
   // Each warpgroup changes its register count at the top of its own branch,
   // so the code of the branch is compiled for that count.
@@ -1075,34 +1106,62 @@ __global__ void __launch_bounds__(kThreads3, 1)
    setmaxnreg_dec<kRegsOther3>();
    if (warp == 8) {
     // ------------------------------------------------------------ producer
-    if (ntiles > 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+    }
+    const int rpb = min(a.bs, BN3);
+    const int nbox = BN3 / rpb;  // <= 16 (block size >= 8)
+    int T = 0, act = 0, k_issued = 0, v_issued = 0;
+    bool ok = true;
+    for (int kq = 0; ok; ++kq) {
+      // next unit: from the launch's counter (longest first, taken by
+      // whichever CTA is free), else every gridDim.x-th; -1 ends the loop
+      const int slot = kq % kUnitRing;
+      if (kq >= kUnitRing &&
+          !__all_sync(0xffffffffu, mbar_wait(bar(E_UE0 + slot), ((kq / kUnitRing) - 1) & 1, abort))) {
+        ok = false;
+        break;
+      }
+      int u = 0;
       if (lane == 0) {
-        prefetch_tmap(&tm_q);
-        prefetch_tmap(&tm_k);
-        prefetch_tmap(&tm_v);
+        u = a.counter ? atomicAdd(a.counter, 1) : (int)blockIdx.x + kq * (int)gridDim.x;
+        if (u >= n_units) u = -1;
+        units[slot] = u;
+        mbar_arrive(bar(E_UF0 + slot));
+      }
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u < 0) break;
+      const Unit3 t = unit3(a, u);
+      if (t.ntiles == 0) continue;
+      // Q of this unit once every QK of the previous one has completed
+      if (act >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(E_QE), (act - 1) & 1, abort))) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
         mbar_arrive_expect_tx(bar(E_Q), 2 * NP * a.QT * a.G * 128);
         for (int p = 0; p < NP; ++p) {
-          tma_load_5d(sbase + L::QA + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, s0, 0, h, b);
-          tma_load_5d(sbase + L::QB + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, s0 + a.QT, 0, h, b);
+          tma_load_5d(sbase + L::QA + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, t.s0, 0, t.h, t.b);
+          tma_load_5d(sbase + L::QB + p * kPanelBytes, &tm_q, bar(E_Q), p * 64, t.s0 + a.QT, 0, t.h, t.b);
         }
       }
-      const int rpb = min(a.bs, BN3);
-      const int nbox = BN3 / rpb;  // <= 16 (block size >= 8)
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
+      for (int j = 0; j < t.ntiles; ++j) {
+        const int Tj = T + j;
         // lane i < nbox fetches rows [i*rpb, (i+1)*rpb) of the tile
         int blk = a.num_blocks;  // out of range -> zero fill
         int row = 0;
         const int key = j * BN3 + lane * rpb;
-        if (lane < nbox && key < kv_end) {
+        if (lane < nbox && key < t.kv_end) {
           if (a.bt == nullptr) {
-            blk = b;
+            blk = t.b;
             row = key;
           } else {
             const int bi = key / a.bs;
             row = key - bi * a.bs;
             if (bi < a.max_blocks) {
-              const int64_t v = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+              const int64_t v = load_index(a.bt, a.bt_dtype, t.b * a.bt_stride + bi);
               if (v >= 0 && v < a.num_blocks) {
                 blk = (int)v;
               } else if (a.err) {
@@ -1111,85 +1170,118 @@ __global__ void __launch_bounds__(kThreads3, 1)
             }
           }
         }
-        const int sk = j % KS;
-        if (j >= KS && !__all_sync(0xffffffffu, mbar_wait(bar(E_KE0 + sk), ((j / KS) - 1) & 1, abort))) break;
+        const int sk = Tj % KS;
+        if (Tj >= KS && !__all_sync(0xffffffffu, mbar_wait(bar(E_KE0 + sk), ((Tj / KS) - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
         if (lane == 0) mbar_arrive_expect_tx(bar(E_KF0 + sk), NP * kPanelBytes);
         __syncwarp();
         if (lane < nbox)
           for (int p = 0; p < NP; ++p)
             tma_load_4d(sbase + L::K0 + sk * L::TILE + p * kPanelBytes + lane * rpb * 128, &tm_k, bar(E_KF0 + sk),
-                        p * 64, row, h, blk);
-        k_issued = j + 1;
-        const int sv = j % VS;
-        if (j >= VS && !__all_sync(0xffffffffu, mbar_wait(bar(E_VE0 + sv), ((j / VS) - 1) & 1, abort))) break;
+                        p * 64, row, t.h, blk);
+        k_issued = Tj + 1;
+        const int sv = Tj % VS;
+        if (Tj >= VS && !__all_sync(0xffffffffu, mbar_wait(bar(E_VE0 + sv), ((Tj / VS) - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
         if (lane == 0) mbar_arrive_expect_tx(bar(E_VF0 + sv), NP * kPanelBytes);
         __syncwarp();
         if (lane < nbox)
           for (int p = 0; p < NP; ++p)
             tma_load_4d(sbase + L::V0 + sv * L::TILE + p * kPanelBytes + lane * rpb * 128, &tm_v, bar(E_VF0 + sv),
-                        p * 64, row, h, blk);
-        v_issued = j + 1;
+                        p * 64, row, t.h, blk);
+        v_issued = Tj + 1;
       }
-      if (*abort) {
-        // let the copies in flight land before the CTA exits
-        const long long t0c = clock64();
-        for (int j = max(0, k_issued - KS); j < k_issued; ++j)
-          while (!mbar_try_wait(bar(E_KF0 + j % KS), (j / KS) & 1) && clock64() - t0c < 4000000) {
-          }
-        for (int j = max(0, v_issued - VS); j < v_issued; ++j)
-          while (!mbar_try_wait(bar(E_VF0 + j % VS), (j / VS) & 1) && clock64() - t0c < 8000000) {
-          }
-      }
+      T += t.ntiles;
+      ++act;
+    }
+    if (*abort) {
+      // let the copies in flight land before the CTA exits
+      const long long t0c = clock64();
+      for (int j = max(0, k_issued - KS); j < k_issued; ++j)
+        while (!mbar_try_wait(bar(E_KF0 + j % KS), (j / KS) & 1) && clock64() - t0c < 4000000) {
+        }
+      for (int j = max(0, v_issued - VS); j < v_issued; ++j)
+        while (!mbar_try_wait(bar(E_VF0 + j % VS), (j / VS) & 1) && clock64() - t0c < 8000000) {
+        }
     }
    } else if (warp == 9) {
     // ------------------------------------------------------------- MMA
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0) {
       const uint32_t id_qk = idesc_f16(BF16, 128, BN3, false);
       const uint32_t id_pv = idesc_f16(BF16, 128, D, true);
-      bool ok = mbar_wait(bar(E_Q), 0, abort);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles && !mbar_wait(bar(E_KF0 + j % KS), (j / KS) & 1, abort)) {
+      int T = 0, act = 0;
+      bool ok = true;
+      for (int kq = 0; ok; ++kq) {
+        const int slot = kq % kUnitRing;
+        if (!mbar_wait(bar(E_UF0 + slot), (kq / kUnitRing) & 1, abort)) {
           ok = false;
           break;
         }
-        if (j >= 1 && !mbar_wait(bar(E_VF0 + (j - 1) % VS), ((j - 1) / VS) & 1, abort)) {
+        const int u = units[slot];
+        mbar_arrive(bar(E_UE0 + slot));
+        if (u < 0) break;
+        const int nt = unit3(a, u).ntiles;
+        if (nt == 0) continue;
+        if (!mbar_wait(bar(E_Q), act & 1, abort)) {
           ok = false;
           break;
         }
-        for (int x = 0; x < 2; ++x) {
-          if (j >= 1) {
-            // PV_x(j-1): A = P in S_x (TMEM), B = V tile j-1
-            if (!mbar_wait(bar(x == 0 ? E_PFA : E_PFB), (j - 1) & 1, abort)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t vb = sbase + L::V0 + ((j - 1) % VS) * L::TILE;
-#pragma unroll
-            for (int kk = 0; kk < BN3 / 16; ++kk) {
-              const uint64_t bd = sw128_desc(vb + kk * 16 * 128, kPanelBytes, 1024);
-              umma_f16_ts(t_o(x), t_s(x) + kk * 8, bd, id_pv, (j > 1 || kk > 0) ? 1u : 0u);
-            }
-            if (j == ntiles) umma_commit(bar(x == 0 ? E_OA : E_OB));
-          } else {
-            tc_fence_after();
+        for (int j = 0; ok && j <= nt; ++j) {
+          const int Tj = T + j;
+          if (j < nt && !mbar_wait(bar(E_KF0 + Tj % KS), (Tj / KS) & 1, abort)) {
+            ok = false;
+            break;
           }
-          if (j < ntiles) {
-            // QK_x(j) into S_x
-            const uint32_t qb = sbase + (x == 0 ? L::QA : L::QB);
-            const uint32_t kb = sbase + L::K0 + (j % KS) * L::TILE;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint64_t ad = sw128_desc(qb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = sw128_desc(kb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
-              umma_f16_ss(t_s(x), ad, bd, id_qk, kk > 0 ? 1u : 0u);
-            }
-            umma_commit(bar(x == 0 ? E_SFA : E_SFB));
+          if (j >= 1 && !mbar_wait(bar(E_VF0 + (Tj - 1) % VS), ((Tj - 1) / VS) & 1, abort)) {
+            ok = false;
+            break;
           }
+          for (int x = 0; x < 2; ++x) {
+            if (j >= 1) {
+              // PV_x(j-1): A = P in S_x (TMEM), B = V tile j-1; the unit's
+              // first PV overwrites O_x once the previous unit's O is read
+              if (!mbar_wait(bar(x == 0 ? E_PFA : E_PFB), (Tj - 1) & 1, abort) ||
+                  (j == 1 && act >= 1 && !mbar_wait(bar(x == 0 ? E_OEA : E_OEB), (act - 1) & 1, abort))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t vb = sbase + L::V0 + ((Tj - 1) % VS) * L::TILE;
+#pragma unroll
+              for (int kk = 0; kk < BN3 / 16; ++kk) {
+                const uint64_t bd = sw128_desc(vb + kk * 16 * 128, kPanelBytes, 1024);
+                umma_f16_ts(t_o(x), t_s(x) + kk * 8, bd, id_pv, (j > 1 || kk > 0) ? 1u : 0u);
+              }
+              if (j == nt) umma_commit(bar(x == 0 ? E_OA : E_OB));
+            } else {
+              tc_fence_after();
+            }
+            if (j < nt) {
+              // QK_x(j) into S_x
+              const uint32_t qb = sbase + (x == 0 ? L::QA : L::QB);
+              const uint32_t kb = sbase + L::K0 + (Tj % KS) * L::TILE;
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint64_t ad = sw128_desc(qb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+                const uint64_t bd = sw128_desc(kb + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
+                umma_f16_ss(t_s(x), ad, bd, id_qk, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(bar(x == 0 ? E_SFA : E_SFB));
+            }
+          }
+          if (!ok) break;
+          if (j < nt) {
+            umma_commit(bar(E_KE0 + Tj % KS));
+            if (j == nt - 1) umma_commit(bar(E_QE));
+          }
+          if (j >= 1) umma_commit(bar(E_VE0 + (Tj - 1) % VS));
         }
-        if (!ok) break;
-        if (j < ntiles) umma_commit(bar(E_KE0 + j % KS));
-        if (j >= 1) umma_commit(bar(E_VE0 + (j - 1) % VS));
+        T += nt;
+        ++act;
       }
       if (!ok) {
         umma_commit(bar(E_DONE));
@@ -1207,150 +1299,166 @@ __global__ void __launch_bounds__(kThreads3, 1)
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int g = r / a.QT, i = r - g * a.QT;
-    const int s = s0 + x * a.QT + i;
-    const bool row_ok = (g < a.G) && (s < a.S_q);
-    const int qpos = seq_off + s;
-    const int none_limit = (a.bt == nullptr) ? a.kv_extra : seq_off + a.S_q;
-    // first key any row of this tile may not see (tile-uniform bound for the fast path)
-    const int tile_first_q = seq_off + s0 + x * a.QT;
     const float scale = a.scale_dev ? *a.scale_dev : a.scale;
     const float qk_mult = scale * kLog2e;
+    const float mult = qk_mult > 0.f ? qk_mult : 1.f;
     const int bar_sf = x == 0 ? E_SFA : E_SFB, bar_pf = x == 0 ? E_PFA : E_PFB, bar_o = x == 0 ? E_OA : E_OB;
-    float m_run = neg_inf(), l_run = 0.f;
+    const int bar_oe = x == 0 ? E_OEA : E_OEB;
+    int T = 0, act = 0;
     bool ok = true;
-
-    for (int j = 0; j < ntiles; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(bar_sf), j & 1, abort))) {
+    for (int kq = 0; ok; ++kq) {
+      const int slot = kq % kUnitRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(E_UF0 + slot), (kq / kUnitRing) & 1, abort))) {
         ok = false;
         break;
       }
-      tc_fence_after();
+      const int u = units[slot];
       __syncwarp();
-      const int t0 = j * BN3;
-      const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN3 - 1 <= tile_first_q) && (t0 + BN3 <= kv_end)
-                                                       : (t0 + BN3 <= kv_end);
-      const int lim = (a.mask_mode == MM_CAUSAL) ? min(qpos + 1, kv_end) : min(none_limit, kv_end);
-      // Scores stay unscaled until the exponent: the max is taken on raw
-      // scores (a positive multiplier keeps the order) and the scale is
-      // folded into the packed x*mult - m step.
-      const float mult = qk_mult > 0.f ? qk_mult : 1.f;
-      // the row's 128 scores: four loads, one wait
-      float xv[BN3];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(t_s(x) + lane_off + 0, r0);
-        tmem_ld32(t_s(x) + lane_off + 32, r1);
-        tmem_ld32(t_s(x) + lane_off + 64, r2);
-        tmem_ld32(t_s(x) + lane_off + 96, r3);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          xv[e] = __uint_as_float(r0[e]);
-          xv[32 + e] = __uint_as_float(r1[e]);
-          xv[64 + e] = __uint_as_float(r2[e]);
-          xv[96 + e] = __uint_as_float(r3[e]);
-        }
-      }
-      if (!(qk_mult > 0.f)) {
-#pragma unroll
-        for (int e = 0; e < BN3; e += 2) mul2(xv[e], xv[e + 1], qk_mult, qk_mult);
-      }
-      if (!(interior && row_ok)) {
-#pragma unroll
-        for (int e = 0; e < BN3; ++e)
-          if (!(row_ok && t0 + e < lim)) xv[e] = neg_inf();
-      }
-      float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
-#pragma unroll
-      for (int e = 0; e < BN3; e += 8) {
-        mx0 = max3(mx0, xv[e], xv[e + 1]);
-        mx1 = max3(mx1, xv[e + 2], xv[e + 3]);
-        mx2 = max3(mx2, xv[e + 4], xv[e + 5]);
-        mx3 = max3(mx3, xv[e + 6], xv[e + 7]);
-      }
-      const float mt = max3(mx0, mx1, fmaxf(mx2, mx3)) * mult;
-      const float m_new = fmaxf(m_run, mt);
-      const bool grow = m_new > m_run + 8.f;
-      float factor = 1.f;
-      if (grow) {
-        factor = exp2_approx(m_run - m_new);
-        l_run *= factor;
-        m_run = m_new;
-      }
-      // S_x(j) ready means PV_x(j-1) has completed: O may be rescaled now,
-      // before this tile's PV (which waits for this tile's P)
-      if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
-        __syncwarp();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(t_o(x) + lane_off + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-          tmem_st32(t_o(x) + lane_off + c * 32, o);
-        }
-        tmem_wait_st();
-      }
-      const float nmu = (m_run == neg_inf()) ? 0.f : -m_run;
-#pragma unroll
-      for (int e = 0; e < BN3; e += 2) fma2(xv[e], xv[e + 1], mult, mult, nmu, nmu);
-#pragma unroll
-      for (int e = 0; e < BN3; e += 2) {
-        if (POLY > 0 && (e / 2) % POLY == POLY - 1) {
-          exp2_poly2(xv[e], xv[e + 1]);
-        } else {
-          xv[e] = exp2_approx(xv[e]);
-          xv[e + 1] = exp2_approx(xv[e + 1]);
-        }
-      }
-      float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
-#pragma unroll
-      for (int e = 0; e < BN3; e += 4) {
-        add2(sa0, sa1, xv[e], xv[e + 1]);
-        add2(sb0, sb1, xv[e + 2], xv[e + 3]);
-      }
-      // P of the row over the first 64 columns of S_x (all of S is in registers)
-      __syncwarp();
-#pragma unroll
-      for (int c4 = 0; c4 < BN3 / 32; ++c4) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack2<BF16>(xv[32 * c4 + 2 * e], xv[32 * c4 + 2 * e + 1]);
-        tmem_st16(t_s(x) + lane_off + c4 * 16, pk);
-      }
-      l_run += (sa0 + sa1) + (sb0 + sb1);
-      tmem_wait_st();
-      // keys past kv_end in the last tile may hold unwritten memory: tile A's
-      // warpgroup zeroes their V rows before its P is released (both PV MMAs
-      // of this tile come after that release)
-      if (x == 0 && j == ntiles - 1 && t0 + BN3 > kv_end) {
-        const int sv = j % VS;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(E_VF0 + sv), (j / VS) & 1, abort))) {
+      if (lane == 0) mbar_arrive(bar(E_UE0 + slot));
+      if (u < 0) break;
+      const Unit3 t = unit3(a, u);
+      const int s = t.s0 + x * a.QT + i;
+      const bool row_ok = (g < a.G) && (s < a.S_q);
+      const int qpos = t.seq_off + s;
+      const int none_limit = (a.bt == nullptr) ? a.kv_extra : t.seq_off + a.S_q;
+      // first key any row of this tile may not see (tile-uniform bound for the fast path)
+      const int tile_first_q = t.seq_off + t.s0 + x * a.QT;
+      const int kv_end = t.kv_end, ntiles = t.ntiles;
+      float m_run = neg_inf(), l_run = 0.f;
+
+      for (int j = 0; j < ntiles; ++j) {
+        const int Tj = T + j;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(bar_sf), Tj & 1, abort))) {
           ok = false;
           break;
         }
-        if (t0 + r >= kv_end) {
-          uint8_t* vrow = sgen + L::V0 + sv * L::TILE + r * 128;
+        tc_fence_after();
+        __syncwarp();
+        const int t0 = j * BN3;
+        const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN3 - 1 <= tile_first_q) && (t0 + BN3 <= kv_end)
+                                                         : (t0 + BN3 <= kv_end);
+        const int lim = (a.mask_mode == MM_CAUSAL) ? min(qpos + 1, kv_end) : min(none_limit, kv_end);
+        // the row's 128 scores: four loads, one wait
+        float xv[BN3];
+        {
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(t_s(x) + lane_off + 0, r0);
+          tmem_ld32(t_s(x) + lane_off + 32, r1);
+          tmem_ld32(t_s(x) + lane_off + 64, r2);
+          tmem_ld32(t_s(x) + lane_off + 96, r3);
+          tmem_wait_ld();
 #pragma unroll
-          for (int p = 0; p < NP; ++p)
-#pragma unroll
-            for (int c16 = 0; c16 < 8; ++c16)
-              *reinterpret_cast<uint4*>(vrow + p * kPanelBytes + c16 * 16) = make_uint4(0, 0, 0, 0);
+          for (int e = 0; e < 32; ++e) {
+            xv[e] = __uint_as_float(r0[e]);
+            xv[32 + e] = __uint_as_float(r1[e]);
+            xv[64 + e] = __uint_as_float(r2[e]);
+            xv[96 + e] = __uint_as_float(r3[e]);
+          }
         }
-        fence_proxy_async_smem();  // the zeroed rows are read by the PV MMA (async proxy)
+        // Scores stay unscaled until the exponent: the max is taken on raw
+        // scores (a positive multiplier keeps the order) and the scale is
+        // folded into the packed x*mult - m step.
+        if (!(qk_mult > 0.f)) {
+#pragma unroll
+          for (int e = 0; e < BN3; e += 2) mul2(xv[e], xv[e + 1], qk_mult, qk_mult);
+        }
+        if (!(interior && row_ok)) {
+#pragma unroll
+          for (int e = 0; e < BN3; ++e)
+            if (!(row_ok && t0 + e < lim)) xv[e] = neg_inf();
+        }
+        float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
+#pragma unroll
+        for (int e = 0; e < BN3; e += 8) {
+          mx0 = max3(mx0, xv[e], xv[e + 1]);
+          mx1 = max3(mx1, xv[e + 2], xv[e + 3]);
+          mx2 = max3(mx2, xv[e + 4], xv[e + 5]);
+          mx3 = max3(mx3, xv[e + 6], xv[e + 7]);
+        }
+        const float mt = max3(mx0, mx1, fmaxf(mx2, mx3)) * mult;
+        const float m_new = fmaxf(m_run, mt);
+        const bool grow = m_new > m_run + 8.f;
+        float factor = 1.f;
+        if (grow) {
+          factor = exp2_approx(m_run - m_new);
+          l_run *= factor;
+          m_run = m_new;
+        }
+        // S_x(j) ready means PV_x(j-1) has completed: O may be rescaled now,
+        // before this tile's PV (which waits for this tile's P)
+        if (j >= 1 && __any_sync(0xffffffffu, grow && factor != 1.f)) {
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o(x) + lane_off + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st32(t_o(x) + lane_off + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        const float nmu = (m_run == neg_inf()) ? 0.f : -m_run;
+#pragma unroll
+        for (int e = 0; e < BN3; e += 2) fma2(xv[e], xv[e + 1], mult, mult, nmu, nmu);
+#pragma unroll
+        for (int e = 0; e < BN3; e += 2) {
+          if (POLY > 0 && (e / 2) % POLY == POLY - 1) {
+            exp2_poly2(xv[e], xv[e + 1]);
+          } else {
+            xv[e] = exp2_approx(xv[e]);
+            xv[e + 1] = exp2_approx(xv[e + 1]);
+          }
+        }
+        float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < BN3; e += 4) {
+          add2(sa0, sa1, xv[e], xv[e + 1]);
+          add2(sb0, sb1, xv[e + 2], xv[e + 3]);
+        }
+        l_run += (sa0 + sa1) + (sb0 + sb1);
+        // P of the row over the first 64 columns of S_x (all of S is in registers)
+        __syncwarp();
+#pragma unroll
+        for (int c4 = 0; c4 < BN3 / 32; ++c4) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = pack2<BF16>(xv[32 * c4 + 2 * e], xv[32 * c4 + 2 * e + 1]);
+          tmem_st16(t_s(x) + lane_off + c4 * 16, pk);
+        }
+        tmem_wait_st();
+        // keys past kv_end in the last tile may hold unwritten memory: tile A's
+        // warpgroup zeroes their V rows before its P is released (both PV MMAs
+        // of this tile come after that release)
+        if (x == 0 && j == ntiles - 1 && t0 + BN3 > kv_end) {
+          const int sv = Tj % VS;
+          if (!__all_sync(0xffffffffu, mbar_wait(bar(E_VF0 + sv), (Tj / VS) & 1, abort))) {
+            ok = false;
+            break;
+          }
+          if (t0 + r >= kv_end) {
+            uint8_t* vrow = sgen + L::V0 + sv * L::TILE + r * 128;
+#pragma unroll
+            for (int p = 0; p < NP; ++p)
+#pragma unroll
+              for (int c16 = 0; c16 < 8; ++c16)
+                *reinterpret_cast<uint4*>(vrow + p * kPanelBytes + c16 * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();  // the zeroed rows are read by the PV MMA (async proxy)
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(bar_pf));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(bar_pf));
-    }
 
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(bar_o), 0, abort));
-    tc_fence_after();
-    if (ok) {
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(bar_o), act & 1, abort));
+      if (!ok) break;
+      tc_fence_after();
       const float inv = 1.f / l_run;
-      char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
+      char* orow = a.out + t.b * a.os_b + t.h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -1377,8 +1485,16 @@ __global__ void __launch_bounds__(kThreads3, 1)
       if (row_ok && a.lse) {
         const float v =
             (m_run == neg_inf() || l_run == 0.f) ? neg_inf() : (m_run + __log2f(l_run)) * 0.6931471805599453f;
-        a.lse[b * a.ls_b + h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;
+        a.lse[t.b * a.ls_b + t.h * a.ls_h + g * a.ls_g + (int64_t)s * a.ls_s] = v;
       }
+      if (ntiles > 0) {
+        // O_x has been read: the next unit's first PV may overwrite it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(bar_oe));
+        ++act;
+      }
+      T += ntiles;
     }
   }
 
@@ -1400,6 +1516,7 @@ __global__ void __launch_bounds__(256) prefill_schedule_kernel(const int32_t* se
                                                                int causal, int* work) {
   extern __shared__ int cost[];
   const int n = B * q_tiles;
+  if (threadIdx.x == 0) work[n] = 0;  // unit counter of a persistent launch
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int b = i / q_tiles, t = i - b * q_tiles;
     const int off = max(0, seq[b * seq_stride]);
@@ -1523,6 +1640,19 @@ int launch_tc2_any(const TcLaunch& Lc, cudaStream_t st) {
   return Lc.bf16 ? launch_tc2<64, true>(Lc, st) : launch_tc2<64, false>(Lc, st);
 }
 
+// Streaming multiprocessors of the current device (looked up once per device).
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
 template <int D, bool BF16, int POLY>
 int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
   using SL = SmemLayout3<D>;
@@ -1539,7 +1669,10 @@ int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
     return RBLN_ERR_LAUNCH;
   const long long n = (long long)Lc.a.q_tiles * Lc.a.B * Lc.a.Hkv;
   if (n > 2147483647LL) return RBLN_ERR_UNSUPPORTED;
-  attn_fwd_tc3_kernel<D, BF16, POLY><<<(unsigned)n, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a);
+  // persistent: one CTA per SM, each striding through the units
+  const int grid = (int)std::min<long long>(n, sm_count());
+  if (grid == 0) return RBLN_OK;
+  attn_fwd_tc3_kernel<D, BF16, POLY><<<grid, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -1623,7 +1756,7 @@ int prefill_ws_bytes(const rbln_paged_attn_params_t* p) {
   if (!p || p->group <= 0 || p->group > BM || p->batch <= 0 || p->q_len <= 0) return 0;
   const int QT = BM / p->group;
   const long long n = (long long)p->batch * ((p->q_len + 2 * QT - 1) / (2 * QT));
-  return n <= kMaxScheduledItems ? (int)(n * sizeof(int)) : 0;
+  return n <= kMaxScheduledItems ? (int)((n + 1) * sizeof(int)) : 0;  // items, then the unit counter
 }
 
 int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_mask_op) {
@@ -1736,11 +1869,12 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.err = p->error_flags;
   if (two_tile && p->workspace) {
     const int n = p->batch * a.q_tiles;
-    if (n <= kMaxScheduledItems && p->workspace_bytes >= (size_t)n * sizeof(int)) {
+    if (n <= kMaxScheduledItems && p->workspace_bytes >= (size_t)(n + 1) * sizeof(int)) {
       prefill_schedule_kernel<<<1, 256, n * sizeof(int), st>>>(p->seq, p->seq_stride, p->batch, a.q_tiles, p->q_len,
                                                                2 * QT, (int)span64, p->causal, (int*)p->workspace);
       if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
       a.work = static_cast<const int*>(p->workspace);
+      a.counter = static_cast<int*>(p->workspace) + n;
     }
   }
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);

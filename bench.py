@@ -60,7 +60,8 @@ WORKLOADS = {
     # profiling case for ncu --set full: inputs still larger than L2, ~0.35 GB on the device
     "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
                          B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False),
-    # long context, KV heads sharded over the ranks + one NCCL all-gather of head outputs
+    # long context, KV heads sharded over the ranks; each rank's kernels store its heads'
+    # outputs into every rank's output buffer over NVLink (no separate all-gather)
     # profiling case for the fp8 path (~0.6 GB of fp8 KV on the device)
     "decode_fp8_small": dict(desc="paged decode fp8-e4m3 KV B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
                              B=64, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
@@ -237,14 +238,24 @@ def run_ours(args, wl_name):
     nbytes = decode_bytes(d)
     ops = torch.ops.rbln_custom_ops
 
+    peer = None
+    if head_shard:
+        # every rank's full output buffers, written by all ranks' kernels over NVLink
+        peer = sharding.PeerHeadOutput((q.shape[0], q.shape[1] * ws) + tuple(q.shape[2:]), q.dtype, rank, ws)
+        head0 = rank * q.shape[1]
+        e2e_ws = {}
+
     def op_call(qq, kk, vv, ss, bb):
         if d["fp8"]:
             return ops.paged_causal_attn_decode_kvfp8(qq, kk, vv, kc, vc, ks, vs, ss, scale_t, bb, d["bs"])
-        o = ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
-        return sharding.all_gather_heads(o, ws) if head_shard else o
+        if head_shard:
+            return sharding.head_sharded_paged_decode_p2p(qq, kk, vv, kc, vc, ss, d["scale"], bb, d["bs"], peer,
+                                                          workspace=e2e_ws, q_is_local=True)
+        return ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
 
     # C-ABI parameter block with the timing hook around the main kernel
-    p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs)
+    p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs,
+                                out=peer.outputs[0] if head_shard else None)
     cabi.attach_workspace(p, dev, keep)
     L = cabi.lib()
     stream = torch.cuda.current_stream(dev)
@@ -258,11 +269,15 @@ def run_ours(args, wl_name):
     def cabi_step(ev0=None, ev1=None):
         p.prof_events[0] = ev0.cuda_event if ev0 is not None else None
         p.prof_events[1] = ev1.cuda_event if ev1 is not None else None
-        rc = entry(pref, sh)
+        if head_shard:
+            # decode of the local heads, outputs stored into every rank's buffer, epoch exchange
+            out, po = peer.next(head0)
+            p.out = out.data_ptr()
+            rc = L.rbln_paged_causal_attn_decode_peers(pref, ctypes.byref(po), sh)
+        else:
+            rc = entry(pref, sh)
         if rc != 0:
             raise RuntimeError(f"rbln_paged_causal_attn_decode failed: {rc}")
-        if head_shard:
-            sharding.all_gather_heads(keep["out"], ws)
 
     for _ in range(args.warmup):
         cabi_step()
@@ -340,7 +355,7 @@ def run_ours(args, wl_name):
         "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
         "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
         "config": {"workload": WORKLOADS[wl_name]["desc"], "global_batch": d["B"] if head_shard else d["B"] * ws,
-                   "parallelism": (f"kv-head-sharded x{ws} + NCCL all-gather of head outputs" if head_shard
+                   "parallelism": (f"kv-head-sharded x{ws}, head outputs stored into every rank's buffer by the decode kernels (NVLink P2P) + epoch barrier" if head_shard
                                    else f"batch-sharded x{ws}"),
                    "l2": "inputs larger than L2 (KV pool " + f"{kc.numel() * kc.element_size() * 2 / 1e9:.2f} GB)",
                    "bytes_per_step_per_gpu": nbytes},
@@ -362,6 +377,10 @@ def run_ours(args, wl_name):
         line["cpu_baseline"] = cpu_baseline(wl_name, d, budget_s=args.cpu_budget)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()  # every rank is past its last call before any buffer is unmapped
+    if peer is not None:
+        peer.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -218,6 +218,45 @@ int rbln_sdpa_fwd(const rbln_sdpa_params_t* p, cudaStream_t stream);
 #define RBLN_NOALLOC_SCRATCH_BYTES (16u << 20)
 int rbln_paged_causal_attn_decode_noalloc(const rbln_paged_attn_params_t* p, cudaStream_t stream);
 
+/* ---- KV-head-sharded decode with the head outputs written over NVLink ----
+ * No counterpart in the reference's C++ (its only collective is an
+ * all-gather through ProcessGroupRBLN, torch_rbln/csrc/distributed/c10d/rbln/
+ * ProcessGroupRBLN.cpp:754-830): one process per GPU owns a slice of the KV
+ * heads, and the decode kernels store each final head output straight into
+ * every rank's full output buffer (peer memory mapped with CUDA IPC), then a
+ * one-warp kernel exchanges a per-call epoch through every rank's flag array
+ * and waits (bounded, RBLN_DEVERR_TIMEOUT on expiry) until all ranks' writes
+ * are in. This replaces the decode + all-gather + re-layout copy. */
+#define RBLN_IPC_HANDLE_BYTES 64
+typedef struct rbln_peer_out {
+  void* const* out;       /* device array [n]: every rank's full output buffer, mapped on this GPU */
+  uint32_t* const* flags; /* device array [n]: every rank's flag array (n uint32), mapped on this GPU */
+  int32_t n;              /* ranks */
+  int32_t rank;           /* this rank */
+  int32_t head0;          /* first KV head of this rank in the full output */
+  uint32_t epoch;         /* this call's epoch; strictly increasing over calls (flags start at 0) */
+} rbln_peer_out_t;
+
+/* Device memory that other processes can map: cudaMalloc of `bytes` (zeroed)
+ * and its IPC handle (RBLN_IPC_HANDLE_BYTES bytes). Free with rbln_ipc_free. */
+int rbln_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int rbln_ipc_free(void* ptr);
+/* Maps another process's rbln_ipc_alloc buffer into this process (current
+ * device; peer access enabled lazily). Unmap with rbln_ipc_close. */
+int rbln_ipc_open(const void* handle, void** ptr);
+int rbln_ipc_close(void* ptr);
+
+/* rbln_paged_causal_attn_decode on this rank's KV heads (p describes the
+ * local heads: num_kv_heads, q, k/v, caches), with the output of local head
+ * h written to head peers->head0 + h of every rank's full output buffer;
+ * p->out must be this rank's own full buffer and p->out_stride its strides
+ * (all ranks' buffers have the same layout). When the stream reaches the end
+ * of this call, every rank's buffer holds all heads of this epoch (no host
+ * synchronisation). Buffers reused across calls must alternate (at least two
+ * per rank): a rank may run one call ahead of the others. */
+int rbln_paged_causal_attn_decode_peers(const rbln_paged_attn_params_t* p, const rbln_peer_out_t* peers,
+                                        cudaStream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

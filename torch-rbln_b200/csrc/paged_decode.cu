@@ -41,6 +41,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -97,10 +98,26 @@ struct DecodeArgs {
   float* part_o;    // (.., D) floats per slot
   float* part_lse;  // log2-sum-exp per slot
   uint32_t* err;
+  // head-sharded multi-GPU decode: final outputs go to every rank's buffer
+  char* const* out_peers;  // nullptr: write `out` only
+  int n_peers;
+  int head0;  // first head of this rank in the full output
 };
 
 __device__ __forceinline__ void flag_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
+}
+
+// Stores 4 output elements (one 8-byte pair of pairs) of (b, local head h,
+// query head g, column d4): to `out`, or to every rank's buffer when the
+// heads are sharded over GPUs.
+__device__ __forceinline__ void store_out(const DecodeArgs& a, int b, int h, int g, int d4, uint2 v) {
+  const int64_t off = b * a.os_b + (int64_t)(a.head0 + h) * a.os_h + (int64_t)g * a.os_g + d4 * 2;
+  if (a.out_peers == nullptr) {
+    *reinterpret_cast<uint2*>(a.out + off) = v;
+  } else {
+    for (int r = 0; r < a.n_peers; ++r) *reinterpret_cast<uint2*>(a.out_peers[r] + off) = v;
+  }
 }
 
 // Context length seen by sequence b, and the number of splits covering it.
@@ -503,14 +520,14 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
     const float inv = 1.f / Lsum;
     acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
     if (final_out) {
-      char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
+      store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w)));
     } else {
       const int64_t ps = slot + g;
       *reinterpret_cast<float4*>(a.part_o + ps * D + d4) = acc;
       if (d4 == 0) a.part_lse[ps] = (M == neg_inf()) ? neg_inf() : M + __log2f(Lsum);
     }
   }
+  if (a.out_peers && final_out) __threadfence_system();  // peer stores before the epoch exchange
   __syncthreads();  // the combine area is reused by the CTA's next segment
 }
 
@@ -651,9 +668,9 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h
     float inv = s_inv[g];
     if (inv == 0.f) inv = pos_nan();  // every position masked: NaN, as softmax of all -inf
     acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
-    char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
-    *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w));
+    store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w)));
   }
+  if (a.out_peers) __threadfence_system();  // peer stores visible before the epoch exchange
 }
 
 // Combines the per-split partials of one (sequence, KV head) of the
@@ -686,9 +703,9 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
     for (int idx = threadIdx.x; idx < a.G * (D / 4); idx += kThreads) {
       const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
       const float n = pos_nan();
-      char* dst = a.out + b * a.os_b + h * a.os_h + (int64_t)g * a.os_g + d4 * 2;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n));
+      store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n)));
     }
+    if (a.out_peers) __threadfence_system();
     return;
   }
   const int W = a.prefix[a.B + 1];
@@ -696,6 +713,30 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
   if (cf == cl) return;  // one chunk held the whole sequence and wrote the output
   extern __shared__ float sw[];
   merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw);
+}
+
+// Epoch exchange after a head-sharded decode (one warp): thread t announces
+// to rank t that this rank's output stores are done (release at system
+// scope; they were made by earlier kernels of this stream), then waits until
+// rank t has announced this epoch to this rank (acquire). Waits give up after
+// about 2 s of SM clock with RBLN_DEVERR_TIMEOUT.
+constexpr long long kPeerWaitLimitCycles = 4000000000LL;
+__global__ void __launch_bounds__(32) peer_epoch_barrier_kernel(uint32_t* const* flags, int n, int rank,
+                                                                uint32_t epoch, uint32_t* err) {
+  const int t = threadIdx.x;
+  if (t >= n) return;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags[t] + rank), "r"(epoch) : "memory");
+  const uint32_t* mine = flags[rank] + t;
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if ((int32_t)(v - epoch) >= 0) break;  // a rank may already be one epoch ahead
+    if (clock64() - t0 > kPeerWaitLimitCycles) {
+      flag_error(err, RBLN_DEVERR_TIMEOUT);
+      break;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -900,7 +941,8 @@ int launch_d(const DecodeArgs& a, const Plan& pl, int kv_dt, int q_dt, cudaStrea
   return RBLN_ERR_UNSUPPORTED;
 }
 
-int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_mask) {
+int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_mask,
+               const rbln_peer_out_t* peers = nullptr) {
   Plan pl;
   int rc = plan_decode(p, &pl);
   if (rc != RBLN_OK) return rc;
@@ -972,8 +1014,19 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
     a.part_lse = a.part_o + slots * p->head_dim;
   }
   a.err = p->error_flags;
-  if (p->head_dim == 128) return launch_d<128>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
-  return launch_d<64>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
+  if (peers) {
+    if (peers->n < 1 || peers->n > 32 || peers->rank < 0 || peers->rank >= peers->n || peers->head0 < 0 ||
+        !peers->out || !peers->flags)
+      return RBLN_ERR_INVALID_ARGUMENT;
+    a.out_peers = reinterpret_cast<char* const*>(peers->out);
+    a.n_peers = peers->n;
+    a.head0 = peers->head0;
+  }
+  const int lrc = p->head_dim == 128 ? launch_d<128>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events)
+                                     : launch_d<64>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
+  if (lrc != RBLN_OK || !peers) return lrc;
+  peer_epoch_barrier_kernel<<<1, 32, 0, st>>>(peers->flags, peers->n, peers->rank, peers->epoch, p->error_flags);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -1001,6 +1054,38 @@ int rbln_paged_causal_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_
 int rbln_paged_attn_decode(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
   return rbln::run_decode(p, stream, /*require_mask=*/true);
 }
+
+int rbln_paged_causal_attn_decode_peers(const rbln_paged_attn_params_t* p, const rbln_peer_out_t* peers,
+                                        cudaStream_t stream) {
+  if (!peers) return RBLN_ERR_INVALID_ARGUMENT;
+  return rbln::run_decode(p, stream, /*require_mask=*/false, peers);
+}
+
+int rbln_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return RBLN_ERR_INVALID_ARGUMENT;
+  void* d = nullptr;
+  if (cudaMalloc(&d, bytes) != cudaSuccess) return RBLN_ERR_LAUNCH;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(d, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, d) != cudaSuccess) {
+    cudaFree(d);
+    return RBLN_ERR_LAUNCH;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == RBLN_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = d;
+  return RBLN_OK;
+}
+
+int rbln_ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH; }
+
+int rbln_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return RBLN_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+int rbln_ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH; }
 
 namespace {
 constexpr int kNoallocMaxDevices = 64;

@@ -79,6 +79,14 @@ class SdpaParams(ctypes.Structure):
     ]
 
 
+class PeerOut(ctypes.Structure):
+    """rbln_peer_out_t: every rank's output buffer and flag array, as mapped on this GPU."""
+    _fields_ = [("out", c_vp), ("flags", c_vp), ("n", c_i32), ("rank", c_i32), ("head0", c_i32),
+                ("epoch", ctypes.c_uint32)]
+
+
+IPC_HANDLE_BYTES = 64
+
 # entry points: (name, restype, argtypes)
 ENTRY_POINTS = {
     "rbln_attn_abi_version": (ctypes.c_int, []),
@@ -92,6 +100,12 @@ ENTRY_POINTS = {
     "rbln_paged_causal_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_sdpa_fwd": (ctypes.c_int, [ctypes.POINTER(SdpaParams), c_vp]),
+    "rbln_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(c_vp), c_vp]),
+    "rbln_ipc_free": (ctypes.c_int, [c_vp]),
+    "rbln_ipc_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "rbln_ipc_close": (ctypes.c_int, [c_vp]),
+    "rbln_paged_causal_attn_decode_peers": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams),
+                                                           ctypes.POINTER(PeerOut), c_vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

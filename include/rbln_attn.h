@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define RBLN_ATTN_ABI_VERSION 1
+#define RBLN_ATTN_ABI_VERSION 2
 
 typedef enum {
   RBLN_OK = 0,
@@ -122,6 +122,13 @@ typedef struct {
   /* optional cudaEvent_t pair recorded on `stream` right before and right
    * after the main attention kernel (measurement hook; NULL = none) */
   void* prof_events[2];
+  /* optional attention-sink logits, fp32 [num_kv_heads * group] (index
+   * h * group + g), in the units of scale * q.k: each query head's softmax
+   * gets one extra term exp(sink) that carries no value row, so
+   * out = sum_i e^{s_i} v_i / (sum_i e^{s_i} + e^{sink}). NULL = none.
+   * Schema argument `sinks` of flash_attention_naive_{prefill,decode}
+   * (torch_rbln/_internal/register_custom_ops.py:453-560). */
+  const float* sinks;
 } rbln_paged_attn_params_t;
 
 /* ABI checks for foreign-function bindings. */

@@ -12,6 +12,9 @@ mock implementations" of optimum-rbln's operators):
   paged_attn_decode          test_custom_kernel.py:138-216
   paged_causal_attn_prefill  test_custom_kernel.py:262-343
   paged_causal_attn_decode   test_custom_kernel.py:388-486
+  flash_attention_naive_{prefill,decode}
+                             test_custom_kernel.py:546-645 (unified cache
+                             kv_cache[0] = K pool, kv_cache[1] = V pool)
 
 The reference's CPU definitions only cover one physical block per sequence
 (prefill always uses block 0, decode uses kcache[b]; block_table and
@@ -99,12 +102,18 @@ def _gather(cache, block_table, b, span, block_size, D, scale=None):
     return rows.permute(1, 0, 2), ok
 
 
-def _attend(q, K, V, keep, scale, mode):
+def _attend(q, K, V, keep, scale, mode, sinks=None):
     """softmax(q.K^T * scale | keep) . V for one sequence.
 
     q [Hkv, G, S, D], K/V [Hkv, T, D], keep [S, T] bool -> [Hkv, G, S, D].
+    sinks [Hkv * G] (fp32 mode only): one extra logit per query head that
+    joins the softmax and carries no value row (the attention-sink form,
+    out = sum_t e^{w_t} V_t / (sum_t e^{w_t} + e^{sink})).
     """
     if mode == "mock":
+        # the reference's CPU definitions take `sinks` but do not read it
+        # (test_custom_kernel.py:589-594)
+        assert sinks is None, "mode='mock' follows the reference, which ignores sinks"
         dt = q.dtype
         Kc, Vc = K.to(dt), V.to(dt)
         # matmul in q.dtype, then `* scale` (test_custom_kernel.py:87,199)
@@ -116,13 +125,18 @@ def _attend(q, K, V, keep, scale, mode):
     qf, Kf, Vf = q.float(), K.float(), V.float()
     w = torch.matmul(qf, Kf.unsqueeze(1).transpose(-1, -2)) * float(scale)
     w = w.masked_fill(~keep, -float("inf"))
-    p = torch.softmax(w, dim=-1)
+    if sinks is not None:
+        Hkv, G, S = w.shape[:3]
+        sk = sinks.float().reshape(Hkv, G, 1, 1).expand(Hkv, G, S, 1)
+        p = torch.softmax(torch.cat([w, sk], dim=-1), dim=-1)[..., :-1]
+    else:
+        p = torch.softmax(w, dim=-1)
     return torch.matmul(p, Vf.unsqueeze(1))
 
 
 def paged_decode(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
                  mask: Optional[torch.Tensor] = None, *, k_scale=None, v_scale=None,
-                 mode: str = "fp32") -> torch.Tensor:
+                 mode: str = "fp32", sinks: Optional[torch.Tensor] = None) -> torch.Tensor:
     """paged_causal_attn_decode (mask=None or [B, L]) / paged_attn_decode (mask [B,1,1,1,L]).
 
     Mutates kcache/vcache. Returns [B, Hkv, G, 1, D] in q.dtype (mode="mock")
@@ -150,14 +164,15 @@ def paged_decode(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
             L = min(p + 1, span) if p >= 0 else 0
             keep = t < L
         keep = (keep & okk).reshape(1, span)
-        outs.append(_attend(q[b], K, V, keep, scale, mode))
+        outs.append(_attend(q[b], K, V, keep, scale, mode, sinks))
     out = torch.stack(outs, 0)
     return out if mode == "mock" else out.float()
 
 
 def paged_prefill(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
                   mask: Optional[torch.Tensor] = None, *, causal: bool = True,
-                  position_mask: Optional[torch.Tensor] = None, mode: str = "fp32") -> torch.Tensor:
+                  position_mask: Optional[torch.Tensor] = None, mode: str = "fp32",
+                  sinks: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Chunked prefill over a paged cache.
 
     paged_attn_prefill:        mask = keep-mask [B|1, 1, 1, S_q, L], causal ignored.
@@ -194,9 +209,33 @@ def paged_prefill(q, k, v, kcache, vcache, seq, scale, block_table, block_size,
             pk[:L] = pm[:L] > 0
             keep = keep & pk.reshape(1, span)
         keep = keep & okk.reshape(1, span)
-        outs.append(_attend(q[b], K, V, keep, scale, mode))
+        outs.append(_attend(q[b], K, V, keep, scale, mode, sinks))
     out = torch.stack(outs, 0)
     return out if mode == "mock" else out.float()
+
+
+def flash_attention_naive(q, k, v, kv_cache, mask, scale, seq_idx, block_tables,
+                          sinks: Optional[torch.Tensor] = None, *, decode: bool,
+                          mode: str = "fp32") -> torch.Tensor:
+    """flash_attention_naive_prefill (decode=False) / _decode (decode=True).
+
+    The reference's CPU definition (test_custom_kernel.py:546-573) handles a
+    single partition: it writes k/v into block block_tables[0] at offset
+    seq_idx[0][0] of both halves of kv_cache, then attends over the
+    partition's positions under `mask[..., :partition] > 0` (fp32 softmax,
+    probabilities rounded to q.dtype). The general form is the keep-mask
+    paged op over kv_cache[0] / kv_cache[1] with block_size = partition and
+    seq = seq_idx[:, 0]; on a single partition the two coincide op for op.
+    Mutates kv_cache.
+    """
+    block_size = kv_cache.shape[-2]
+    seq = seq_idx.reshape(seq_idx.shape[0], -1)[:, 0] if seq_idx.dim() > 0 else seq_idx.reshape(1)
+    kc, vc = kv_cache[0], kv_cache[1]
+    if decode:
+        return paged_decode(q, k, v, kc, vc, seq, scale, block_tables, block_size, mask=mask,
+                            mode=mode, sinks=sinks)
+    return paged_prefill(q, k, v, kc, vc, seq, scale, block_tables, block_size, mask=mask,
+                         mode=mode, sinks=sinks)
 
 
 def contiguous_cache(kcache, block_table, block_size, b, D, scale=None):

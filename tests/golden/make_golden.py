@@ -6,7 +6,8 @@ run the tests):
     python tests/golden/make_golden.py --reference /root/reference
 
 Sources executed:
-  * the reference's CPU definitions of the paged ops,
+  * the reference's CPU definitions of the paged ops and of
+    flash_attention_naive_{prefill,decode},
     test/rbln/test_custom_kernel.py lines 1-646 (the module-level
     torch.library.custom_op definitions), executed without their
     `torch.testing._internal` import (it needs `expecttest`, absent here);
@@ -170,6 +171,45 @@ def run_prefill(case):
     return res
 
 
+def naive_cases(gen):
+    """flash_attention_naive_{prefill,decode} on one partition, as
+    test_custom_kernel.py:1003-1093 runs them (kv_cache [2, 1, Hkv, 1, P, D]
+    of random values, keep-mask over [0, valid_len)), with the heads and the
+    partition scaled down, plus a chunk at a nonzero offset with a causal
+    keep-mask (prefill) and a longer history (decode)."""
+    out = []
+    Hkv, G, P = 1, 4, 64
+    for dtype, D in ((torch.float16, 64), (torch.float16, 128), (torch.bfloat16, 64), (torch.float32, 64)):
+        for name, decode, S, s0, causal in (("prefill", False, P, 0, False),
+                                            ("prefill_offset", False, 40, 24, True),
+                                            ("decode", True, 1, 32, False),
+                                            ("decode_long", True, 1, 50, False)):
+            q = torch.randn([1, Hkv, G, S, D], generator=gen).to(dtype)
+            k = torch.randn([1, Hkv, 1, S, D], generator=gen).to(dtype)
+            v = torch.randn([1, Hkv, 1, S, D], generator=gen).to(dtype)
+            kv = torch.randn([2, 1, Hkv, 1, P, D], generator=gen).to(dtype)
+            mask = torch.zeros([1, 1, 1, S, P], dtype=dtype)
+            if causal:
+                mask[0, 0, 0] = torch.ones([S, P], dtype=dtype).tril(diagonal=s0)
+            else:
+                mask[..., : s0 + S] = 1
+            out.append(dict(name=name, decode=decode, dtype=dtype, D=D, Hkv=Hkv, G=G, P=P, S=S, s0=s0,
+                            q=q, k=k, v=v, kv_cache=kv, mask=mask))
+    return out
+
+
+def run_naive(case):
+    ops = torch.ops.rbln_custom_ops
+    kv = case["kv_cache"].clone()
+    scale = torch.tensor(1.0 / math.sqrt(case["D"]))
+    seq_idx = torch.tensor([[case["s0"]]], dtype=torch.int32)
+    bt = torch.tensor([[0]], dtype=torch.int16) if case["decode"] else torch.tensor([0], dtype=torch.int16)
+    slots = torch.arange(case["S"], dtype=torch.int32)
+    op = ops.flash_attention_naive_decode if case["decode"] else ops.flash_attention_naive_prefill
+    o = op(case["q"], case["k"], case["v"], kv, case["mask"], scale, seq_idx, bt, slots)
+    return dict(out=o, kv_cache=sha(kv))
+
+
 def sdpa_cases(gen, fallback):
     cases = []
     for dtype in (torch.float32, torch.float16, torch.bfloat16):
@@ -219,6 +259,10 @@ def main():
     torch.save(pre, os.path.join(HERE, "paged_prefill.pt"))
     torch.save(sdpa_cases(gen, fallback), os.path.join(HERE, "sdpa_small.pt"))
     torch.save(sdpa_config1(fallback), os.path.join(HERE, "sdpa_config1.pt"))
+    naive = naive_cases(torch.Generator().manual_seed(4321))
+    for c in naive:
+        c["results"] = run_naive(c)
+    torch.save(naive, os.path.join(HERE, "flash_attention_naive.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

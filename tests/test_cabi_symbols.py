@@ -41,7 +41,7 @@ def test_abi_version_and_struct_size():
     from torch_rbln_b200 import cabi
 
     L = cabi.lib()
-    assert L.rbln_attn_abi_version() == 1
+    assert L.rbln_attn_abi_version() == 2
     assert L.rbln_paged_attn_params_sizeof() == ctypes.sizeof(cabi.PagedAttnParams)
 
 
@@ -86,6 +86,20 @@ def test_torch_ops_registered_with_reference_schemas():
     assert str(ops.paged_attn_prefill.default._schema) == (
         "rbln_custom_ops::paged_attn_prefill(Tensor q, Tensor k, Tensor v, Tensor mask, Tensor(a4!) kcache, "
         "Tensor(a5!) vcache, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size) -> Tensor")
+    # test_custom_kernel.py:576-645
+    for name in ("flash_attention_naive_prefill", "flash_attention_naive_decode"):
+        assert str(getattr(ops, name).default._schema) == (
+            f"rbln_custom_ops::{name}(Tensor q, Tensor k, Tensor v, Tensor(a3!) kv_cache, Tensor mask, "
+            "Tensor scale, Tensor seq_idx, Tensor block_tables, Tensor slot_mapping, Tensor? sinks=None) -> Tensor")
+
+
+def test_naive_wrappers_keep_the_argument_count_contract():
+    """register_custom_ops.py:476,534: 9 or 10 inputs, else RuntimeError."""
+    import torch_rbln_b200 as tr
+
+    for fn in (tr.flash_attention_naive_prefill, tr.flash_attention_naive_decode):
+        with pytest.raises(RuntimeError, match="takes 9 or 10 inputs"):
+            fn(*([None] * 8))
 
 
 def test_fake_kernels_give_q_metadata():

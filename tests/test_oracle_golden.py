@@ -202,3 +202,61 @@ def test_contiguous_prefill_restatement_matches_reference(idx):
     out = opa.mock_prefill_contiguous(c["q"], c["k"], c["v"], kc, vc, s1, torch.tensor(1.0 / math.sqrt(D)), mask)
     assert torch.equal(out, exp["out"])
     assert _sha(kc) == exp["kc"] and _sha(vc) == exp["vc"]
+
+
+NAIVE = _load("flash_attention_naive.pt")
+
+
+@pytest.mark.parametrize("idx", range(len(NAIVE)))
+def test_flash_attention_naive_oracle_matches_reference(idx):
+    """flash_attention_naive_{prefill,decode} (test_custom_kernel.py:546-645):
+    the keep-mask paged restatement over kv_cache[0] / kv_cache[1] equals the
+    reference's single-partition definition, output and mutated cache."""
+    c = NAIVE[idx]
+    exp = c["results"]
+    scale = torch.tensor(1.0 / math.sqrt(c["D"]))
+    seq_idx = torch.tensor([[c["s0"]]], dtype=torch.int32)
+    bt = torch.tensor([[0]], dtype=torch.int16) if c["decode"] else torch.tensor([0], dtype=torch.int16)
+    for mode in ("mock", "fp32"):
+        kv = c["kv_cache"].clone()
+        out = opa.flash_attention_naive(c["q"], c["k"], c["v"], kv, c["mask"], scale, seq_idx, bt,
+                                        decode=c["decode"], mode=mode)
+        if mode == "mock":
+            assert out.dtype == exp["out"].dtype and out.shape == exp["out"].shape
+            assert torch.equal(out, exp["out"]), f"max diff {(out.float() - exp['out'].float()).abs().max()}"
+        else:
+            torch.testing.assert_close(out, exp["out"].float(), **_tol(c["dtype"]))
+        assert _sha(kv) == exp["kv_cache"]
+
+
+def test_sinks_oracle_properties():
+    """Attention-sink restatement: a sink of -inf is no sink; a sink is the
+    softmax over the scores plus one extra logit whose column is dropped, so
+    out(sink) = out(no sink) * Z / (Z + e^sink) per query head, Z the sum of
+    e^score over the kept positions."""
+    c = NAIVE[0]
+    scale = 1.0 / math.sqrt(c["D"])
+    seq_idx = torch.tensor([[c["s0"]]], dtype=torch.int32)
+    bt = torch.tensor([0], dtype=torch.int16)
+    H = c["Hkv"] * c["G"]
+    gen = torch.Generator().manual_seed(7)
+    sinks = torch.randn(H, generator=gen) * 2
+
+    def run(s):
+        kv = c["kv_cache"].clone()
+        return opa.flash_attention_naive(c["q"], c["k"], c["v"], kv, c["mask"], scale, seq_idx, bt, s,
+                                         decode=False)
+
+    base = run(None)
+    assert torch.equal(run(torch.full([H], -float("inf"))), base)
+    with_sink = run(sinks)
+    # Z per (head, query row): recompute the scores of the written cache
+    kv = c["kv_cache"].clone()
+    run_kv = opa.flash_attention_naive(c["q"], c["k"], c["v"], kv, c["mask"], scale, seq_idx, bt, decode=False)
+    assert torch.equal(run_kv, base)
+    K = kv[0, 0, :, 0].float()  # [Hkv, P, D]
+    w = torch.matmul(c["q"][0].float(), K.unsqueeze(1).transpose(-1, -2)) * scale  # [Hkv, G, S, P]
+    keep = c["mask"][0, 0, 0] > 0
+    Z = torch.where(keep, w.exp(), torch.zeros_like(w)).sum(-1, keepdim=True)  # [Hkv, G, S, 1]
+    e = sinks.reshape(c["Hkv"], c["G"], 1, 1).exp()
+    torch.testing.assert_close(with_sink[0], base[0] * Z / (Z + e), rtol=1e-5, atol=1e-6)

@@ -87,6 +87,7 @@ struct AttnArgs {
   uint32_t* err;
   const int* work;  // optional: items (b * q_tiles + tile) in launch order, longest first
   int* counter;     // optional: next unit of a persistent launch (zeroed by the schedule pre-pass)
+  const float* sinks;  // optional [Hkv * G] sink logits (natural-log units), index h * G + g; v1 kernel only
 };
 
 __device__ __forceinline__ float mask_value(const void* base, int dt, int64_t i) {
@@ -436,7 +437,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PV), (ntiles - 1) & 1, abort));
     tc_fence_after();
     if (ok) {
-      const float inv = 1.f / l_run;  // l_run == 0 -> inf -> NaN (all keys masked)
+      // l_run == 0 -> inf -> NaN (all keys masked). A sink adds e^{sink - m}
+      // to the denominator only (all keys masked then gives 0).
+      const float inv =
+          1.f / (a.sinks && g < a.G ? l_run + exp2f(a.sinks[h * a.G + g] * kLog2e - m_run) : l_run);
       char* orow = a.out + b * a.os_b + h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -1814,7 +1818,7 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   Lc.D = D;
   Lc.bf16 = p->q_dtype == RBLN_DT_BF16;
   const int mfk = mask_free_kernel();
-  const bool two_tile = !keep_mask_op && !p->mask &&
+  const bool two_tile = !keep_mask_op && !p->mask && !p->sinks &&
                         (mfk == 3 || (bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0));
   const int rpb = std::min(bs, (two_tile && mfk == 2) ? BN2 : BN);
   if (!map_q(&Lc.tq, p->q, p->q_dtype, p->batch, p->num_kv_heads, G, p->q_len, D, p->q_stride, QT))
@@ -1867,6 +1871,7 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.scale = p->scale;
   a.scale_dev = p->scale_dev;
   a.err = p->error_flags;
+  a.sinks = p->sinks;
   if (two_tile && p->workspace) {
     const int n = p->batch * a.q_tiles;
     if (n <= kMaxScheduledItems && p->workspace_bytes >= (size_t)(n + 1) * sizeof(int)) {

@@ -102,7 +102,14 @@ struct DecodeArgs {
   char* const* out_peers;  // nullptr: write `out` only
   int n_peers;
   int head0;  // first head of this rank in the full output
+  const float* sinks;  // optional [Hkv * G] sink logits (natural-log units), index h * G + g
 };
+
+// Sink logit of local query head (h, g) in the log2 domain of the scores,
+// or -inf when there are no sinks.
+__device__ __forceinline__ float sink_log2(const DecodeArgs& a, int h, int g) {
+  return a.sinks ? a.sinks[h * a.G + g] * kLog2e : neg_inf();
+}
 
 __device__ __forceinline__ void flag_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
@@ -517,11 +524,15 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
       const float4 o = *reinterpret_cast<const float4*>(&sO[w][g][d4]);
       acc.x += f * o.x; acc.y += f * o.y; acc.z += f * o.z; acc.w += f * o.w;
     }
-    const float inv = 1.f / Lsum;
-    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
     if (final_out) {
+      // the sink adds e^{sink - M} to the denominator only; all positions
+      // masked (M = -inf) then gives 0, and NaN without a sink
+      const float inv = 1.f / (a.sinks ? Lsum + exp2f(sink_log2(a, h, g) - M) : Lsum);
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
       store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w)));
     } else {
+      const float inv = 1.f / Lsum;
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
       const int64_t ps = slot + g;
       *reinterpret_cast<float4*>(a.part_o + ps * D + d4) = acc;
       if (d4 == 0) a.part_lse[ps] = (M == neg_inf()) ? neg_inf() : M + __log2f(Lsum);
@@ -643,7 +654,9 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h
     for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, a.part_lse[(base + s) * a.G + g]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float S = 0.f;
+    const float sk = sink_log2(a, h, g);
+    M = fmaxf(M, sk);
+    float S = (lane == 0 && sk != neg_inf()) ? exp2f(sk - M) : 0.f;
     for (int s = lane; s < nsplit; s += 32) {
       const float l = a.part_lse[(base + s) * a.G + g];
       const float w = (l == neg_inf()) ? 0.f : exp2_approx(l - M);
@@ -702,7 +715,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
     if (a.k_new != nullptr && pos >= 0 && pos < a.span) append_token<D, KV, Q_BF16>(a, b, h, pos);
     for (int idx = threadIdx.x; idx < a.G * (D / 4); idx += kThreads) {
       const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
-      const float n = pos_nan();
+      const float n = a.sinks ? 0.f : pos_nan();  // all softmax mass on the sink
       store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n)));
     }
     if (a.out_peers) __threadfence_system();
@@ -1014,6 +1027,7 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
     a.part_lse = a.part_o + slots * p->head_dim;
   }
   a.err = p->error_flags;
+  a.sinks = p->sinks;
   if (peers) {
     if (peers->n < 1 || peers->n > 32 || peers->rank < 0 || peers->rank >= peers->n || peers->head0 < 0 ||
         !peers->out || !peers->flags)

@@ -1,6 +1,6 @@
 // PyTorch operator layer: defines the rbln_custom_ops schemas (identical to
 // the ones the reference's torch.library.custom_op definitions generate,
-// test/rbln/test_custom_kernel.py:31-486) and registers CUDA kernels that
+// test/rbln/test_custom_kernel.py:31-486, 576-645) and registers CUDA kernels that
 // validate the tensors, allocate the output and scratch from the PyTorch
 // caching allocator, and call the C-ABI entry points of librbln_attn.
 //
@@ -68,7 +68,7 @@ at::Tensor on_device(const at::Tensor& t, const at::Tensor& like) {
 }
 
 struct Common {
-  at::Tensor q, k, v, seq, bt, mask, scale_dev, out, err;
+  at::Tensor q, k, v, seq, bt, mask, scale_dev, out, err, sinks;
   rbln_paged_attn_params_t p{};
 };
 
@@ -305,6 +305,69 @@ at::Tensor paged_causal_attn_prefill_cuda(const at::Tensor& q, const at::Tensor&
 }
 
 // ---------------------------------------------------------------------------
+// flash_attention_naive_{prefill,decode}: the unified-cache form of the paged
+// ops (torch_rbln/_internal/register_custom_ops.py:453-560; CPU semantics in
+// test/rbln/test_custom_kernel.py:546-573). kv_cache [2, num_blocks, Hkv, 1,
+// P, D] stacks the K pool (index 0) and the V pool (index 1), each block one
+// partition of P tokens; block_tables lists a sequence's partitions (1-D for
+// prefill, [B, NP] for decode); seq_idx [B, 1] is the position of the first
+// new token; mask is a keep-mask over partition positions. The new rows are
+// written at seq_idx through the block table and attention runs over the
+// mask's positions: the keep-mask paged path on kv_cache[0] / kv_cache[1].
+// slot_mapping is accepted for the schema and not read (the positions follow
+// from seq_idx and block_tables, as in the reference's CPU semantics).
+// sinks [Hkv * G] (any float dtype) are per-query-head sink logits.
+// ---------------------------------------------------------------------------
+at::Tensor flash_attention_naive(const char* op, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                 at::Tensor& kv_cache, const at::Tensor& mask, const at::Tensor& scale,
+                                 const at::Tensor& seq_idx, const at::Tensor& block_tables,
+                                 const at::Tensor& slot_mapping, const std::optional<at::Tensor>& sinks,
+                                 bool decode) {
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(0) == 2, op,
+              ": kv_cache must be [2, num_blocks, Hkv, 1, partition, D], got ", kv_cache.sizes());
+  TORCH_CHECK(kv_cache.size(-1) % 64 == 0, op,
+              ": The last dimension of kv_cache must be a multiple of 64, but got shape ", kv_cache.sizes());
+  TORCH_CHECK(kv_cache.scalar_type() == q.scalar_type(), op, ": kv_cache dtype must equal q dtype");
+  if (!decode)
+    for (const at::Tensor* t : {&q, &k, &v})
+      TORCH_CHECK(t->dim() >= 1 && t->size(0) == 1, op, " batch size of q/k/v must be 1, but got shape ",
+                  t->sizes());
+  TORCH_CHECK(slot_mapping.defined(), op, ": slot_mapping is required");
+  at::Tensor kcache = kv_cache.select(0, 0);
+  at::Tensor vcache = kv_cache.select(0, 1);
+  // seq_idx [B, 1] (or [B]): one start position per sequence
+  const at::Tensor seq = seq_idx.dim() == 2 ? seq_idx.select(1, 0) : seq_idx;
+  Common c;
+  fill_paged(c, op, q, k, v, kcache, vcache, seq, scale, block_tables, kv_cache.size(-2), mask, decode);
+  if (sinks.has_value() && sinks->defined()) {
+    TORCH_CHECK(at::isFloatingType(sinks->scalar_type()), op, ": sinks must be floating point");
+    TORCH_CHECK(sinks->numel() == (int64_t)c.p.num_kv_heads * c.p.group, op, ": sinks must hold one logit per ",
+                "query head (", c.p.num_kv_heads * c.p.group, "), got ", sinks->sizes());
+    c.sinks = on_device(*sinks, c.q).to(at::kFloat).contiguous();
+    c.p.sinks = c.sinks.data_ptr<float>();
+  }
+  return decode ? run_decode(c, kcache, op, true) : run_prefill(c, op, true);
+}
+
+at::Tensor flash_attention_naive_prefill_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                              at::Tensor& kv_cache, const at::Tensor& mask, const at::Tensor& scale,
+                                              const at::Tensor& seq_idx, const at::Tensor& block_tables,
+                                              const at::Tensor& slot_mapping,
+                                              const std::optional<at::Tensor>& sinks) {
+  return flash_attention_naive("flash_attention_naive_prefill", q, k, v, kv_cache, mask, scale, seq_idx,
+                               block_tables, slot_mapping, sinks, false);
+}
+
+at::Tensor flash_attention_naive_decode_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                             at::Tensor& kv_cache, const at::Tensor& mask, const at::Tensor& scale,
+                                             const at::Tensor& seq_idx, const at::Tensor& block_tables,
+                                             const at::Tensor& slot_mapping,
+                                             const std::optional<at::Tensor>& sinks) {
+  return flash_attention_naive("flash_attention_naive_decode", q, k, v, kv_cache, mask, scale, seq_idx,
+                               block_tables, slot_mapping, sinks, true);
+}
+
+// ---------------------------------------------------------------------------
 // SDPA: aten::_scaled_dot_product_fused_attention_overrideable on CUDA, and
 // the backend choice that routes F.scaled_dot_product_attention to it
 // (mirrors _fused_sdp_choice_privateuse1, aten/src/ATen/native/
@@ -484,6 +547,12 @@ TORCH_LIBRARY(rbln_custom_ops, m) {
       "paged_causal_attn_decode_kvfp8(Tensor q, Tensor k, Tensor v, Tensor(a3!) kcache, Tensor(a4!) vcache, "
       "Tensor k_scale, Tensor v_scale, Tensor seq, Tensor scale, Tensor block_table, SymInt block_size, "
       "Tensor? mask=None) -> Tensor");
+  m.def(
+      "flash_attention_naive_prefill(Tensor q, Tensor k, Tensor v, Tensor(a3!) kv_cache, Tensor mask, "
+      "Tensor scale, Tensor seq_idx, Tensor block_tables, Tensor slot_mapping, Tensor? sinks=None) -> Tensor");
+  m.def(
+      "flash_attention_naive_decode(Tensor q, Tensor k, Tensor v, Tensor(a3!) kv_cache, Tensor mask, "
+      "Tensor scale, Tensor seq_idx, Tensor block_tables, Tensor slot_mapping, Tensor? sinks=None) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(rbln_custom_ops, CUDA, m) {
@@ -492,4 +561,6 @@ TORCH_LIBRARY_IMPL(rbln_custom_ops, CUDA, m) {
   m.impl("paged_attn_decode", &paged_attn_decode_cuda);
   m.impl("paged_causal_attn_decode", &paged_causal_attn_decode_cuda);
   m.impl("paged_causal_attn_decode_kvfp8", &paged_causal_attn_decode_kvfp8_cuda);
+  m.impl("flash_attention_naive_prefill", &flash_attention_naive_prefill_cuda);
+  m.impl("flash_attention_naive_decode", &flash_attention_naive_decode_cuda);
 }

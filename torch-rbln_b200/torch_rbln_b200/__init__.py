@@ -35,6 +35,8 @@ torch.ops.load_library(TORCH_LIBRARY)
 
 from . import _fake  # noqa: E402,F401  (registers fake kernels)
 from .ops import (  # noqa: E402,F401
+    flash_attention_naive_decode,
+    flash_attention_naive_prefill,
     paged_attn_decode,
     paged_attn_prefill,
     paged_causal_attn_decode,
@@ -43,6 +45,8 @@ from .ops import (  # noqa: E402,F401
 )
 
 __all__ = [
+    "flash_attention_naive_decode",
+    "flash_attention_naive_prefill",
     "paged_attn_decode",
     "paged_attn_prefill",
     "paged_causal_attn_decode",

@@ -1,6 +1,6 @@
 """Fake (meta) kernels: output metadata equals q's, as in the reference's
 register_fake functions (test/rbln/test_custom_kernel.py:95-135, 219-259,
-346-385, 489-526)."""
+346-385, 489-526, 597-645)."""
 
 from __future__ import annotations
 
@@ -12,6 +12,8 @@ _NAMES = (
     "paged_causal_attn_prefill",
     "paged_causal_attn_decode",
     "paged_causal_attn_decode_kvfp8",
+    "flash_attention_naive_prefill",
+    "flash_attention_naive_decode",
 )
 
 

@@ -61,6 +61,7 @@ class PagedAttnParams(ctypes.Structure):
         ("error_flags", c_vp),
         ("num_splits", c_i32),
         ("prof_events", c_vp * 2),
+        ("sinks", c_vp),
     ]
 
 

@@ -2,7 +2,7 @@
 
 Thin wrappers over torch.ops.rbln_custom_ops.* that keep the reference
 frontends' argument-count contract (torch_rbln/_internal/
-register_custom_ops.py:175-450: "takes 10 inputs" / "takes 9 or 10 inputs"
+register_custom_ops.py:175-560: "takes 10 inputs" / "takes 9 or 10 inputs"
 RuntimeErrors). Model code may call either these or torch.ops directly.
 """
 
@@ -42,3 +42,13 @@ def paged_causal_attn_decode(*args):
 def paged_causal_attn_decode_kvfp8(*args):
     _count("paged_causal_attn_decode_kvfp8", args, 11, 12)
     return _ops.paged_causal_attn_decode_kvfp8(*args)
+
+
+def flash_attention_naive_prefill(*args):
+    _count("flash_attention_naive_prefill", args, 9, 10)
+    return _ops.flash_attention_naive_prefill(*args)
+
+
+def flash_attention_naive_decode(*args):
+    _count("flash_attention_naive_decode", args, 9, 10)
+    return _ops.flash_attention_naive_decode(*args)

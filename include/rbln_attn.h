@@ -206,6 +206,54 @@ typedef struct {
  * f32 exactly in fp32. D in {64, 128}. */
 int rbln_sdpa_fwd(const rbln_sdpa_params_t* p, cudaStream_t stream);
 
+/* Dense scaled dot-product attention, backward. Shapes and strides as for
+ * the forward; every tensor's last dim contiguous, rows 16-byte aligned. */
+typedef struct {
+  int32_t batch, num_heads, num_kv_heads, q_len, kv_len, head_dim;
+  int32_t dtype;          /* F16 or BF16, shared by every tensor below except lse / dbias */
+  const void* q;          /* [B, Hq, L, D] */
+  int64_t q_stride[3];
+  const void* k;          /* [B, Hkv, S, D] */
+  int64_t k_stride[3];
+  const void* v;
+  int64_t v_stride[3];
+  const void* out;        /* forward output [B, Hq, L, D] */
+  int64_t out_stride[3];
+  const void* dout;       /* gradient of the output [B, Hq, L, D] */
+  int64_t dout_stride[3];
+  const float* lse;       /* forward logsumexp [B, Hq, L] (natural log; -inf for a row with no key) */
+  int64_t lse_stride[3];
+  void* dq;               /* [B, Hq, L, D]; NULL: not computed */
+  int64_t dq_stride[3];
+  void* dk;               /* [B, Hkv, S, D] (summed over the query heads of each KV head); NULL: not computed */
+  int64_t dk_stride[3];
+  void* dv;               /* [B, Hkv, S, D]; NULL: not computed */
+  int64_t dv_stride[3];
+  const void* mask;       /* as in rbln_sdpa_params_t */
+  int32_t mask_dtype;
+  int32_t mask_additive;
+  int64_t mask_stride[4];
+  float* dbias;           /* optional fp32 [B, Hq, L, S] contiguous: gradient of an additive mask */
+  int32_t causal;
+  float scale;
+  void* workspace;        /* rbln_sdpa_bwd_workspace_size bytes */
+  size_t workspace_bytes;
+  uint32_t* error_flags;
+} rbln_sdpa_bwd_params_t;
+
+/* Scratch for rbln_sdpa_bwd: one {lse, rowsum(dout * out)} pair per query row. */
+int rbln_sdpa_bwd_workspace_size(const rbln_sdpa_bwd_params_t* p, size_t* bytes);
+
+/* aten::_scaled_dot_product_fused_attention_overrideable_backward
+ * (reference torch_rbln/_internal/kernels/sdpa.py:754-821 with the math of
+ * _sdpa_backward_fallback, sdpa.py:614-667, and grad_attn_bias at :800-818):
+ * with P the forward's attention weights (recomputed from q, k and lse),
+ *   dv = P^T dout, dS = P * (dout v^T - rowsum(dout * out)),
+ *   dq = scale * dS k, dk = scale * dS^T q, dbias = dS,
+ * GQA gradients summed over each KV head's query heads. bf16/f16 on the
+ * tensor cores, D in {64, 128}. */
+int rbln_sdpa_bwd(const rbln_sdpa_bwd_params_t* p, cudaStream_t stream);
+
 /* No counterpart in the reference: a variant of rbln_paged_causal_attn_decode
  * for callers that cannot allocate device memory -- for example a runtime
  * that has handed all device memory to its own pool at start-up, or a

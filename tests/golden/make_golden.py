@@ -11,9 +11,11 @@ Sources executed:
     test/rbln/test_custom_kernel.py lines 1-646 (the module-level
     torch.library.custom_op definitions), executed without their
     `torch.testing._internal` import (it needs `expecttest`, absent here);
-  * torch_rbln._internal.kernels.sdpa._sdpa_cpu_fallback (sdpa.py:244-289),
-    imported with TORCH_RBLN_DIAGNOSE=1 so that the package skips loading the
-    NPU runtime.
+  * torch_rbln._internal.kernels.sdpa._sdpa_cpu_fallback (sdpa.py:244-289)
+    and scaled_dot_product_fused_attention_overrideable_backward_rbln
+    (sdpa.py:754-821) on CPU tensors, imported with TORCH_RBLN_DIAGNOSE=1 so
+    that the package skips loading the NPU runtime (its CPU-fallback log hook,
+    which needs that runtime, is replaced by a no-op).
 
 The configurations are the reference tests' (test_custom_kernel.py:660-1001:
 num_kv_heads 8, q heads per KV head 4, head_dim 64, seq 256, block_size ==
@@ -37,6 +39,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def load_reference(ref: str):
+    """Returns (_sdpa_cpu_fallback, the backward entry point)."""
     sys.path.insert(0, ref)
     path = os.path.join(ref, "test", "rbln", "test_custom_kernel.py")
     lines = open(path).read().split("\n")[:646]
@@ -46,7 +49,10 @@ def load_reference(ref: str):
     os.environ["TORCH_RBLN_DIAGNOSE"] = "1"
     from torch_rbln._internal.kernels import sdpa as ref_sdpa  # noqa: E402
 
-    return ref_sdpa._sdpa_cpu_fallback
+    # the CPU-fallback log line needs the NPU runtime's extension module;
+    # only that logging hook is replaced
+    ref_sdpa.rbln_log_cpu_fallback = lambda *a, **k: None
+    return ref_sdpa._sdpa_cpu_fallback, ref_sdpa.scaled_dot_product_fused_attention_overrideable_backward_rbln
 
 
 def sha(t: torch.Tensor) -> str:
@@ -210,6 +216,31 @@ def run_naive(case):
     return dict(out=o, kv_cache=sha(kv))
 
 
+def sdpa_bwd_cases(gen, backward):
+    """The reference's SDPA backward on CPU tensors (sdpa.py:754-821: the
+    attention-weight cache misses, so it runs _sdpa_attn_weights_fallback and
+    _sdpa_backward_fallback, plus grad_attn_bias): GQA 4 query heads over 2
+    KV heads, L = 24 queries over S = 40 keys, causal or not, with or without
+    an additive float mask."""
+    cases = []
+    B, H, Hkv, L, S = 1, 4, 2, 24, 40
+    for dtype, D in ((torch.float16, 64), (torch.float16, 128), (torch.bfloat16, 64), (torch.float32, 64)):
+        for causal in (False, True):
+            for masked in (False, True):
+                q = torch.randn(B, H, L, D, generator=gen).to(dtype)
+                k = torch.randn(B, Hkv, S, D, generator=gen).to(dtype)
+                v = torch.randn(B, Hkv, S, D, generator=gen).to(dtype)
+                go = torch.randn(B, H, L, D, generator=gen).to(dtype)
+                mask = (torch.randn(1, H, L, S, generator=gen) * 2).to(dtype) if masked else None
+                out = torch.empty(B, H, L, D, dtype=dtype)  # read only by the attention-weight cache
+                e = torch.empty(0)
+                dq, dk, dv, db = backward(go, q, k, v, mask, [True, True, True, masked], out, e, e, e, L, S, 0.0,
+                                          causal, torch.empty(()), torch.empty(()), None)
+                cases.append(dict(dtype=dtype, D=D, causal=causal, q=q, k=k, v=v, grad_out=go, mask=mask,
+                                  dq=dq, dk=dk, dv=dv, dbias=db if masked else None))
+    return cases
+
+
 def sdpa_cases(gen, fallback):
     cases = []
     for dtype in (torch.float32, torch.float16, torch.bfloat16):
@@ -246,7 +277,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     args = ap.parse_args()
-    fallback = load_reference(args.reference)
+    fallback, backward = load_reference(args.reference)
     torch.manual_seed(0)
     gen = torch.Generator().manual_seed(1234)
     dec = decode_cases(gen)
@@ -263,6 +294,7 @@ def main():
     for c in naive:
         c["results"] = run_naive(c)
     torch.save(naive, os.path.join(HERE, "flash_attention_naive.pt"))
+    torch.save(sdpa_bwd_cases(torch.Generator().manual_seed(987), backward), os.path.join(HERE, "sdpa_bwd.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -38,6 +38,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tma_map.cuh"
 
 namespace rbln {
 namespace {
@@ -1574,40 +1575,6 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// rank-N tiled map, innermost dim first; strides in bytes for dims 1..N-1.
-bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
-              const uint64_t* strides_bytes, const uint32_t* box) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t d[5], s[4];
-  cuuint32_t bx[5], es[5];
-  for (int i = 0; i < rank; ++i) {
-    d[i] = dims[i];
-    bx[i] = box[i];
-    es[i] = 1;
-  }
-  for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
-  return fn(m, dt, rank, base, d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 struct TcLaunch {
   CUtensorMap tq, tk, tv;
   AttnArgs a;
@@ -1730,10 +1697,6 @@ int launch_tc_any(const TcLaunch& Lc, cudaStream_t st) {
   return Lc.bf16 ? launch_tc<64, true>(Lc, st) : launch_tc<64, false>(Lc, st);
 }
 
-CUtensorMapDataType tmap_dtype(int dt) {
-  return dt == RBLN_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-}
-
 // q [B, Hkv, G, S, D] (element strides b, hkv, g, s) -> 5-D map, box {64, QT, G, 1, 1}
 bool map_q(CUtensorMap* m, const void* q, int dt, int B, int Hkv, int G, int S, int D, const int64_t* qs, int QT) {
   uint64_t dims[5] = {(uint64_t)D, (uint64_t)S, (uint64_t)G, (uint64_t)Hkv, (uint64_t)B};
@@ -1742,14 +1705,6 @@ bool map_q(CUtensorMap* m, const void* q, int dt, int B, int Hkv, int G, int S, 
   return make_map(m, tmap_dtype(dt), 5, const_cast<void*>(q), dims, str, box);
 }
 
-// cache [NB, Hkv, rows, D] (element strides block, head, row) -> 4-D map, box {64, rpb, 1, 1}
-bool map_kv(CUtensorMap* m, const void* c, int dt, int NB, int Hkv, int rows, int D, int64_t s_blk, int64_t s_head,
-            int64_t s_row, int rpb) {
-  uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)Hkv, (uint64_t)NB};
-  uint64_t str[3] = {(uint64_t)s_row * 2, (uint64_t)s_head * 2, (uint64_t)s_blk * 2};
-  uint32_t box[4] = {64, (uint32_t)rpb, 1, 1};
-  return make_map(m, tmap_dtype(dt), 4, const_cast<void*>(c), dims, str, box);
-}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -18,6 +18,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
+#include <array>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -401,12 +403,15 @@ bool sdpa_supported(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
   if (k.size(1) == 0 || q.size(1) % k.size(1) != 0) return false;
   if (q.numel() == 0 || k.numel() == 0) return false;
   if (dropout_p > 0.0) return false;
-  if (c10::GradMode::is_enabled() && (q.requires_grad() || k.requires_grad() || v.requires_grad())) return false;
+  // the backward (sdpa_bwd.cu) runs on the tensor cores: bf16 / f16 only
+  const bool grad = c10::GradMode::is_enabled() &&
+                    (q.requires_grad() || k.requires_grad() || v.requires_grad() ||
+                     (mask.has_value() && mask->defined() && mask->requires_grad()));
+  if (grad && dt == at::kFloat) return false;
   if (mask.has_value() && mask->defined()) {
     const auto& m = *mask;
     if (m.dim() < 2 || m.dim() > 4 || m.device() != q.device()) return false;
     if (m.scalar_type() != at::kBool && !at::isFloatingType(m.scalar_type())) return false;
-    if (m.requires_grad() && c10::GradMode::is_enabled()) return false;
   }
   return true;
 }
@@ -444,7 +449,8 @@ sdpa_overrideable_cuda(const at::Tensor& query, const at::Tensor& key, const at:
   }
   TORCH_CHECK(sdpa_supported(query, key, value, attn_bias, dropout_p),
               "_scaled_dot_product_fused_attention_overrideable (CUDA, sm_100a): unsupported inputs "
-              "(need 4-D bf16/f16/f32 q/k/v with head_dim 64 or 128, Hq % Hkv == 0, no dropout, no grad)");
+              "(need 4-D bf16/f16/f32 q/k/v with head_dim 64 or 128, Hq % Hkv == 0, no dropout; "
+              "bf16/f16 when a gradient is needed)");
   c10::cuda::CUDAGuard guard(query.device());
   auto inner = [](const at::Tensor& t) { return t.stride(-1) == 1 ? t : t.contiguous(); };
   at::Tensor q = inner(query), k = inner(key), v = inner(value);
@@ -509,6 +515,114 @@ sdpa_overrideable_cuda(const at::Tensor& query, const at::Tensor& key, const at:
   return {out, lse, cum_q, cum_k, c10::SymInt(L), c10::SymInt(S), seed, offset, debug};
 }
 
+// aten::_scaled_dot_product_fused_attention_overrideable_backward on CUDA
+// (reference sdpa.py:754-821): dq, dk, dv as grad_input_mask asks, and
+// grad_attn_bias for a floating-point mask (full [B, H, L, S], in the mask's
+// dtype; autograd sums it down to the mask's broadcast shape). P is
+// recomputed from q, k and the forward's logsumexp.
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> sdpa_overrideable_backward_cuda(
+    const at::Tensor& grad_out, const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+    const at::Tensor& attn_bias, std::array<bool, 4> grad_input_mask, const at::Tensor& out,
+    const at::Tensor& logsumexp, const at::Tensor& cum_seq_q, const at::Tensor& cum_seq_k, c10::SymInt max_q,
+    c10::SymInt max_k, double dropout_p, bool is_causal, const at::Tensor& philox_seed,
+    const at::Tensor& philox_offset, std::optional<double> scale) {
+  const char* op = "_scaled_dot_product_fused_attention_overrideable_backward";
+  TORCH_CHECK(dropout_p == 0.0, op, ": dropout is not supported");
+  TORCH_CHECK(query.dim() == 4 && key.dim() == 4 && value.dim() == 4 && grad_out.dim() == 4 && out.dim() == 4, op,
+              ": expected 4-D tensors");
+  const auto dt = query.scalar_type();
+  TORCH_CHECK(dt == at::kBFloat16 || dt == at::kHalf, op, ": bf16 / f16 only, got ", dt);
+  TORCH_CHECK(key.scalar_type() == dt && value.scalar_type() == dt && grad_out.scalar_type() == dt &&
+                  out.scalar_type() == dt,
+              op, ": q, k, v, out and grad_out must share a dtype");
+  c10::cuda::CUDAGuard guard(query.device());
+  // last dim contiguous and 16-byte aligned rows
+  auto rows16 = [](const at::Tensor& t) {
+    const bool ok = t.stride(-1) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15u) == 0 &&
+                    (t.stride(0) * 2) % 16 == 0 && (t.stride(1) * 2) % 16 == 0 && (t.stride(2) * 2) % 16 == 0;
+    return ok ? t : t.contiguous();
+  };
+  at::Tensor q = rows16(query), k = rows16(key), v = rows16(value), o = rows16(out), dout = rows16(grad_out);
+  const int64_t B = q.size(0), H = q.size(1), L = q.size(2), D = q.size(3);
+  const int64_t Hkv = k.size(1), S = k.size(2);
+  TORCH_CHECK(logsumexp.defined() && logsumexp.dim() == 3 && logsumexp.size(0) == B && logsumexp.size(1) == H &&
+                  logsumexp.size(2) == L && logsumexp.scalar_type() == at::kFloat,
+              op, ": logsumexp must be the forward's fp32 [B, H, L]");
+  at::Tensor lse = logsumexp;
+  at::Tensor dq = grad_input_mask[0] ? at::empty_like(q, at::MemoryFormat::Contiguous) : at::Tensor();
+  at::Tensor dk = grad_input_mask[1] ? at::empty_like(k, at::MemoryFormat::Contiguous) : at::Tensor();
+  at::Tensor dv = grad_input_mask[2] ? at::empty_like(v, at::MemoryFormat::Contiguous) : at::Tensor();
+  rbln_sdpa_bwd_params_t p{};
+  p.batch = (int32_t)B;
+  p.num_heads = (int32_t)H;
+  p.num_kv_heads = (int32_t)Hkv;
+  p.q_len = (int32_t)L;
+  p.kv_len = (int32_t)S;
+  p.head_dim = (int32_t)D;
+  p.dtype = to_rbln_dtype(dt);
+  p.q = q.data_ptr();
+  p.k = k.data_ptr();
+  p.v = v.data_ptr();
+  p.out = o.data_ptr();
+  p.dout = dout.data_ptr();
+  p.lse = lse.data_ptr<float>();
+  for (int i = 0; i < 3; ++i) {
+    p.q_stride[i] = q.stride(i);
+    p.k_stride[i] = k.stride(i);
+    p.v_stride[i] = v.stride(i);
+    p.out_stride[i] = o.stride(i);
+    p.dout_stride[i] = dout.stride(i);
+    p.lse_stride[i] = lse.stride(i);
+    if (dq.defined()) p.dq_stride[i] = dq.stride(i);
+    if (dk.defined()) p.dk_stride[i] = dk.stride(i);
+    if (dv.defined()) p.dv_stride[i] = dv.stride(i);
+  }
+  p.dq = dq.defined() ? dq.data_ptr() : nullptr;
+  p.dk = dk.defined() ? dk.data_ptr() : nullptr;
+  p.dv = dv.defined() ? dv.data_ptr() : nullptr;
+  at::Tensor m, dbias;
+  if (attn_bias.defined() && attn_bias.numel() > 0) {  // an empty tensor means no mask (sdpa.py:800)
+    m = attn_bias;
+    TORCH_CHECK(m.scalar_type() == at::kBool || at::isFloatingType(m.scalar_type()), op,
+                ": attn_bias must be bool or floating point");
+    if (m.scalar_type() != at::kBool && m.scalar_type() != at::kFloat && m.scalar_type() != at::kHalf &&
+        m.scalar_type() != at::kBFloat16)
+      m = m.to(at::kFloat);
+    while (m.dim() < 4) m = m.unsqueeze(0);
+    m = m.expand({B, H, L, S});
+    if (m.stride(3) != 1) m = m.contiguous();
+    p.mask = m.data_ptr();
+    p.mask_dtype = to_rbln_dtype(m.scalar_type());
+    p.mask_additive = m.scalar_type() == at::kBool ? 0 : 1;
+    for (int i = 0; i < 4; ++i) p.mask_stride[i] = m.stride(i);
+    if (grad_input_mask[3] && m.scalar_type() != at::kBool) {
+      dbias = at::empty({B, H, L, S}, q.options().dtype(at::kFloat));
+      p.dbias = dbias.data_ptr<float>();
+    }
+  }
+  p.causal = is_causal ? 1 : 0;
+  p.scale = (float)(scale.has_value() ? *scale : 1.0 / std::sqrt((double)D));
+  size_t ws = 0;
+  check_rc(rbln_sdpa_bwd_workspace_size(&p, &ws), op);
+  at::Tensor wst = at::empty({(int64_t)std::max<size_t>(ws, 16)}, q.options().dtype(at::kByte));
+  p.workspace = wst.data_ptr();
+  p.workspace_bytes = ws;
+  at::Tensor err;
+  if (debug_checks()) {
+    err = at::zeros({1}, q.options().dtype(at::kInt));
+    p.error_flags = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  }
+  auto stream = at::cuda::getCurrentCUDAStream(q.device().index());
+  check_rc(rbln_sdpa_bwd(&p, stream.stream()), op);
+  if (err.defined()) {
+    const int flags = err.item<int>();
+    TORCH_CHECK(flags == 0, op, ": device error flags 0x", std::hex, flags);
+  }
+  at::Tensor gbias;
+  if (dbias.defined()) gbias = dbias.to(attn_bias.scalar_type());
+  return {dq, dk, dv, gbias};
+}
+
 void set_sdpa_route(bool enabled) { g_sdpa_route.store(enabled); }
 bool sdpa_route_enabled() { return g_sdpa_route.load(); }
 
@@ -527,6 +641,7 @@ TORCH_LIBRARY_IMPL(rbln_attn, CompositeExplicitAutograd, m) {
 TORCH_LIBRARY_IMPL(aten, CUDA, m) {
   m.impl("_fused_sdp_choice", &fused_sdp_choice_cuda);
   m.impl("_scaled_dot_product_fused_attention_overrideable", &sdpa_overrideable_cuda);
+  m.impl("_scaled_dot_product_fused_attention_overrideable_backward", &sdpa_overrideable_backward_cuda);
 }
 
 TORCH_LIBRARY(rbln_custom_ops, m) {

@@ -85,10 +85,28 @@ def test_route_and_fp32_grad_goes_elsewhere():
 FIX = torch.load(os.path.join(os.path.dirname(__file__), "golden", "sdpa_bwd.pt"), weights_only=False)
 
 
+def grads_aten(q, k, v, go, mask, causal):
+    """The forward and backward aten ops called directly (F.scaled_dot_product_attention
+    refuses an explicit mask together with is_causal=True; the ops take both)."""
+    qd, kd, vd, god = q.to(DEV), k.to(DEV), v.to(DEV), go.to(DEV)
+    md = None if mask is None else mask.to(DEV)
+    res = torch.ops.aten._scaled_dot_product_fused_attention_overrideable(qd, kd, vd, md, 0.0, causal, False)
+    e = torch.empty(0, device=DEV)
+    g = torch.ops.aten._scaled_dot_product_fused_attention_overrideable_backward(
+        god, qd, kd, vd, md if md is not None else e, [True, True, True, md is not None], res[0], res[1], res[2],
+        res[3], res[4], res[5], 0.0, causal, res[6], res[7])
+    torch.cuda.synchronize()
+    return [t.cpu() if t is not None else None for t in g]
+
+
 @pytest.mark.parametrize("idx", [i for i, c in enumerate(FIX) if c["dtype"] != torch.float32])
 def test_reference_fixtures(idx):
     c = FIX[idx]
-    got = grads_cuda(c["q"], c["k"], c["v"], c["grad_out"], c["mask"], c["causal"], mask_grad=c["mask"] is not None)
+    if c["causal"] and c["mask"] is not None:
+        got = grads_aten(c["q"], c["k"], c["v"], c["grad_out"], c["mask"], True)
+    else:
+        got = grads_cuda(c["q"], c["k"], c["v"], c["grad_out"], c["mask"], c["causal"],
+                         mask_grad=c["mask"] is not None)
     for name, gv in zip(("dq", "dk", "dv"), got):
         assert gv.shape == c[name].shape and gv.dtype == c[name].dtype
     check(got, c["q"], c["k"], c["v"], c["grad_out"], c["mask"], c["causal"])
@@ -119,7 +137,10 @@ def test_backward_matches_exact(case):
     elif mk == "bool":
         mask = torch.rand((L, S), generator=g) > 0.3
         mask[:, 0] = True  # every row keeps a key
-    got = grads_cuda(q, k, v, go, mask, causal, mask_grad=mk == "float")
+    if causal and mask is not None:
+        got = grads_aten(q, k, v, go, mask, True)
+    else:
+        got = grads_cuda(q, k, v, go, mask, causal, mask_grad=mk == "float")
     check(got, q, k, v, go, mask, causal)
     if causal and S > L:
         # top-left causal: keys past the last query are seen by nobody

@@ -515,6 +515,8 @@ COMPUTE = {
                  desc="SDPA causal GQA fp32 B=1 Hq=32 Hkv=8 L=S=512 D=64 (Llama-3.2-1B attention shape)"),
     "sdpa_bf16": dict(kind="sdpa", B=4, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
                       desc="SDPA causal GQA bf16 B=4 Hq=32 Hkv=8 L=S=4096 D=128"),
+    "sdpa_bwd": dict(kind="sdpa_bwd", B=2, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
+                     desc="SDPA backward causal GQA bf16 B=2 Hq=32 Hkv=8 L=S=4096 D=128 (dq, dk, dv)"),
 }
 
 
@@ -551,7 +553,13 @@ def build_sdpa(wl, seed=0):
     k = torch.randn([B, Hkv, L, D], generator=g).to(wl["dtype"])
     v = torch.randn([B, Hkv, L, D], generator=g).to(wl["dtype"])
     flops = 4 * D * Hq * B * (L * (L + 1) // 2)
-    return dict(q=q, k=k, v=v, flops=flops, scale=1.0 / math.sqrt(D))
+    d = dict(q=q, k=k, v=v, flops=flops, scale=1.0 / math.sqrt(D))
+    if wl["kind"] == "sdpa_bwd":
+        # algorithmic backward FLOPs: five L x S x D products (dV, dP, dQ, dK and the
+        # recomputed S) against the forward's two, i.e. 2.5x the forward count
+        d["flops"] = flops * 5 // 2
+        d["dout"] = torch.randn([B, Hq, L, D], generator=g).to(wl["dtype"])
+    return d
 
 
 def _timed_kernel_loop(args, stream, step, kernel_step, flush):
@@ -624,6 +632,42 @@ def run_compute_ours(args, wl_name):
         kernel = "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)"
         dtype = "bf16"
         l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
+    elif wl["kind"] == "sdpa_bwd":
+        d = build_sdpa(wl, seed=0)
+        q, k, v, dout = (d[x].to(dev) for x in ("q", "k", "v", "dout"))
+        fwd = torch.ops.aten._scaled_dot_product_fused_attention_overrideable(q, k, v, None, 0.0, True, False,
+                                                                              scale=d["scale"])
+        out, lse = fwd[0], fwd[1]
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        bp = cabi.sdpa_bwd_params(q, k, v, out, dout, lse, dq, dk, dv, causal=True, scale=d["scale"])
+        wsz = ctypes.c_size_t(0)
+        L.rbln_sdpa_bwd_workspace_size(ctypes.byref(bp), ctypes.byref(wsz))
+        wsb = torch.empty(wsz.value, dtype=torch.uint8, device=dev)
+        bp.workspace, bp.workspace_bytes = wsb.data_ptr(), wsz.value
+        bpref = ctypes.byref(bp)
+
+        def step():
+            rc = L.rbln_sdpa_bwd(bpref, sh)
+            if rc != 0:
+                raise RuntimeError(f"rbln_sdpa_bwd failed: {rc}")
+
+        kernel_step = step
+
+        e0t = torch.empty(0, device=dev)
+
+        def op_call(qq, kk, vv, oo, gg, ll):
+            return torch.ops.aten._scaled_dot_product_fused_attention_overrideable_backward(
+                gg, qq, kk, vv, e0t, [True, True, True, False], oo, ll, fwd[2], fwd[3], fwd[4], fwd[5], 0.0, True,
+                fwd[6], fwd[7], scale=d["scale"])[:3]
+
+        host_inputs = [d["q"], d["k"], d["v"], out.cpu(), d["dout"], lse.cpu()]
+        out_shape, out_dtype = None, None
+        metric = "SDPA backward TFLOP/s"
+        launches = 3  # row pre-pass, dK/dV kernel, dQ kernel
+        kernel = ("sdpa_bwd_kv_kernel<128, bf16> + sdpa_bwd_q_kernel<128, bf16> + row pre-pass "
+                  "(tcgen05/TMEM/TMA; whole backward timed)")
+        dtype = "bf16"
+        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
     else:
         d = build_sdpa(wl, seed=0)
         q, k, v = (d[x].to(dev) for x in ("q", "k", "v"))
@@ -666,13 +710,17 @@ def run_compute_ours(args, wl_name):
 
     # e2e through the public torch API with host buffers
     pinned = [t.cpu().pin_memory() for t in host_inputs]
-    hout = torch.empty(out_shape, dtype=out_dtype).pin_memory()
+    if out_shape is None:  # backward: the three gradients come back
+        houts = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
+    else:
+        houts = [torch.empty(out_shape, dtype=out_dtype).pin_memory()]
     h2d = sum(t.numel() * t.element_size() for t in pinned)
-    d2h = hout.numel() * hout.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in houts)
 
     def e2e_step():
         o = op_call(*[t.to(dev, non_blocking=True) for t in pinned])
-        hout.copy_(o, non_blocking=True)
+        for h, t in zip(houts, o if isinstance(o, (tuple, list)) else [o]):
+            h.copy_(t, non_blocking=True)
 
     for _ in range(max(2, args.warmup)):
         e2e_step()
@@ -701,8 +749,9 @@ def run_compute_ours(args, wl_name):
         "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}", "l2": l2, "flops_per_step": flops},
         "e2e": {"value": round(ws * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "api": ("torch.ops.rbln_custom_ops.paged_causal_attn_prefill" if wl["kind"] == "prefill"
-                        else "torch.nn.functional.scaled_dot_product_attention")},
+                "api": {"prefill": "torch.ops.rbln_custom_ops.paged_causal_attn_prefill",
+                        "sdpa_bwd": "torch.ops.aten._scaled_dot_product_fused_attention_overrideable_backward"}.get(
+                            wl["kind"], "torch.nn.functional.scaled_dot_product_attention")},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_peak, "unit": "TFLOP/s",
                      "frac": round(achieved / tf_peak, 4), "traffic": _traffic_from_profiles(wl_name),
                      "kernel": kernel, "kernel_ms": round(k_ms, 4),
@@ -751,6 +800,14 @@ def _cpu_compute_times(wl, d, reps, budget_s):
         fn = lambda: opa.mock_prefill_contiguous(q, k, v, kc.clone(), vc.clone(), ctx, sc, mask)
         sample = (f"1 of {d['B']} sequences (median cached context {ctx}, 512 new tokens), reference CPU "
                   f"algorithm (oracle.paged_attention.mock_prefill_contiguous, bf16, per-sequence layout)")
+    elif wl["kind"] == "sdpa_bwd":
+        # one batch entry, one KV head and its 4 query heads: 1/(B * Hkv) of the workload
+        G = wl["Hq"] // wl["Hkv"]
+        q, k, v, go = d["q"][:1, :G], d["k"][:1, :1], d["v"][:1, :1], d["dout"][:1, :G]
+        flops = d["flops"] // (wl["B"] * wl["Hkv"])
+        fn = lambda: osd.sdpa_backward_reference(go, q, k, v, None, True, d["scale"])
+        sample = (f"1 of {wl['B']} batch entries x 1 of {wl['Hkv']} KV heads ({G} query heads), reference CPU "
+                  f"backward (oracle.sdpa.sdpa_backward_reference: attention weights + 4 products, bf16)")
     else:
         q, k, v = d["q"], d["k"], d["v"]
         flops = d["flops"]
@@ -785,10 +842,11 @@ def run_reference_compute(args, wl_name):
     med, flops, sample, n = _cpu_compute_times(wl, d, args.steps, 120.0)
     val = flops / med / 1e12
     unit = "TFLOP/s"
-    line = {"impl": "reference", "metric": "paged chunked prefill TFLOP/s" if wl["kind"] == "prefill"
-            else "SDPA TFLOP/s", "value": round(val, 5), "unit": unit, "n_gpus": ws, "steps": n,
+    metric = {"prefill": "paged chunked prefill TFLOP/s", "sdpa_bwd": "SDPA backward TFLOP/s"}.get(wl["kind"],
+                                                                                                 "SDPA TFLOP/s")
+    line = {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": unit, "n_gpus": ws, "steps": n,
             "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32" if wl["kind"] == "sdpa" and wl["dtype"] == torch.float32 else "bf16",
+            "vs_baseline": None, "dtype": "f32" if wl["kind"] != "prefill" and wl["dtype"] == torch.float32 else "bf16",
             "data": "synthetic (seeded)", "config": {"workload": wl["desc"]},
             "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
                              "sample": sample},

@@ -45,14 +45,18 @@ def test_abi_version_and_struct_size():
     assert L.rbln_paged_attn_params_sizeof() == ctypes.sizeof(cabi.PagedAttnParams)
 
 
-def test_struct_field_offsets_match_c():
+@pytest.mark.parametrize("cname,pyname", [("rbln_paged_attn_params_t", "PagedAttnParams"),
+                                          ("rbln_sdpa_params_t", "SdpaParams"),
+                                          ("rbln_sdpa_bwd_params_t", "SdpaBwdParams")])
+def test_struct_field_offsets_match_c(cname, pyname):
     from torch_rbln_b200 import cabi
 
-    fields = [f for f, _ in cabi.PagedAttnParams._fields_]
+    cls = getattr(cabi, pyname)
+    fields = [f for f, _ in cls._fields_]
     src = "#include <stdio.h>\n#include <stddef.h>\n#include \"rbln_attn.h\"\nint main(void){\n"
     for f in fields:
-        src += f'  printf("%zu\\n", offsetof(rbln_paged_attn_params_t, {f}));\n'
-    src += "  return 0;\n}\n"
+        src += f'  printf("%zu\\n", offsetof({cname}, {f}));\n'
+    src += f'  printf("%zu\\n", sizeof({cname}));\n  return 0;\n}}\n'
     with tempfile.TemporaryDirectory() as td:
         c = os.path.join(td, "off.c")
         exe = os.path.join(td, "off")
@@ -63,7 +67,7 @@ def test_struct_field_offsets_match_c():
         if r.returncode != 0:
             pytest.skip("gcc or CUDA headers unavailable: " + r.stderr[-200:])
         offs = [int(x) for x in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
-    got = [getattr(cabi.PagedAttnParams, f).offset for f in fields]
+    got = [getattr(cls, f).offset for f in fields] + [ctypes.sizeof(cls)]
     assert offs == got
 
 

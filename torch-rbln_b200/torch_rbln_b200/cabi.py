@@ -80,6 +80,27 @@ class SdpaParams(ctypes.Structure):
     ]
 
 
+class SdpaBwdParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_i32), ("num_heads", c_i32), ("num_kv_heads", c_i32), ("q_len", c_i32), ("kv_len", c_i32),
+        ("head_dim", c_i32), ("dtype", c_i32),
+        ("q", c_vp), ("q_stride", c_i64 * 3),
+        ("k", c_vp), ("k_stride", c_i64 * 3),
+        ("v", c_vp), ("v_stride", c_i64 * 3),
+        ("out", c_vp), ("out_stride", c_i64 * 3),
+        ("dout", c_vp), ("dout_stride", c_i64 * 3),
+        ("lse", c_vp), ("lse_stride", c_i64 * 3),
+        ("dq", c_vp), ("dq_stride", c_i64 * 3),
+        ("dk", c_vp), ("dk_stride", c_i64 * 3),
+        ("dv", c_vp), ("dv_stride", c_i64 * 3),
+        ("mask", c_vp), ("mask_dtype", c_i32), ("mask_additive", c_i32), ("mask_stride", c_i64 * 4),
+        ("dbias", c_vp),
+        ("causal", c_i32), ("scale", ctypes.c_float),
+        ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("error_flags", c_vp),
+    ]
+
+
 class PeerOut(ctypes.Structure):
     """rbln_peer_out_t: every rank's output buffer and flag array, as mapped on this GPU."""
     _fields_ = [("out", c_vp), ("flags", c_vp), ("n", c_i32), ("rank", c_i32), ("head0", c_i32),
@@ -101,6 +122,8 @@ ENTRY_POINTS = {
     "rbln_paged_causal_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_sdpa_fwd": (ctypes.c_int, [ctypes.POINTER(SdpaParams), c_vp]),
+    "rbln_sdpa_bwd_workspace_size": (ctypes.c_int, [ctypes.POINTER(SdpaBwdParams), ctypes.POINTER(ctypes.c_size_t)]),
+    "rbln_sdpa_bwd": (ctypes.c_int, [ctypes.POINTER(SdpaBwdParams), c_vp]),
     "rbln_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(c_vp), c_vp]),
     "rbln_ipc_free": (ctypes.c_int, [c_vp]),
     "rbln_ipc_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
@@ -210,6 +233,25 @@ def sdpa_params(q, k, v, out, lse=None, causal=True, scale=None):
         p.lse = lse.data_ptr()
         for i in range(3):
             p.lse_stride[i] = lse.stride(i)
+    p.causal = 1 if causal else 0
+    p.scale = scale if scale is not None else 1.0 / (q.shape[-1] ** 0.5)
+    return p
+
+
+def sdpa_bwd_params(q, k, v, out, dout, lse, dq=None, dk=None, dv=None, causal=True, scale=None):
+    """Fills SdpaBwdParams (no mask); dq / dk / dv None are not computed."""
+    p = SdpaBwdParams()
+    p.batch, p.num_heads, p.q_len, p.head_dim = q.shape
+    p.num_kv_heads, p.kv_len = k.shape[1], k.shape[2]
+    p.dtype = _DT[q.dtype]
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out), ("dout", dout), ("lse", lse), ("dq", dq),
+                    ("dk", dk), ("dv", dv)):
+        if t is None:
+            continue
+        setattr(p, name, t.data_ptr())
+        st = getattr(p, name + "_stride")
+        for i in range(3):
+            st[i] = t.stride(i)
     p.causal = 1 if causal else 0
     p.scale = scale if scale is not None else 1.0 / (q.shape[-1] ** 0.5)
     return p

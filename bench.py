@@ -517,6 +517,9 @@ COMPUTE = {
                       desc="SDPA causal GQA bf16 B=4 Hq=32 Hkv=8 L=S=4096 D=128"),
     "sdpa_bwd": dict(kind="sdpa_bwd", B=2, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
                      desc="SDPA backward causal GQA bf16 B=2 Hq=32 Hkv=8 L=S=4096 D=128 (dq, dk, dv)"),
+    # profiling case for ncu --set full
+    "sdpa_bwd_small": dict(kind="sdpa_bwd", B=1, Hq=32, Hkv=8, L=2048, D=128, dtype=torch.bfloat16,
+                           desc="SDPA backward causal GQA bf16 B=1 Hq=32 Hkv=8 L=S=2048 D=128 (dq, dk, dv)"),
 }
 
 

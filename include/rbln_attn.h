@@ -233,7 +233,7 @@ typedef struct {
   int32_t mask_dtype;
   int32_t mask_additive;
   int64_t mask_stride[4];
-  float* dbias;           /* optional fp32 [B, Hq, L, S] contiguous: gradient of an additive mask */
+  float* dbias;           /* optional fp32 [B, Hq, L, S] contiguous: gradient of the additive mask (needs mask) */
   int32_t causal;
   float scale;
   void* workspace;        /* rbln_sdpa_bwd_workspace_size bytes */

@@ -35,9 +35,14 @@
 //                         dS over S's buffer, dQ += dS K.
 // No atomics: every output element has one writer.
 //
-// Warp roles in both tile kernels (192 threads): warp 0 issues the TMA copies
-// (one thread), warp 1 owns TMEM and issues the MMAs (one thread), warps 2-5
-// compute (thread = TMEM lane). Every mbarrier wait is bounded (sm100.cuh);
+// Warp roles in both tile kernels (320 threads): warp 0 issues the TMA copies
+// (one thread; in the dK/dV kernel also a bulk copy of the tile's 128 row
+// pairs into shared memory), warp 1 owns TMEM and issues the MMAs (one
+// thread), warps 2-9 compute: thread = TMEM lane, the two warps of a lane
+// quadrant each take 64 of the tile's 128 columns. The mask, the dbias store
+// and the causal test are compile-time or per-32-column-chunk decisions, so
+// an unmasked chunk costs one FMA, one exp2, two FP ops and a pack per
+// element. Every mbarrier wait is bounded (sm100.cuh);
 // on timeout the CTA raises RBLN_DEVERR_TIMEOUT, drains its copies and MMAs,
 // frees TMEM and returns.
 
@@ -53,7 +58,6 @@ namespace {
 using namespace sm100;
 
 constexpr int BT = 128;                 // rows per tile: keys (kv kernel) or queries (q kernel)
-constexpr int kBwdThreads = 192;        // 6 warps
 constexpr int kPanel = 128 * 128;       // 128 rows x 64 16-bit elements, 128B-swizzled
 
 struct BwdArgs {
@@ -157,7 +161,8 @@ struct KvLayout {
   static constexpr int V = K + NP * kPanel;
   static constexpr int Q0 = V + NP * kPanel;     // stage s at Q0 + s * NP * kPanel
   static constexpr int DO0 = Q0 + 2 * NP * kPanel;
-  static constexpr int BAR = DO0 + 2 * NP * kPanel;
+  static constexpr int RI0 = DO0 + 2 * NP * kPanel;  // stage s: the tile's 128 row pairs (1 KB)
+  static constexpr int BAR = RI0 + 2 * BT * 8;
   static constexpr int TMEM_SLOT = BAR + 16 * 8;
   static constexpr int ABORT = TMEM_SLOT + 8;
   static constexpr int TOTAL = ABORT + 8;
@@ -174,7 +179,20 @@ __device__ __forceinline__ void kv_tile(int i, int per_g, int qt0, int& g, int& 
   qt = qt0 + (i - g * per_g);
 }
 
-template <int D, bool BF16>
+// Packed (16-bit pairs) outputs of the compute warps sit at column offset
+// kPackOff of the S / dP buffers: chunk c (32 fp32 columns) packs into
+// columns [kPackOff + 16c, kPackOff + 16c + 16). The warp of half 0 reads
+// chunks 0-1 (columns [0, 64)) and processes chunk 1 first; the warp of
+// half 1 reads chunks 2-3 ([64, 128)) and processes chunk 2 first. So every
+// packed store lands on columns its own warp has already read, and the two
+// warps of a lane quadrant never touch each other's columns.
+constexpr int kPackOff = 32;
+
+// 8 compute warps (2..9): lane quadrant warp % 4, column half (warp - 2) / 4.
+constexpr int kBwdThreads = 320;
+constexpr int kComputeWarps = 8;
+
+template <int D, bool BF16, bool MASK, bool DBIAS>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     sdpa_bwd_kv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -200,7 +218,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < KB_COUNT; ++i) mbar_init(bar(i), i == KB_PF ? 4u : 1u);
+    for (int i = 0; i < KB_COUNT; ++i) mbar_init(bar(i), i == KB_PF ? (uint32_t)kComputeWarps : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -232,12 +250,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         int g, qt;
         kv_tile(i, per_g, qt0, g, qt);
         const int hq = h * a.G + g;
-        mbar_arrive_expect_tx(bar(KB_QF0 + st), 2 * NP * kPanel);
+        mbar_arrive_expect_tx(bar(KB_QF0 + st), 2 * NP * kPanel + BT * 8);
         for (int p = 0; p < NP; ++p) {
           tma_load_4d(sbase + Lay::Q0 + (st * NP + p) * kPanel, &tm_q, bar(KB_QF0 + st), p * 64, qt * BT, hq, b);
           tma_load_4d(sbase + Lay::DO0 + (st * NP + p) * kPanel, &tm_do, bar(KB_QF0 + st), p * 64, qt * BT, hq,
                       b);
         }
+        // {lse, delta} of the tile's 128 query rows: 1 KB at a 1 KB-aligned offset
+        bulk_load(sbase + Lay::RI0 + st * BT * 8, a.rows + ((int64_t)b * a.H + hq) * a.Lp + qt * BT, BT * 8,
+                  bar(KB_QF0 + st));
         issued = i + 1;
       }
       if (*abort) {
@@ -268,7 +289,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t qb = sbase + Lay::Q0 + st * NP * kPanel;
         const uint32_t db = sbase + Lay::DO0 + st * NP * kPanel;
         // (the previous tile's dV / dK MMAs read P^T and dS^T from these
-        // columns; tcgen05.mma runs in issue order, so these writes follow)
+        // buffers; tcgen05.mma runs in issue order, so these writes follow)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
@@ -290,8 +311,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_f16_ts(t_dv, t_s + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
-          umma_f16_ts(t_dk, t_dp + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+          umma_f16_ts(t_dv, t_s + kPackOff + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+          umma_f16_ts(t_dk, t_dp + kPackOff + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
         }
         umma_commit(bar(KB_QE0 + st));
       }
@@ -306,53 +327,78 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     // ------------------------------------------------------------- compute
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // key row == TMEM lane
     const int t = t0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
+      const int st = i & 1;
       int g, qt;
       kv_tile(i, per_g, qt0, g, qt);
       const int hq = h * a.G + g;
       const int l0 = qt * BT;
-      const float2* ri = a.rows + ((int64_t)b * a.H + hq) * a.Lp + l0;
-      const int64_t mrow = a.mask ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h : 0;
-      float* dbrow = a.dbias ? a.dbias + (((int64_t)b * a.H + hq) * a.L) * a.S + t : nullptr;
-      // tcgen05.ld is .sync.aligned: the whole warp takes the same path
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(KB_SF), i & 1, abort))) {
+      const int64_t mrow = MASK ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h : 0;
+      float* dbrow = DBIAS ? a.dbias + (((int64_t)b * a.H + hq) * a.L) * a.S + t : nullptr;
+      // S^T / dP^T of this tile are in TMEM once SF completes; the row pairs
+      // were copied with the tile's Q / dO (QF). tcgen05.ld is .sync.aligned:
+      // the whole warp takes the same path.
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(KB_QF0 + st), (i >> 1) & 1, abort) &&
+                                       mbar_wait(bar(KB_SF), i & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const float2* ri = reinterpret_cast<const float2*>(sgen + Lay::RI0 + st * BT * 8);
 #pragma unroll 1
-      for (int c4 = 0; c4 < BT / 32; ++c4) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c4 = half == 0 ? 1 - cc : 2 + cc;
         uint32_t sv[32], dv[32];
         __syncwarp();
         tmem_ld32(t_s + lane_off + c4 * 32, sv);
         tmem_ld32(t_dp + lane_off + c4 * 32, dv);
         tmem_wait_ld();
+        const int la = l0 + c4 * 32;
+        // 0: nothing visible, 1: everything (but padding rows, whose lse is
+        // +inf), 2: the causal diagonal crosses the chunk
+        const int cls = t >= a.S ? 0 : (!a.causal || t <= la) ? 1 : (t > la + 31 ? 0 : 2);
         uint32_t pk[16], dk[16];
+        if (cls == 0) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pp[2], dd[2];
+          for (int e = 0; e < 16; ++e) pk[e] = dk[e] = 0u;
+        } else {
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = c4 * 32 + 2 * e + u;
-            const int l = l0 + c;
-            const float2 rw = ri[c];  // uniform across the warp: broadcast load
-            const float x = masked_score(a, __uint_as_float(sv[2 * e + u]), t, l, mrow);
-            const float p = exp2_approx(x - rw.x);  // -inf -> 0; padding rows have rw.x = +inf
-            const float ds = (x == neg_inf()) ? 0.f : p * (__uint_as_float(dv[2 * e + u]) - rw.y);
-            pp[u] = p;
-            dd[u] = ds;
-            if (dbrow && t < a.S && l < a.L) dbrow[(int64_t)l * a.S] = ds;
+          for (int e = 0; e < 16; ++e) {
+            float pp[2], dd[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int c = c4 * 32 + 2 * e + u;
+              const int l = la + 2 * e + u;
+              const float2 rw = ri[c];  // shared-memory broadcast
+              float x = fmaf(__uint_as_float(sv[2 * e + u]), a.qk_mult, -rw.x);
+              bool keep = cls == 1 || t <= l;
+              if (MASK) {
+                if (l < a.L) {
+                  const float mv = bias_value(a.mask, a.mask_dtype, mrow + (int64_t)l * a.m_l + t);
+                  if (a.mask_additive) {
+                    x = fmaf(mv, kLog2e, x);
+                  } else {
+                    keep = keep && mv > 0.f;
+                  }
+                }
+              }
+              const float p = keep ? exp2_approx(x) : 0.f;  // padding rows: x = -inf, p = 0
+              const float ds = keep ? p * (__uint_as_float(dv[2 * e + u]) - rw.y) : 0.f;
+              pp[u] = p;
+              dd[u] = ds;
+              if (DBIAS && l < a.L) dbrow[(int64_t)l * a.S] = ds;
+            }
+            pk[e] = pack2<BF16>(pp[0], pp[1]);
+            dk[e] = pack2<BF16>(dd[0], dd[1]);
           }
-          pk[e] = pack2<BF16>(pp[0], pp[1]);
-          dk[e] = pack2<BF16>(dd[0], dd[1]);
         }
-        // columns [16 c4, 16 c4 + 16) were read by this chunk or an earlier one
-        tmem_st16(t_s + lane_off + c4 * 16, pk);
-        tmem_st16(t_dp + lane_off + c4 * 16, dk);
+        tmem_st16(t_s + lane_off + kPackOff + c4 * 16, pk);
+        tmem_st16(t_dp + lane_off + kPackOff + c4 * 16, dk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -361,6 +407,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    // each of the quadrant's two warps stores half of the D columns
     ok = __all_sync(0xffffffffu, ok);
     if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(KB_DONE), 0, abort));
     tc_fence_after();
@@ -368,7 +415,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       char* dvrow = a.dv ? a.dv + b * a.dv_b + h * a.dv_h + (int64_t)t * a.dv_l : nullptr;
       char* dkrow = a.dk ? a.dk + b * a.dk_b + h * a.dk_h + (int64_t)t * a.dk_l : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t ov[32], ok2[32];
         if (ntiles > 0) {
           __syncwarp();
@@ -427,7 +474,7 @@ struct QLayout {
 
 enum QBar { QB_Q = 0, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SF, QB_PF, QB_DONE, QB_COUNT };
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool MASK>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     sdpa_bwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -451,7 +498,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < QB_COUNT; ++i) mbar_init(bar(i), i == QB_PF ? 4u : 1u);
+    for (int i = 0; i < QB_COUNT; ++i) mbar_init(bar(i), i == QB_PF ? (uint32_t)kComputeWarps : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -531,7 +578,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          umma_f16_ts(t_dq, t_s + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
+          umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar(QB_KE0 + st));
       }
@@ -544,11 +591,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // query row == TMEM lane
     const int l = l0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float2 rw = a.rows[((int64_t)b * a.H + hq) * a.Lp + l];  // padding rows: {+inf, 0}
-    const int64_t mrow = a.mask ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h : 0;
+    const int64_t mrow = MASK ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h + (int64_t)min(l, a.L - 1) * a.m_l : 0;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int kt0 = j * BT;
@@ -558,26 +606,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int c4 = 0; c4 < BT / 32; ++c4) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c4 = half == 0 ? 1 - cc : 2 + cc;
         uint32_t sv[32], dv[32];
         __syncwarp();
         tmem_ld32(t_s + lane_off + c4 * 32, sv);
         tmem_ld32(t_dp + lane_off + c4 * 32, dv);
         tmem_wait_ld();
+        const int ta = kt0 + c4 * 32;
+        // 0: nothing visible, 1: every key (rows past L have lse +inf), 2: per key
+        const int cls = (ta >= a.S || (a.causal && ta > l)) ? 0
+                        : ((!a.causal || ta + 31 <= l) && ta + 31 < a.S) ? 1 : 2;
         uint32_t dk[16];
+        if (cls == 0) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float dd[2];
+          for (int e = 0; e < 16; ++e) dk[e] = 0u;
+        } else {
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int t = kt0 + c4 * 32 + 2 * e + u;
-            const float x = masked_score(a, __uint_as_float(sv[2 * e + u]), t, l, mrow);
-            const float p = exp2_approx(x - rw.x);
-            dd[u] = (x == neg_inf()) ? 0.f : p * (__uint_as_float(dv[2 * e + u]) - rw.y);
+          for (int e = 0; e < 16; ++e) {
+            float dd[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int t = ta + 2 * e + u;
+              float x = fmaf(__uint_as_float(sv[2 * e + u]), a.qk_mult, -rw.x);
+              bool keep = cls == 1 || (t < a.S && (!a.causal || t <= l));
+              if (MASK) {
+                if (keep && l < a.L) {
+                  const float mv = bias_value(a.mask, a.mask_dtype, mrow + t);
+                  if (a.mask_additive) {
+                    x = fmaf(mv, kLog2e, x);
+                  } else {
+                    keep = mv > 0.f;
+                  }
+                }
+              }
+              const float p = keep ? exp2_approx(x) : 0.f;
+              dd[u] = keep ? p * (__uint_as_float(dv[2 * e + u]) - rw.y) : 0.f;
+            }
+            dk[e] = pack2<BF16>(dd[0], dd[1]);
           }
-          dk[e] = pack2<BF16>(dd[0], dd[1]);
         }
-        tmem_st16(t_s + lane_off + c4 * 16, dk);
+        tmem_st16(t_s + lane_off + kPackOff + c4 * 16, dk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -591,7 +660,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (ok && a.dq) {
       char* qrow = a.dq + b * a.dq_b + hq * a.dq_h + (int64_t)l * a.dq_l;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t ov[32];
         if (nk > 0) {
           __syncwarp();
@@ -639,6 +708,26 @@ struct BwdMaps {
   CUtensorMap q, k, v, dout;
 };
 
+template <int D, bool BF16, bool MASK, bool DBIAS>
+int launch_kv(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
+  constexpr int sm = KvLayout<D>::ALLOC;
+  auto* k = sdpa_bwd_kv_kernel<D, BF16, MASK, DBIAS>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
+  dim3 grid((a.S + BT - 1) / BT, a.Hkv, a.B);
+  k<<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
+template <int D, bool BF16, bool MASK>
+int launch_q(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
+  constexpr int sm = QLayout<D>::ALLOC;
+  auto* k = sdpa_bwd_q_kernel<D, BF16, MASK>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
+  dim3 grid((a.L + BT - 1) / BT, a.H, a.B);
+  k<<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}
+
 template <int D, bool BF16>
 int launch_bwd(const rbln_sdpa_bwd_params_t* p, const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   const int64_t nrows = (int64_t)a.B * a.H * a.Lp;
@@ -651,22 +740,14 @@ int launch_bwd(const rbln_sdpa_bwd_params_t* p, const BwdMaps& m, const BwdArgs&
   if (p->dbias && cudaMemsetAsync(p->dbias, 0, (size_t)a.B * a.H * a.L * a.S * sizeof(float), st) != cudaSuccess)
     return RBLN_ERR_LAUNCH;
   if (p->dk || p->dv || p->dbias) {
-    constexpr int sm = KvLayout<D>::ALLOC;
-    if (cudaFuncSetAttribute(sdpa_bwd_kv_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) !=
-        cudaSuccess)
-      return RBLN_ERR_LAUNCH;
-    dim3 grid((a.S + BT - 1) / BT, a.Hkv, a.B);
-    sdpa_bwd_kv_kernel<D, BF16><<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
-    if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
+    const int rc = !a.mask  ? launch_kv<D, BF16, false, false>(m, a, st)
+                   : p->dbias ? launch_kv<D, BF16, true, true>(m, a, st)
+                              : launch_kv<D, BF16, true, false>(m, a, st);
+    if (rc != RBLN_OK) return rc;
   }
   if (p->dq) {
-    constexpr int sm = QLayout<D>::ALLOC;
-    if (cudaFuncSetAttribute(sdpa_bwd_q_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) !=
-        cudaSuccess)
-      return RBLN_ERR_LAUNCH;
-    dim3 grid((a.L + BT - 1) / BT, a.H, a.B);
-    sdpa_bwd_q_kernel<D, BF16><<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
-    if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
+    const int rc = a.mask ? launch_q<D, BF16, true>(m, a, st) : launch_q<D, BF16, false>(m, a, st);
+    if (rc != RBLN_OK) return rc;
   }
   return RBLN_OK;
 }
@@ -696,7 +777,7 @@ int rbln_sdpa_bwd(const rbln_sdpa_bwd_params_t* p, cudaStream_t stream) {
   if (p->num_heads > 65535 || p->num_kv_heads > 65535 || p->batch > 65535) return RBLN_ERR_UNSUPPORTED;
   if (!p->q || !p->k || !p->v || !p->out || !p->dout || !p->lse) return RBLN_ERR_INVALID_ARGUMENT;
   if (p->mask && p->mask_stride[3] != 1) return RBLN_ERR_INVALID_ARGUMENT;
-  if (p->dbias && !p->mask_additive) return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->dbias && (!p->mask || !p->mask_additive)) return RBLN_ERR_INVALID_ARGUMENT;
   const void* ptrs[8] = {p->q, p->k, p->v, p->out, p->dout, p->dq, p->dk, p->dv};
   for (const void* q : ptrs)
     if (q && !al16(q)) return RBLN_ERR_INVALID_ARGUMENT;

@@ -171,7 +171,10 @@ struct KvLayout {
   static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
 };
 
-enum KvBar { KB_KV = 0, KB_QF0, KB_QF1, KB_QE0, KB_QE1, KB_SF, KB_PF, KB_DONE, KB_COUNT };
+// SF/PF come in two halves (A: the tile's columns 0-63, B: 64-127): the
+// compute warps of half A start while the tensor cores compute half B, and
+// dV / dK of half A run while the compute warps of half B work.
+enum KvBar { KB_KV = 0, KB_QF0, KB_QF1, KB_QE0, KB_QE1, KB_SFA, KB_SFB, KB_PFA, KB_PFB, KB_DONE, KB_COUNT };
 
 // Tile i of a kv CTA: query head g of the group, query tile qt.
 __device__ __forceinline__ void kv_tile(int i, int per_g, int qt0, int& g, int& qt) {
@@ -218,7 +221,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < KB_COUNT; ++i) mbar_init(bar(i), i == KB_PF ? (uint32_t)kComputeWarps : 1u);
+    for (int i = 0; i < KB_COUNT; ++i)
+      mbar_init(bar(i), (i == KB_PFA || i == KB_PFB) ? (uint32_t)(kComputeWarps / 2) : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -276,8 +280,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
     if (lane == 0 && ntiles > 0) {
-      const uint32_t id_s = idesc_f16(BF16, BT, BT, false);  // S^T, dP^T: both operands K-major over D
-      const uint32_t id_acc = idesc_f16(BF16, BT, D, true);  // dV, dK: B (dO, Q) MN-major
+      const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S^T, dP^T halves: K-major over D
+      const uint32_t id_acc = idesc_f16(BF16, BT, D, true);      // dV, dK: B (dO, Q) MN-major
       bool ok = mbar_wait(bar(KB_KV), 0, abort);
       for (int i = 0; ok && i < ntiles; ++i) {
         const int st = i & 1;
@@ -290,30 +294,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t db = sbase + Lay::DO0 + st * NP * kPanel;
         // (the previous tile's dV / dK MMAs read P^T and dS^T from these
         // buffers; tcgen05.mma runs in issue order, so these writes follow)
+        for (int hh = 0; hh < 2; ++hh) {  // query rows [64 hh, 64 hh + 64) of the tile: 8 KB into each panel
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_f16_ss(t_s, sw128_desc(sbase + Lay::K + off, 16, 1024), sw128_desc(qb + off, 16, 1024), id_s,
-                      kk > 0 ? 1u : 0u);
-        }
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+            umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::K + off, 16, 1024),
+                        sw128_desc(qb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_f16_ss(t_dp, sw128_desc(sbase + Lay::V + off, 16, 1024), sw128_desc(db + off, 16, 1024), id_s,
-                      kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+            umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::V + off, 16, 1024),
+                        sw128_desc(db + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(KB_SFA + hh));
         }
-        umma_commit(bar(KB_SF));
-        if (!mbar_wait(bar(KB_PF), i & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!mbar_wait(bar(KB_PFA + hh), i & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BT / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_f16_ts(t_dv, t_s + kPackOff + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
-          umma_f16_ts(t_dk, t_dp + kPackOff + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+          for (int k4 = 0; k4 < BT / 32; ++k4) {  // the half's 64 query rows: 4 steps of 16
+            const int kk = hh * (BT / 32) + k4;
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_ts(t_dv, t_s + kPackOff + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+            umma_f16_ts(t_dk, t_dp + kPackOff + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+          }
         }
+        if (!ok) break;
         umma_commit(bar(KB_QE0 + st));
       }
       umma_commit(bar(KB_DONE));
@@ -344,7 +354,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // were copied with the tile's Q / dO (QF). tcgen05.ld is .sync.aligned:
       // the whole warp takes the same path.
       if (!__all_sync(0xffffffffu, mbar_wait(bar(KB_QF0 + st), (i >> 1) & 1, abort) &&
-                                       mbar_wait(bar(KB_SF), i & 1, abort))) {
+                                       mbar_wait(bar(KB_SFA + half), i & 1, abort))) {
         ok = false;
         break;
       }
@@ -403,7 +413,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(KB_PF));
+      if (lane == 0) mbar_arrive(bar(KB_PFA + half));
     }
 
     // ------------------------------------------------------------ epilogue
@@ -472,7 +482,7 @@ struct QLayout {
   static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
 };
 
-enum QBar { QB_Q = 0, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SF, QB_PF, QB_DONE, QB_COUNT };
+enum QBar { QB_Q = 0, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SFA, QB_SFB, QB_PFA, QB_PFB, QB_DONE, QB_COUNT };
 
 template <int D, bool BF16, bool MASK>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -498,7 +508,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < QB_COUNT; ++i) mbar_init(bar(i), i == QB_PF ? (uint32_t)kComputeWarps : 1u);
+    for (int i = 0; i < QB_COUNT; ++i)
+      mbar_init(bar(i), (i == QB_PFA || i == QB_PFB) ? (uint32_t)(kComputeWarps / 2) : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -546,8 +557,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && nk > 0) {
-      const uint32_t id_s = idesc_f16(BF16, BT, BT, false);
-      const uint32_t id_dq = idesc_f16(BF16, BT, D, true);  // B (K) MN-major
+      const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S, dP halves (64 keys each)
+      const uint32_t id_dq = idesc_f16(BF16, BT, D, true);       // B (K) MN-major
       bool ok = mbar_wait(bar(QB_Q), 0, abort);
       for (int j = 0; ok && j < nk; ++j) {
         const int st = j & 1;
@@ -558,28 +569,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
         const uint32_t kb = sbase + Lay::K0 + st * NP * kPanel;
         const uint32_t vb = sbase + Lay::V0 + st * NP * kPanel;
+        for (int hh = 0; hh < 2; ++hh) {  // keys [64 hh, 64 hh + 64) of the tile
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_f16_ss(t_s, sw128_desc(sbase + Lay::Q + off, 16, 1024), sw128_desc(kb + off, 16, 1024), id_s,
-                      kk > 0 ? 1u : 0u);
-        }
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+            umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::Q + off, 16, 1024),
+                        sw128_desc(kb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_f16_ss(t_dp, sw128_desc(sbase + Lay::DO + off, 16, 1024), sw128_desc(vb + off, 16, 1024), id_s,
-                      kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+            umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::DO + off, 16, 1024),
+                        sw128_desc(vb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(QB_SFA + hh));
         }
-        umma_commit(bar(QB_SF));
-        if (!mbar_wait(bar(QB_PF), j & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!mbar_wait(bar(QB_PFA + hh), j & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BT / 16; ++kk)
-          umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          for (int k4 = 0; k4 < BT / 32; ++k4) {
+            const int kk = hh * (BT / 32) + k4;
+            umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (!ok) break;
         umma_commit(bar(QB_KE0 + st));
       }
       umma_commit(bar(QB_DONE));
@@ -600,7 +618,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int kt0 = j * BT;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SF), j & 1, abort))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SFA + half), j & 1, abort))) {
         ok = false;
         break;
       }
@@ -651,7 +669,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(QB_PF));
+      if (lane == 0) mbar_arrive(bar(QB_PFA + half));
     }
 
     ok = __all_sync(0xffffffffu, ok);

@@ -92,7 +92,8 @@ typedef struct {
   void* vcache;
   int32_t kv_dtype;
   int64_t cache_stride[3]; /* block, head, token (same for K and V) */
-  /* fp8 only: one fp32 dequant scale per (block, head), K and V separately */
+  /* fp8 only: one fp32 dequant scale per (block, head), K and V separately
+   * (read-only for attention; rbln_paged_kv_write rewrites the touched ones) */
   const float* k_scale;
   const float* v_scale;
   int64_t scale_stride[2]; /* block, head */
@@ -176,6 +177,20 @@ int rbln_paged_causal_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream
  * Same write; attention keeps key t for query row s when
  * mask[b, s, t] > 0 (p->mask required, mask_stride = {batch, query row}). */
 int rbln_paged_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stream);
+
+/* Paged KV-cache write on its own: k_new/v_new [B, Hkv, S = q_len, D]
+ * (strides b, h, s in k_new_stride / v_new_stride) written at positions
+ * [seq[b], seq[b] + S) through the block table -- the append step of the
+ * decode and prefill ops (reference CPU semantics test_custom_kernel.py:63-79,
+ * 182-186), for a cache filled without attending in the same call. q_dtype
+ * is the dtype of k_new / v_new (BF16 / F16). kv_dtype equal to it: a copy.
+ * kv_dtype FP8_E4M3 with k_scale / v_scale [num_blocks, Hkv]: every touched
+ * (block, head) gets scale = max(amax, 1e-6) / 448 over its valid rows (those
+ * the sequence already holds before seq[b], and the new ones); held rows are
+ * re-quantized to the new scale, new rows quantized as x / scale (round to
+ * nearest even, saturated). Rows past the write are left as they are.
+ * No reference counterpart as a separate entry point. */
+int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream_t stream);
 
 /* Dense scaled dot-product attention, forward. */
 typedef struct {

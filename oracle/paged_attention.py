@@ -298,3 +298,47 @@ def mock_prefill_contiguous(q, k, v, kcache, vcache, s, scale, keep_mask):
     w = w + torch.where(keep_mask[:, :, :, :, :partition] > 0, 0.0, -float("inf"))
     w = torch.softmax(w, dim=-1, dtype=torch.float32).to(q.dtype)
     return torch.matmul(w, vs)
+
+
+def kv_write(k_new, v_new, kcache, vcache, seq, block_table, block_size, k_scale=None, v_scale=None):
+    """The paged ops' append step on its own (what rbln_paged_kv_write does).
+
+    k_new / v_new [B, Hkv, 1, S, D] go to positions [seq[b], seq[b] + S) of
+    each sequence through the block table (test_custom_kernel.py:63-79 writes
+    the same rows into the reference's single block). A bf16 / f16 cache
+    takes the values as they are. An fp8-e4m3 cache with scales
+    [num_blocks, Hkv]: for every (block, head) the write touches,
+      amax  = max(|float(e4m3) * old_scale| over the rows the sequence holds
+                  in the block before seq[b], |new values|)
+      scale = max(amax, 1e-6) / 448
+    held rows become e4m3(float(e4m3) * old_scale / scale), new rows
+    e4m3(x / scale) (round to nearest even after saturating to +-448), in
+    float32 with IEEE division. Rows past the write stay as they are.
+    Mutates the caches (and scales).
+    """
+    B, Hkv, _, S, D = k_new.shape
+    seqv = seq.reshape(-1).to(torch.int64)
+    fp8 = kcache.dtype == torch.float8_e4m3fn
+    for b in range(B):
+        s0 = int(seqv[b])
+        row = _bt_row(block_table, b)
+        for bi in range(s0 // block_size, (s0 + S - 1) // block_size + 1):
+            phys = int(row[bi])
+            base = bi * block_size
+            lo, hi = max(s0, base) - base, min(s0 + S, base + block_size) - base
+            held = lo if s0 > base else 0
+            for cache, new, scales in ((kcache, k_new, k_scale), (vcache, v_new, v_scale)):
+                rows_new = new[b, :, 0, base + lo - s0: base + hi - s0, :D]  # [Hkv, n, D]
+                if not fp8:
+                    cache[phys, :, 0, lo:hi, :D] = rows_new.to(cache.dtype)
+                    continue
+                for h in range(Hkv):
+                    old = scales[phys, h].float()
+                    deq = cache[phys, h, 0, :held, :D].float() * old
+                    nv = rows_new[h].float()
+                    amax = torch.cat([deq.abs().reshape(-1), nv.abs().reshape(-1)]).max()
+                    sc = torch.clamp(amax, min=1e-6) / FP8_MAX
+                    if held > 0 and bool(sc != old):
+                        cache[phys, h, 0, :held, :D] = quantize_fp8(deq, sc)
+                    cache[phys, h, 0, lo:hi, :D] = quantize_fp8(nv, sc)
+                    scales[phys, h] = sc

@@ -283,3 +283,20 @@ def test_sdpa_backward_oracle_matches_reference(idx):
         for name, e in zip(("dq", "dk", "dv", "dbias"), ex):
             if c[name] is not None:
                 torch.testing.assert_close(c[name].double(), e.expand_as(c[name]), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("idx", range(len(PREFILL)))
+def test_kv_write_matches_reference_prefill_writes(idx):
+    """The standalone write (oracle.kv_write) leaves the caches exactly as the
+    reference's paged_attn_prefill leaves them (fixture digests), at seq 0 and
+    at seq s1 over a cache already holding s1 rows."""
+    c = PREFILL[idx]
+    D, ms, dt, s1 = c["D"], c["max_seq"], c["dtype"], c["s1"]
+    bt = torch.tensor([0], dtype=torch.int16)
+    for key, s0 in (("paged_attn_prefill_s0", 0), ("paged_attn_prefill_s1", s1)):
+        kc = torch.zeros([1, c["Hkv"], 1, ms, D], dtype=dt)
+        vc = torch.zeros_like(kc)
+        if s0:
+            kc[:, :, :, :s1], vc[:, :, :, :s1] = c["kpre"], c["vpre"]
+        opa.kv_write(c["k"], c["v"], kc, vc, torch.tensor([[s0]], dtype=torch.int32), bt, ms)
+        assert _sha(kc) == c["results"][key]["kc"] and _sha(vc) == c["results"][key]["vc"]

@@ -1,0 +1,202 @@
+// Paged KV-cache write as a standalone kernel: new k/v rows [B, Hkv, S, D]
+// written at logical positions [seq[b], seq[b] + S) of each sequence through
+// the block table. This is the append step the decode and prefill kernels
+// perform in-line (paged_decode.cu append_token, attn_prefill.cu
+// paged_append_kernel; the reference's ops do it inside their compiled
+// graphs, test/rbln/test_custom_kernel.py:63-79, 182-186), for callers that
+// fill a cache without attending in the same call.
+//
+// bf16 / f16 caches: a copy. fp8-e4m3 caches with one fp32 scale per
+// (block, KV head): the scale of every block the write touches is recomputed
+// from the block's valid rows -- the rows the sequence already holds in that
+// block (positions before seq[b]) and the new ones -- as
+// scale = max(amax, 1e-6) / 448; the held rows are re-quantized from the old
+// scale to the new one and the new rows quantized with it (x / scale, round to
+// nearest even, saturated to +-448). Rows of the block past the write are
+// left untouched.
+//
+// One CTA per (touched block slot, KV head x {K, V}, sequence), HBM-bound:
+// every byte of the touched blocks' valid rows is read at most twice (amax,
+// then re-quantization) and written once.
+
+#include "common.cuh"
+
+namespace rbln {
+namespace {
+
+constexpr int kWriteThreads = 256;
+constexpr float kFp8Max = 448.f;
+
+struct WriteArgs {
+  const char* k_new;
+  const char* v_new;
+  int64_t kn_b, kn_h, kn_s, vn_b, vn_h, vn_s;  // bytes
+  char* kcache;
+  char* vcache;
+  int64_t cs_block, cs_head, cs_tok;  // elements
+  float* k_scale;
+  float* v_scale;
+  int64_t ss_block, ss_head;
+  const int32_t* seq;
+  int64_t seq_stride;
+  const void* bt;
+  int bt_dtype;
+  int64_t bt_stride;
+  int B, Hkv, S, D, bs, max_blocks, num_blocks;
+  uint32_t* err;
+};
+
+template <bool IN_BF16>
+__device__ __forceinline__ float new_value(const char* row, int d) {
+  if constexpr (IN_BF16) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[d]);
+  } else {
+    return __half2float(reinterpret_cast<const __half*>(row)[d]);
+  }
+}
+
+__device__ __forceinline__ uint8_t to_e4m3(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float from_e4m3(uint8_t q) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)q, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+__device__ float block_max(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < kWriteThreads / 32 ? red[lane] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <bool IN_BF16, bool FP8>
+__global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const WriteArgs a) {
+  const int j = blockIdx.x, h = blockIdx.y >> 1, part = blockIdx.y & 1, b = blockIdx.z;
+  const int s0 = a.seq[b * a.seq_stride];
+  if (s0 < 0 || (int64_t)s0 + a.S > (int64_t)a.max_blocks * a.bs) {
+    if (threadIdx.x == 0 && j == 0 && blockIdx.y == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_SEQ_RANGE);
+    return;
+  }
+  const int bi = s0 / a.bs + j;
+  if (bi > (s0 + a.S - 1) / a.bs) return;
+  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+  if (phys < 0 || phys >= a.num_blocks) {
+    if (threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    return;
+  }
+  const int base = bi * a.bs;
+  const int lo = max(s0, base) - base;             // first new row in the block
+  const int hi = min(s0 + a.S, base + a.bs) - base;  // one past the last
+  const int held = s0 > base ? lo : 0;             // rows [0, held) hold the sequence's context
+  const char* src = part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h : a.v_new + b * a.vn_b + h * a.vn_h;
+  const int64_t src_s = part == 0 ? a.kn_s : a.vn_s;
+  char* cache = part == 0 ? a.kcache : a.vcache;
+  const int64_t cbase = phys * a.cs_block + (int64_t)h * a.cs_head;  // elements
+  const int D = a.D;
+
+  if constexpr (!FP8) {
+    // 16-byte chunks of the new rows
+    const int cpr = D * 2 / 16;
+    for (int i = threadIdx.x; i < (hi - lo) * cpr; i += kWriteThreads) {
+      const int r = lo + i / cpr, c = i % cpr;
+      const uint4 v = *reinterpret_cast<const uint4*>(src + (int64_t)(base + r - s0) * src_s + c * 16);
+      *reinterpret_cast<uint4*>(cache + (cbase + (int64_t)r * a.cs_tok) * 2 + c * 16) = v;
+    }
+  } else {
+    __shared__ float red[kWriteThreads / 32];
+    float* scales = part == 0 ? a.k_scale : a.v_scale;
+    float* sp = scales + phys * a.ss_block + (int64_t)h * a.ss_head;
+    const float old = *sp;
+    uint8_t* c8 = reinterpret_cast<uint8_t*>(cache) + cbase;
+    float m = 0.f;
+    for (int i = threadIdx.x; i < held * D; i += kWriteThreads) {
+      const int r = i / D, d = i % D;
+      m = fmaxf(m, fabsf(from_e4m3(c8[(int64_t)r * a.cs_tok + d]) * old));
+    }
+    for (int i = threadIdx.x; i < (hi - lo) * D; i += kWriteThreads) {
+      const int r = lo + i / D, d = i % D;
+      m = fmaxf(m, fabsf(new_value<IN_BF16>(src + (int64_t)(base + r - s0) * src_s, d)));
+    }
+    const float amax = block_max(m, red);
+    const float scale = __fdiv_rn(fmaxf(amax, 1e-6f), kFp8Max);
+    if (held > 0 && scale != old) {
+      for (int i = threadIdx.x; i < held * D; i += kWriteThreads) {
+        const int r = i / D, d = i % D;
+        uint8_t* q = c8 + (int64_t)r * a.cs_tok + d;
+        *q = to_e4m3(__fdiv_rn(from_e4m3(*q) * old, scale));
+      }
+    }
+    for (int i = threadIdx.x; i < (hi - lo) * D; i += kWriteThreads) {
+      const int r = lo + i / D, d = i % D;
+      const float x = new_value<IN_BF16>(src + (int64_t)(base + r - s0) * src_s, d);
+      c8[(int64_t)r * a.cs_tok + d] = to_e4m3(__fdiv_rn(x, scale));
+    }
+    __syncthreads();  // every thread has read `old` before it is replaced
+    if (threadIdx.x == 0) *sp = scale;
+  }
+}
+
+}  // namespace
+}  // namespace rbln
+
+extern "C" int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream_t stream) {
+  using namespace rbln;
+  if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->q_len < 0 || p->block_size <= 0 || p->max_blocks <= 0 ||
+      p->num_blocks <= 0)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->batch == 0 || p->q_len == 0) return RBLN_OK;
+  if (p->head_dim != 64 && p->head_dim != 128) return RBLN_ERR_UNSUPPORTED;
+  if (p->q_dtype != RBLN_DT_BF16 && p->q_dtype != RBLN_DT_F16) return RBLN_ERR_UNSUPPORTED;
+  const bool fp8 = p->kv_dtype == RBLN_DT_FP8_E4M3;
+  if (!fp8 && p->kv_dtype != p->q_dtype) return RBLN_ERR_UNSUPPORTED;
+  if (!p->k_new || !p->v_new || !p->kcache || !p->vcache || !p->seq || !p->block_table)
+    return RBLN_ERR_INVALID_ARGUMENT;
+  if (fp8 && (!p->k_scale || !p->v_scale)) return RBLN_ERR_INVALID_ARGUMENT;
+  if (p->block_table_dtype != RBLN_DT_I16 && p->block_table_dtype != RBLN_DT_I32 &&
+      p->block_table_dtype != RBLN_DT_I64)
+    return RBLN_ERR_UNSUPPORTED;
+  if (!fp8) {  // 16-byte vector copies
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (!al(p->k_new) || !al(p->v_new) || !al(p->kcache) || !al(p->vcache)) return RBLN_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < 3; ++i)
+      if ((p->k_new_stride[i] * 2) % 16 || (p->v_new_stride[i] * 2) % 16 || (p->cache_stride[i] * 2) % 16)
+        return RBLN_ERR_INVALID_ARGUMENT;
+  }
+  WriteArgs a{};
+  a.k_new = static_cast<const char*>(p->k_new);
+  a.v_new = static_cast<const char*>(p->v_new);
+  a.kn_b = p->k_new_stride[0] * 2; a.kn_h = p->k_new_stride[1] * 2; a.kn_s = p->k_new_stride[2] * 2;
+  a.vn_b = p->v_new_stride[0] * 2; a.vn_h = p->v_new_stride[1] * 2; a.vn_s = p->v_new_stride[2] * 2;
+  a.kcache = static_cast<char*>(p->kcache);
+  a.vcache = static_cast<char*>(p->vcache);
+  a.cs_block = p->cache_stride[0]; a.cs_head = p->cache_stride[1]; a.cs_tok = p->cache_stride[2];
+  a.k_scale = const_cast<float*>(p->k_scale);
+  a.v_scale = const_cast<float*>(p->v_scale);
+  a.ss_block = p->scale_stride[0]; a.ss_head = p->scale_stride[1];
+  a.seq = p->seq; a.seq_stride = p->seq_stride;
+  a.bt = p->block_table; a.bt_dtype = p->block_table_dtype; a.bt_stride = p->block_table_stride;
+  a.B = p->batch; a.Hkv = p->num_kv_heads; a.S = p->q_len; a.D = p->head_dim; a.bs = p->block_size;
+  a.max_blocks = p->max_blocks; a.num_blocks = p->num_blocks;
+  a.err = p->error_flags;
+  // blocks one sequence's write can touch: S rows starting anywhere in a block
+  const int slots = (p->q_len + p->block_size - 1) / p->block_size + 1;
+  if (p->num_kv_heads * 2 > 65535 || p->batch > 65535) return RBLN_ERR_UNSUPPORTED;
+  dim3 grid(slots, p->num_kv_heads * 2, p->batch);
+  const bool bf = p->q_dtype == RBLN_DT_BF16;
+  if (fp8) {
+    if (bf) paged_kv_write_kernel<true, true><<<grid, kWriteThreads, 0, stream>>>(a);
+    else paged_kv_write_kernel<false, true><<<grid, kWriteThreads, 0, stream>>>(a);
+  } else {
+    if (bf) paged_kv_write_kernel<true, false><<<grid, kWriteThreads, 0, stream>>>(a);
+    else paged_kv_write_kernel<false, false><<<grid, kWriteThreads, 0, stream>>>(a);
+  }
+  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+}

@@ -306,6 +306,81 @@ at::Tensor paged_causal_attn_prefill_cuda(const at::Tensor& q, const at::Tensor&
   return run_prefill(c, op, false);
 }
 
+// rbln_attn::paged_kv_write: the paged ops' append step on its own (k, v
+// [B, Hkv, 1, S, D] at positions [seq[b], seq[b] + S)); fp8 caches take
+// k_scale / v_scale [num_blocks, Hkv] and get per-(block, head) scales
+// recomputed (rbln_paged_kv_write, kv_write.cu).
+void paged_kv_write_cuda(const at::Tensor& k_in, const at::Tensor& v_in, at::Tensor& kcache, at::Tensor& vcache,
+                         const at::Tensor& seq_in, const at::Tensor& block_table_in, int64_t block_size,
+                         const std::optional<at::Tensor>& k_scale, const std::optional<at::Tensor>& v_scale) {
+  const char* op = "paged_kv_write";
+  TORCH_CHECK(k_in.is_cuda() && k_in.dim() == 5 && v_in.sizes() == k_in.sizes() && k_in.size(2) == 1, op,
+              ": k/v must be CUDA [B, Hkv, 1, S, D]");
+  TORCH_CHECK(kcache.dim() == 5 && kcache.sizes() == vcache.sizes() && kcache.strides() == vcache.strides() &&
+                  kcache.stride(-1) == 1 && kcache.size(3) == block_size && kcache.device() == k_in.device(),
+              op, ": caches must be [num_blocks, Hkv, 1, block_size, D] on k's device, alike");
+  const auto dt = k_in.scalar_type();
+  TORCH_CHECK((dt == at::kBFloat16 || dt == at::kHalf) && v_in.scalar_type() == dt, op, ": k/v bf16 or f16");
+  const bool fp8 = kcache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || kcache.scalar_type() == dt, op, ": cache dtype must be k's or float8_e4m3fn");
+  TORCH_CHECK(vcache.scalar_type() == kcache.scalar_type(), op, ": kcache and vcache dtypes differ");
+  at::Tensor k = k_in.contiguous(), v = v_in.contiguous();
+  const int64_t B = k.size(0), Hkv = k.size(1), S = k.size(3), D = k.size(4);
+  TORCH_CHECK(kcache.size(1) == Hkv && kcache.size(-1) == D, op, ": cache heads / head_dim differ from k's");
+  at::Tensor seq = on_device(seq_in, k).reshape({-1}).to(at::kInt).contiguous();
+  TORCH_CHECK(seq.numel() == B, op, ": seq must hold one entry per sequence");
+  at::Tensor bt = on_device(block_table_in, k);
+  if (bt.dim() == 1) bt = bt.unsqueeze(0);
+  TORCH_CHECK(bt.dim() == 2 && (bt.size(0) == B || bt.size(0) == 1), op, ": block_table must be [B, max_blocks]");
+  if (bt.stride(1) != 1) bt = bt.contiguous();
+  rbln_paged_attn_params_t p{};
+  p.batch = (int32_t)B;
+  p.num_kv_heads = (int32_t)Hkv;
+  p.group = 1;
+  p.q_len = (int32_t)S;
+  p.head_dim = (int32_t)D;
+  p.num_blocks = (int32_t)kcache.size(0);
+  p.block_size = (int32_t)block_size;
+  p.max_blocks = (int32_t)bt.size(1);
+  p.q_dtype = to_rbln_dtype(dt);
+  p.k_new = k.data_ptr();
+  p.v_new = v.data_ptr();
+  p.k_new_stride[0] = k.stride(0); p.k_new_stride[1] = k.stride(1); p.k_new_stride[2] = k.stride(3);
+  p.v_new_stride[0] = v.stride(0); p.v_new_stride[1] = v.stride(1); p.v_new_stride[2] = v.stride(3);
+  p.kcache = kcache.data_ptr();
+  p.vcache = vcache.data_ptr();
+  p.kv_dtype = to_rbln_dtype(kcache.scalar_type());
+  p.cache_stride[0] = kcache.stride(0); p.cache_stride[1] = kcache.stride(1); p.cache_stride[2] = kcache.stride(3);
+  if (fp8) {
+    TORCH_CHECK(k_scale.has_value() && v_scale.has_value() && k_scale->scalar_type() == at::kFloat &&
+                    v_scale->scalar_type() == at::kFloat && k_scale->dim() == 2 &&
+                    k_scale->size(0) == kcache.size(0) && k_scale->size(1) == Hkv &&
+                    v_scale->sizes() == k_scale->sizes() && v_scale->strides() == k_scale->strides() &&
+                    k_scale->device() == k.device() && v_scale->device() == k.device(),
+                op, ": fp8 caches need float32 k_scale / v_scale [num_blocks, Hkv] on the caches' device");
+    p.k_scale = k_scale->data_ptr<float>();
+    p.v_scale = v_scale->data_ptr<float>();
+    p.scale_stride[0] = k_scale->stride(0);
+    p.scale_stride[1] = k_scale->stride(1);
+  }
+  p.seq = seq.data_ptr<int32_t>();
+  p.seq_stride = 1;
+  p.block_table = bt.data_ptr();
+  p.block_table_dtype = to_rbln_dtype(bt.scalar_type());
+  p.block_table_stride = bt.size(0) == 1 ? 0 : bt.stride(0);
+  at::Tensor err;
+  if (debug_checks()) {
+    err = at::zeros({1}, k.options().dtype(at::kInt));
+    p.error_flags = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  }
+  c10::cuda::CUDAGuard guard(k.device());
+  check_rc(rbln_paged_kv_write(&p, at::cuda::getCurrentCUDAStream(k.device().index()).stream()), op);
+  if (err.defined()) {
+    const int flags = err.item<int>();
+    TORCH_CHECK(flags == 0, op, ": device-side input check failed (flags 0x", std::hex, flags, ")");
+  }
+}
+
 // ---------------------------------------------------------------------------
 // flash_attention_naive_{prefill,decode}: the unified-cache form of the paged
 // ops (torch_rbln/_internal/register_custom_ops.py:453-560; CPU semantics in
@@ -631,7 +706,12 @@ bool sdpa_route_enabled() { return g_sdpa_route.load(); }
 TORCH_LIBRARY(rbln_attn, m) {
   m.def("set_sdpa_route(bool enabled) -> ()");
   m.def("sdpa_route_enabled() -> bool");
+  m.def(
+      "paged_kv_write(Tensor k, Tensor v, Tensor(a!) kcache, Tensor(b!) vcache, Tensor seq, Tensor block_table, "
+      "SymInt block_size, Tensor(c!)? k_scale=None, Tensor(d!)? v_scale=None) -> ()");
 }
+
+TORCH_LIBRARY_IMPL(rbln_attn, CUDA, m) { m.impl("paged_kv_write", &paged_kv_write_cuda); }
 
 TORCH_LIBRARY_IMPL(rbln_attn, CompositeExplicitAutograd, m) {
   m.impl("set_sdpa_route", &set_sdpa_route);

@@ -121,6 +121,7 @@ ENTRY_POINTS = {
                                                          ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_paged_causal_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
+    "rbln_paged_kv_write": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
     "rbln_sdpa_fwd": (ctypes.c_int, [ctypes.POINTER(SdpaParams), c_vp]),
     "rbln_sdpa_bwd_workspace_size": (ctypes.c_int, [ctypes.POINTER(SdpaBwdParams), ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_sdpa_bwd": (ctypes.c_int, [ctypes.POINTER(SdpaBwdParams), c_vp]),

@@ -857,19 +857,175 @@ def run_reference_compute(args, wl_name):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# standalone KV-cache write (HBM-bound)
+# ---------------------------------------------------------------------------
+KVWRITE = {
+    "kv_write_fp8": dict(B=64, Hkv=8, D=128, bs=16, S=512, cmax=4096,
+                         desc="paged KV write bf16 -> fp8-e4m3 cache, per-(block, head) scale recompute: B=64 "
+                              "sequences x 512 new rows, Hkv=8, D=128, bs=16, start ~U[0,4096]"),
+}
+
+
+def build_kv_write(wl, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    B, Hkv, D, bs, S = wl["B"], wl["Hkv"], wl["D"], wl["bs"], wl["S"]
+    starts = torch.randint(0, wl["cmax"] + 1, (B,), generator=g).to(torch.int32)
+    mb = (wl["cmax"] + S) // bs + 2
+    nblk = B * mb
+    bt = torch.randperm(nblk, generator=g).reshape(B, mb).to(torch.int32)
+    k = torch.randn([B, Hkv, 1, S, D], generator=g).to(torch.bfloat16)
+    v = torch.randn([B, Hkv, 1, S, D], generator=g).to(torch.bfloat16)
+    held = (starts % bs).to(torch.int64)
+    # new rows read (bf16) + written (fp8), K and V; held rows of the first
+    # block read and re-written; the touched blocks' two scales
+    touched = sum(((int(s0) + S - 1) // bs - int(s0) // bs + 1) for s0 in starts)
+    nbytes = 2 * Hkv * (B * S * D * 3 + int(held.sum()) * D * 2) + 2 * Hkv * touched * 8
+    return dict(k=k, v=v, seq=starts, bt=bt, nblk=nblk, bytes=nbytes, B=B, Hkv=Hkv, D=D, bs=bs, S=S)
+
+
+def _cpu_kv_write(d, budget_s):
+    """oracle.paged_attention.kv_write on one sequence (all KV heads)."""
+    from oracle import paged_attention as opa
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    per_seq = d["bytes"] / d["B"]
+    kc = torch.zeros([d["nblk"], d["Hkv"], 1, d["bs"], d["D"]], dtype=torch.float8_e4m3fn)
+    vc = kc.clone()
+    ks, vs = torch.ones(d["nblk"], d["Hkv"]), torch.ones(d["nblk"], d["Hkv"])
+    times = []
+    t_end = time.perf_counter() + budget_s
+    b = 0
+    while True:
+        t = time.perf_counter()
+        opa.kv_write(d["k"][b:b + 1], d["v"][b:b + 1], kc, vc, d["seq"][b:b + 1], d["bt"][b:b + 1], d["bs"], ks, vs)
+        times.append(time.perf_counter() - t)
+        b = (b + 1) % d["B"]
+        if time.perf_counter() > t_end or len(times) >= d["B"]:
+            break
+    med = statistics.median(times)
+    return per_seq / med / 1e9, med, len(times)
+
+
+def run_kv_write(args, wl_name):
+    import ctypes
+
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        wl = KVWRITE[wl_name]
+        d = build_kv_write(wl)
+        val, med, n = _cpu_kv_write(d, max(10.0, args.cpu_budget))
+        sample = f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, median of {n} runs"
+        print(json.dumps({"impl": "reference", "metric": "paged KV write GB/s", "value": round(val, 4),
+                          "unit": "GB/s", "n_gpus": ws, "steps": n, "warmup": args.warmup,
+                          "ms_per_step": round(med * 1e3 * d["B"], 3), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)",
+                          "config": {"workload": wl["desc"]},
+                          "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                           "kind": "port", "sample": sample},
+                          "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch_rbln_b200  # noqa: F401
+    from torch_rbln_b200 import cabi
+
+    wl = KVWRITE[wl_name]
+    d = build_kv_write(wl, seed=1000 * rank)
+    k, v, seq, bt = (d[x].to(dev) for x in ("k", "v", "seq", "bt"))
+    shape = [d["nblk"], d["Hkv"], 1, d["bs"], d["D"]]
+    kc = torch.zeros(shape, dtype=torch.float8_e4m3fn, device=dev)
+    vc = torch.zeros_like(kc)
+    ks = torch.ones(d["nblk"], d["Hkv"], device=dev)
+    vs = torch.ones_like(ks)
+    qshape = torch.empty([d["B"], d["Hkv"], 1, d["S"], d["D"]], dtype=torch.bfloat16, device=dev)
+    p, keep = cabi.paged_params(qshape, k, v, kc, vc, seq, bt, d["bs"], 1.0, k_scale=ks, v_scale=vs)
+    L = cabi.lib()
+    stream = torch.cuda.current_stream(dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    pref = ctypes.byref(p)
+
+    def step():
+        rc = L.rbln_paged_kv_write(pref, sh)
+        if rc != 0:
+            raise RuntimeError(f"rbln_paged_kv_write failed: {rc}")
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        op_ms, _ = _timed_kernel_loop(args, stream, step, step, flush)
+    # e2e: the torch op with k / v / seq / block_table from pinned host memory, the scales read back
+    pinned = [d[x].pin_memory() for x in ("k", "v", "seq", "bt")]
+    hks = torch.empty(ks.shape, dtype=ks.dtype).pin_memory()
+    hvs = torch.empty(vs.shape, dtype=vs.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = hks.numel() * 4 * 2
+
+    def e2e_step():
+        kk, vv, ss, bb = (t.to(dev, non_blocking=True) for t in pinned)
+        torch.ops.rbln_attn.paged_kv_write(kk, vv, kc, vc, ss, bb, d["bs"], ks, vs)
+        hks.copy_(ks, non_blocking=True)
+        hvs.copy_(vs, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    hbm_peak, _, peak_src = load_peaks()
+    gbs = d["bytes"] / (op_ms * 1e-3) / 1e9
+    line = {
+        "metric": "paged KV write GB/s", "value": round(ws * gbs, 1), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(op_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded N(0,1) rows, seeded starts and block-table permutation)",
+        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}",
+                   "l2": "L2 flushed between iterations (256 MB write, outside the timed events)",
+                   "bytes_per_step": d["bytes"]},
+        "e2e": {"value": round(ws * d["bytes"] / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "torch.ops.rbln_attn.paged_kv_write"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(gbs / hbm_peak, 4), "traffic": None,
+                     "kernel": "paged_kv_write_kernel<bf16, fp8>", "kernel_ms": round(op_ms, 4),
+                     "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                                     else "fallback 6.65 TB/s")},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        val, med, n = _cpu_kv_write(build_kv_write(wl), args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, "
+                                          f"median of {n} runs, {med * 1e3:.1f} ms"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(COMPUTE))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(COMPUTE) + sorted(KVWRITE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in COMPUTE:
+    if args.workload in KVWRITE:
+        run_kv_write(args, args.workload)
+    elif args.workload in COMPUTE:
         (run_reference_compute if args.impl == "reference" else run_compute_ours)(args, args.workload)
     elif args.impl == "reference":
         run_reference(args, args.workload)

@@ -187,8 +187,9 @@ int rbln_paged_attn_prefill(const rbln_paged_attn_params_t* p, cudaStream_t stre
  * kv_dtype FP8_E4M3 with k_scale / v_scale [num_blocks, Hkv]: every touched
  * (block, head) gets scale = max(amax, 1e-6) / 448 over its valid rows (those
  * the sequence already holds before seq[b], and the new ones); held rows are
- * re-quantized to the new scale, new rows quantized as x / scale (round to
- * nearest even, saturated). Rows past the write are left as they are.
+ * re-quantized to the new scale, new rows quantized as x * (1 / scale) in
+ * float32 (round to nearest even, saturated). Rows past the write are left
+ * as they are.
  * No reference counterpart as a separate entry point. */
 int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream_t stream);
 

@@ -311,9 +311,9 @@ def kv_write(k_new, v_new, kcache, vcache, seq, block_table, block_size, k_scale
       amax  = max(|float(e4m3) * old_scale| over the rows the sequence holds
                   in the block before seq[b], |new values|)
       scale = max(amax, 1e-6) / 448
-    held rows become e4m3(float(e4m3) * old_scale / scale), new rows
-    e4m3(x / scale) (round to nearest even after saturating to +-448), in
-    float32 with IEEE division. Rows past the write stay as they are.
+    held rows become e4m3(float(e4m3) * old_scale * inv), new rows
+    e4m3(x * inv), inv = 1 / scale rounded once to float32 (round to nearest
+    even after saturating to +-448). Rows past the write stay as they are.
     Mutates the caches (and scales).
     """
     B, Hkv, _, S, D = k_new.shape
@@ -338,7 +338,12 @@ def kv_write(k_new, v_new, kcache, vcache, seq, block_table, block_size, k_scale
                     nv = rows_new[h].float()
                     amax = torch.cat([deq.abs().reshape(-1), nv.abs().reshape(-1)]).max()
                     sc = torch.clamp(amax, min=1e-6) / FP8_MAX
+                    inv = 1.0 / sc
+
+                    def q8(x):
+                        return (x * inv).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
                     if held > 0 and bool(sc != old):
-                        cache[phys, h, 0, :held, :D] = quantize_fp8(deq, sc)
-                    cache[phys, h, 0, lo:hi, :D] = quantize_fp8(nv, sc)
+                        cache[phys, h, 0, :held, :D] = q8(deq)
+                    cache[phys, h, 0, lo:hi, :D] = q8(nv)
                     scales[phys, h] = sc

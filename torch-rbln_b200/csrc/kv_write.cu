@@ -11,13 +11,15 @@
 // from the block's valid rows -- the rows the sequence already holds in that
 // block (positions before seq[b]) and the new ones -- as
 // scale = max(amax, 1e-6) / 448; the held rows are re-quantized from the old
-// scale to the new one and the new rows quantized with it (x / scale, round to
-// nearest even, saturated to +-448). Rows of the block past the write are
-// left untouched.
+// scale to the new one and the new rows quantized with it (x * (1 / scale)
+// in float32, round to nearest even, saturated to +-448). Rows of the block
+// past the write are left untouched.
 //
-// One CTA per (touched block slot, KV head x {K, V}, sequence), HBM-bound:
-// every byte of the touched blocks' valid rows is read at most twice (amax,
-// then re-quantization) and written once.
+// One warp per (touched block slot, KV head, K or V, sequence), HBM-bound:
+// 16-byte loads of the new rows, an amax by warp shuffles, then one
+// correctly rounded reciprocal of the scale per block and one multiply per
+// element (q = e4m3(x * (1 / scale))). New rows are read twice (amax, then
+// quantization; the second read mostly hits L2) and written once.
 
 #include "common.cuh"
 
@@ -46,101 +48,129 @@ struct WriteArgs {
   uint32_t* err;
 };
 
-template <bool IN_BF16>
-__device__ __forceinline__ float new_value(const char* row, int d) {
-  if constexpr (IN_BF16) {
-    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[d]);
-  } else {
-    return __half2float(reinterpret_cast<const __half*>(row)[d]);
-  }
-}
-
-__device__ __forceinline__ uint8_t to_e4m3(float x) {
-  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
-}
 __device__ __forceinline__ float from_e4m3(uint8_t q) {
   const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)q, __NV_E4M3);
   return __half2float(__half(h));
 }
 
-__device__ float block_max(float v, float* red) {
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    v = lane < kWriteThreads / 32 ? red[lane] : 0.f;
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red[0] = v;
+// 8 new values (16 bytes of bf16 / f16) as floats
+template <bool IN_BF16>
+__device__ __forceinline__ void unpack8(uint4 w, float (&x)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<IN_BF16>(u[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
   }
-  __syncthreads();
-  return red[0];
+}
+// 8 e4m3 values (8 bytes) as floats, times `s`
+__device__ __forceinline__ void unpack8_e4m3(uint2 w, float s, float (&x)[8]) {
+  const uint32_t u[2] = {w.x, w.y};
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[4 * i + k] = from_e4m3((uint8_t)(u[i] >> (8 * k))) * s;
+}
+// round to nearest even after saturating to +-448, 8 values -> 8 bytes
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&x)[8], float inv) {
+  uint32_t u[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i] * inv, x[4 * i + 1] * inv), __NV_SATFINITE,
+                                                 __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i + 2] * inv, x[4 * i + 3] * inv),
+                                                 __NV_SATFINITE, __NV_E4M3);
+    u[i] = (lo & 0xffffu) | (hi << 16);
+  }
+  return make_uint2(u[0], u[1]);
 }
 
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per (touched block slot j, KV head h, K or V, sequence b); the
+// block's rows are walked in 8-element chunks, lane-strided, so a warp moves
+// 512 contiguous source bytes per step.
 template <bool IN_BF16, bool FP8>
-__global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const WriteArgs a) {
-  const int j = blockIdx.x, h = blockIdx.y >> 1, part = blockIdx.y & 1, b = blockIdx.z;
+__global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const WriteArgs a, int slots) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * (kWriteThreads / 32) + warp;
+  const int64_t units = (int64_t)slots * a.Hkv * 2 * a.B;
+  if (unit >= units) return;
+  const int j = (int)(unit % slots);
+  const int64_t rest = unit / slots;
+  const int part = (int)(rest & 1), h = (int)((rest >> 1) % a.Hkv), b = (int)(rest / (2 * a.Hkv));
   const int s0 = a.seq[b * a.seq_stride];
   if (s0 < 0 || (int64_t)s0 + a.S > (int64_t)a.max_blocks * a.bs) {
-    if (threadIdx.x == 0 && j == 0 && blockIdx.y == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_SEQ_RANGE);
+    if (lane == 0 && j == 0 && h == 0 && part == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_SEQ_RANGE);
     return;
   }
   const int bi = s0 / a.bs + j;
   if (bi > (s0 + a.S - 1) / a.bs) return;
   const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
   if (phys < 0 || phys >= a.num_blocks) {
-    if (threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
     return;
   }
   const int base = bi * a.bs;
-  const int lo = max(s0, base) - base;             // first new row in the block
+  const int lo = max(s0, base) - base;               // first new row in the block
   const int hi = min(s0 + a.S, base + a.bs) - base;  // one past the last
-  const int held = s0 > base ? lo : 0;             // rows [0, held) hold the sequence's context
+  const int held = s0 > base ? lo : 0;               // rows [0, held) hold the sequence's context
   const char* src = part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h : a.v_new + b * a.vn_b + h * a.vn_h;
   const int64_t src_s = part == 0 ? a.kn_s : a.vn_s;
   char* cache = part == 0 ? a.kcache : a.vcache;
   const int64_t cbase = phys * a.cs_block + (int64_t)h * a.cs_head;  // elements
-  const int D = a.D;
+  const int cpr = a.D / 8;                                           // 8-element chunks per row
+  auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
 
   if constexpr (!FP8) {
-    // 16-byte chunks of the new rows
-    const int cpr = D * 2 / 16;
-    for (int i = threadIdx.x; i < (hi - lo) * cpr; i += kWriteThreads) {
-      const int r = lo + i / cpr, c = i % cpr;
-      const uint4 v = *reinterpret_cast<const uint4*>(src + (int64_t)(base + r - s0) * src_s + c * 16);
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      const uint4 v = *reinterpret_cast<const uint4*>(new_row(r) + c * 16);
       *reinterpret_cast<uint4*>(cache + (cbase + (int64_t)r * a.cs_tok) * 2 + c * 16) = v;
     }
   } else {
-    __shared__ float red[kWriteThreads / 32];
-    float* scales = part == 0 ? a.k_scale : a.v_scale;
-    float* sp = scales + phys * a.ss_block + (int64_t)h * a.ss_head;
+    float* sp = (part == 0 ? a.k_scale : a.v_scale) + phys * a.ss_block + (int64_t)h * a.ss_head;
     const float old = *sp;
     uint8_t* c8 = reinterpret_cast<uint8_t*>(cache) + cbase;
     float m = 0.f;
-    for (int i = threadIdx.x; i < held * D; i += kWriteThreads) {
-      const int r = i / D, d = i % D;
-      m = fmaxf(m, fabsf(from_e4m3(c8[(int64_t)r * a.cs_tok + d]) * old));
+    for (int i = lane; i < held * cpr; i += 32) {
+      const int r = i / cpr, c = i - r * cpr;
+      float x[8];
+      unpack8_e4m3(*reinterpret_cast<const uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8), old, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
-    for (int i = threadIdx.x; i < (hi - lo) * D; i += kWriteThreads) {
-      const int r = lo + i / D, d = i % D;
-      m = fmaxf(m, fabsf(new_value<IN_BF16>(src + (int64_t)(base + r - s0) * src_s, d)));
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
-    const float amax = block_max(m, red);
-    const float scale = __fdiv_rn(fmaxf(amax, 1e-6f), kFp8Max);
+    const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
+    const float inv = __frcp_rn(scale);
     if (held > 0 && scale != old) {
-      for (int i = threadIdx.x; i < held * D; i += kWriteThreads) {
-        const int r = i / D, d = i % D;
-        uint8_t* q = c8 + (int64_t)r * a.cs_tok + d;
-        *q = to_e4m3(__fdiv_rn(from_e4m3(*q) * old, scale));
+      for (int i = lane; i < held * cpr; i += 32) {
+        const int r = i / cpr, c = i - r * cpr;
+        uint2* q = reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8);
+        float x[8];
+        unpack8_e4m3(*q, old, x);
+        *q = pack8_e4m3(x, inv);
       }
     }
-    for (int i = threadIdx.x; i < (hi - lo) * D; i += kWriteThreads) {
-      const int r = lo + i / D, d = i % D;
-      const float x = new_value<IN_BF16>(src + (int64_t)(base + r - s0) * src_s, d);
-      c8[(int64_t)r * a.cs_tok + d] = to_e4m3(__fdiv_rn(x, scale));
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
     }
-    __syncthreads();  // every thread has read `old` before it is replaced
-    if (threadIdx.x == 0) *sp = scale;
+    __syncwarp();  // every lane has read `old` before it is replaced
+    if (lane == 0) *sp = scale;
   }
 }
 
@@ -163,11 +193,14 @@ extern "C" int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream
   if (p->block_table_dtype != RBLN_DT_I16 && p->block_table_dtype != RBLN_DT_I32 &&
       p->block_table_dtype != RBLN_DT_I64)
     return RBLN_ERR_UNSUPPORTED;
-  if (!fp8) {  // 16-byte vector copies
-    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-    if (!al(p->k_new) || !al(p->v_new) || !al(p->kcache) || !al(p->vcache)) return RBLN_ERR_INVALID_ARGUMENT;
+  {  // 16-byte vector loads of the new rows; 16-byte (copy) or 8-byte (fp8) stores
+    auto al = [](const void* q, unsigned m) { return (reinterpret_cast<uintptr_t>(q) & m) == 0; };
+    const unsigned cm = fp8 ? 7u : 15u;
+    const int csz = fp8 ? 1 : 2;
+    if (!al(p->k_new, 15u) || !al(p->v_new, 15u) || !al(p->kcache, cm) || !al(p->vcache, cm))
+      return RBLN_ERR_INVALID_ARGUMENT;
     for (int i = 0; i < 3; ++i)
-      if ((p->k_new_stride[i] * 2) % 16 || (p->v_new_stride[i] * 2) % 16 || (p->cache_stride[i] * 2) % 16)
+      if ((p->k_new_stride[i] * 2) % 16 || (p->v_new_stride[i] * 2) % 16 || (p->cache_stride[i] * csz) % (cm + 1))
         return RBLN_ERR_INVALID_ARGUMENT;
   }
   WriteArgs a{};
@@ -188,15 +221,17 @@ extern "C" int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream
   a.err = p->error_flags;
   // blocks one sequence's write can touch: S rows starting anywhere in a block
   const int slots = (p->q_len + p->block_size - 1) / p->block_size + 1;
-  if (p->num_kv_heads * 2 > 65535 || p->batch > 65535) return RBLN_ERR_UNSUPPORTED;
-  dim3 grid(slots, p->num_kv_heads * 2, p->batch);
+  const int64_t units = (int64_t)slots * p->num_kv_heads * 2 * p->batch;
+  const int64_t ctas = (units + kWriteThreads / 32 - 1) / (kWriteThreads / 32);
+  if (ctas > INT32_MAX) return RBLN_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)ctas);
   const bool bf = p->q_dtype == RBLN_DT_BF16;
   if (fp8) {
-    if (bf) paged_kv_write_kernel<true, true><<<grid, kWriteThreads, 0, stream>>>(a);
-    else paged_kv_write_kernel<false, true><<<grid, kWriteThreads, 0, stream>>>(a);
+    if (bf) paged_kv_write_kernel<true, true><<<grid, kWriteThreads, 0, stream>>>(a, slots);
+    else paged_kv_write_kernel<false, true><<<grid, kWriteThreads, 0, stream>>>(a, slots);
   } else {
-    if (bf) paged_kv_write_kernel<true, false><<<grid, kWriteThreads, 0, stream>>>(a);
-    else paged_kv_write_kernel<false, false><<<grid, kWriteThreads, 0, stream>>>(a);
+    if (bf) paged_kv_write_kernel<true, false><<<grid, kWriteThreads, 0, stream>>>(a, slots);
+    else paged_kv_write_kernel<false, false><<<grid, kWriteThreads, 0, stream>>>(a, slots);
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }

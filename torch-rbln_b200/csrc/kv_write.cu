@@ -19,8 +19,7 @@
 // 16-byte loads of the new rows, an amax by warp shuffles, then one
 // correctly rounded reciprocal of the scale per block and one multiply per
 // element (q = e4m3(x * (1 / scale))). New rows are read twice (amax, then
-// quantization, unless they fit in the warp's registers: up to 8 16-byte
-// chunks per lane, e.g. a 16-row block of D = 128) and written once.
+// quantization; the second read mostly hits L2) and written once.
 
 #include "common.cuh"
 
@@ -129,7 +128,6 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
   auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
 
   if constexpr (!FP8) {
-#pragma unroll 4
     for (int i = lane; i < (hi - lo) * cpr; i += 32) {
       const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
       const uint4 v = *reinterpret_cast<const uint4*>(new_row(r) + c * 16);
@@ -147,38 +145,12 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
 #pragma unroll
       for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
-    const int nnew = (hi - lo) * cpr;
-    // up to kRegChunks chunks per lane stay in registers between the amax and
-    // the stores: all loads issue back to back and the rows are read once
-    constexpr int kRegChunks = 8;
-    const bool in_regs = nnew <= kRegChunks * 32;
-    uint4 keep[kRegChunks];
-    if (in_regs) {
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
 #pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        const int i = lane + 32 * k;
-        if (i < nnew) {
-          const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-          keep[k] = *reinterpret_cast<const uint4*>(new_row(r) + c * 16);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        if (lane + 32 * k < nnew) {
-          float x[8];
-          unpack8<IN_BF16>(keep[k], x);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
-        }
-      }
-    } else {
-      for (int i = lane; i < nnew; i += 32) {
-        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-        float x[8];
-        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
-      }
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
     const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
     const float inv = __frcp_rn(scale);
@@ -191,24 +163,11 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
         *q = pack8_e4m3(x, inv);
       }
     }
-    if (in_regs) {
-#pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        const int i = lane + 32 * k;
-        if (i < nnew) {
-          const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-          float x[8];
-          unpack8<IN_BF16>(keep[k], x);
-          *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
-        }
-      }
-    } else {
-      for (int i = lane; i < nnew; i += 32) {
-        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-        float x[8];
-        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
-        *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
-      }
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
     }
     __syncwarp();  // every lane has read `old` before it is replaced
     if (lane == 0) *sp = scale;

@@ -864,6 +864,10 @@ KVWRITE = {
     "kv_write_fp8": dict(B=64, Hkv=8, D=128, bs=16, S=512, cmax=4096,
                          desc="paged KV write bf16 -> fp8-e4m3 cache, per-(block, head) scale recompute: B=64 "
                               "sequences x 512 new rows, Hkv=8, D=128, bs=16, start ~U[0,4096]"),
+    # profiling case for ncu --set full
+    "kv_write_fp8_small": dict(B=16, Hkv=8, D=128, bs=16, S=512, cmax=4096,
+                               desc="paged KV write bf16 -> fp8-e4m3 cache: B=16 sequences x 512 new rows, Hkv=8, "
+                                    "D=128, bs=16"),
 }
 
 

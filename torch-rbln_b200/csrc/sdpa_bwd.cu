@@ -282,49 +282,74 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0 && ntiles > 0) {
       const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S^T, dP^T halves: K-major over D
       const uint32_t id_acc = idesc_f16(BF16, BT, D, true);      // dV, dK: B (dO, Q) MN-major
-      bool ok = mbar_wait(bar(KB_KV), 0, abort);
+      // S^T and dP^T of half hh (query rows [64 hh, 64 hh + 64)) of tile i
+      auto issue_s = [&](int i, int hh) {
+        const int st = i & 1;
+        const uint32_t qb = sbase + Lay::Q0 + st * NP * kPanel + hh * 8192;
+        const uint32_t db = sbase + Lay::DO0 + st * NP * kPanel + hh * 8192;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::K + off, 16, 1024), sw128_desc(qb + off, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::V + off, 16, 1024), sw128_desc(db + off, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(KB_SFA + hh));
+      };
+      // dV += P^T dO and dK += dS^T Q over half hh's 64 query rows of tile i
+      auto issue_acc = [&](int i, int hh) {
+        const int st = i & 1;
+        const uint32_t qb = sbase + Lay::Q0 + st * NP * kPanel;
+        const uint32_t db = sbase + Lay::DO0 + st * NP * kPanel;
+#pragma unroll
+        for (int k4 = 0; k4 < BT / 32; ++k4) {
+          const int kk = hh * (BT / 32) + k4;
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_f16_ts(t_dv, t_s + kPackOff + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+          umma_f16_ts(t_dk, t_dp + kPackOff + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
+        }
+      };
+      // Software pipeline over tiles: half A of tile i + 1 is issued as soon as
+      // half A of tile i has been consumed, so the compute warps of half A
+      // work on tile i + 1 while those of half B finish tile i. Every write
+      // of a new S^T / dP^T half follows, in issue order, the MMAs that read
+      // the packed P^T / dS^T it overwrites (tcgen05.mma runs in issue order).
+      bool ok = mbar_wait(bar(KB_KV), 0, abort) && mbar_wait(bar(KB_QF0), 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(0, 1);
+      }
       for (int i = 0; ok && i < ntiles; ++i) {
         const int st = i & 1;
-        if (!mbar_wait(bar(KB_QF0 + st), (i >> 1) & 1, abort)) {
+        const bool more = i + 1 < ntiles;
+        if (!mbar_wait(bar(KB_PFA), i & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t qb = sbase + Lay::Q0 + st * NP * kPanel;
-        const uint32_t db = sbase + Lay::DO0 + st * NP * kPanel;
-        // (the previous tile's dV / dK MMAs read P^T and dS^T from these
-        // buffers; tcgen05.mma runs in issue order, so these writes follow)
-        for (int hh = 0; hh < 2; ++hh) {  // query rows [64 hh, 64 hh + 64) of the tile: 8 KB into each panel
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-            umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::K + off, 16, 1024),
-                        sw128_desc(qb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-            umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::V + off, 16, 1024),
-                        sw128_desc(db + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(bar(KB_SFA + hh));
-        }
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          if (!mbar_wait(bar(KB_PFA + hh), i & 1, abort)) {
+        issue_acc(i, 0);
+        if (more) {
+          if (!mbar_wait(bar(KB_QF0 + ((i + 1) & 1)), ((i + 1) >> 1) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int k4 = 0; k4 < BT / 32; ++k4) {  // the half's 64 query rows: 4 steps of 16
-            const int kk = hh * (BT / 32) + k4;
-            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-            umma_f16_ts(t_dv, t_s + kPackOff + kk * 8, sw128_desc(db + kk * 16 * 128, kPanel, 1024), id_acc, acc);
-            umma_f16_ts(t_dk, t_dp + kPackOff + kk * 8, sw128_desc(qb + kk * 16 * 128, kPanel, 1024), id_acc, acc);
-          }
+          issue_s(i + 1, 0);
         }
-        if (!ok) break;
+        if (!mbar_wait(bar(KB_PFB), i & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_acc(i, 1);
         umma_commit(bar(KB_QE0 + st));
+        if (more) issue_s(i + 1, 1);
       }
       umma_commit(bar(KB_DONE));
       if (!ok) {
@@ -559,46 +584,65 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0 && nk > 0) {
       const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S, dP halves (64 keys each)
       const uint32_t id_dq = idesc_f16(BF16, BT, D, true);       // B (K) MN-major
-      bool ok = mbar_wait(bar(QB_Q), 0, abort);
+      auto issue_s = [&](int j, int hh) {  // S, dP of keys [64 hh, 64 hh + 64) of tile j
+        const int st = j & 1;
+        const uint32_t kb = sbase + Lay::K0 + st * NP * kPanel + hh * 8192;
+        const uint32_t vb = sbase + Lay::V0 + st * NP * kPanel + hh * 8192;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::Q + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::DO + off, 16, 1024), sw128_desc(vb + off, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(QB_SFA + hh));
+      };
+      auto issue_dq = [&](int j, int hh) {  // dQ += dS K over half hh's 64 keys
+        const uint32_t kb = sbase + Lay::K0 + (j & 1) * NP * kPanel;
+#pragma unroll
+        for (int k4 = 0; k4 < BT / 32; ++k4) {
+          const int kk = hh * (BT / 32) + k4;
+          umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      // the same two-half software pipeline as the dK/dV kernel
+      bool ok = mbar_wait(bar(QB_Q), 0, abort) && mbar_wait(bar(QB_KF0), 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(0, 1);
+      }
       for (int j = 0; ok && j < nk; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(bar(QB_KF0 + st), (j >> 1) & 1, abort)) {
+        const bool more = j + 1 < nk;
+        if (!mbar_wait(bar(QB_PFA), j & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t kb = sbase + Lay::K0 + st * NP * kPanel;
-        const uint32_t vb = sbase + Lay::V0 + st * NP * kPanel;
-        for (int hh = 0; hh < 2; ++hh) {  // keys [64 hh, 64 hh + 64) of the tile
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-            umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::Q + off, 16, 1024),
-                        sw128_desc(kb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-            umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::DO + off, 16, 1024),
-                        sw128_desc(vb + hh * 8192 + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(bar(QB_SFA + hh));
-        }
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          if (!mbar_wait(bar(QB_PFA + hh), j & 1, abort)) {
+        issue_dq(j, 0);
+        if (more) {
+          if (!mbar_wait(bar(QB_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int k4 = 0; k4 < BT / 32; ++k4) {
-            const int kk = hh * (BT / 32) + k4;
-            umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
-                        (j > 0 || kk > 0) ? 1u : 0u);
-          }
+          issue_s(j + 1, 0);
         }
-        if (!ok) break;
+        if (!mbar_wait(bar(QB_PFB), j & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_dq(j, 1);
         umma_commit(bar(QB_KE0 + st));
+        if (more) issue_s(j + 1, 1);
       }
       umma_commit(bar(QB_DONE));
       if (!ok) {

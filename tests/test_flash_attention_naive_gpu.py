@@ -208,3 +208,10 @@ def test_sinks_shape_is_checked():
     x = make_case(1, 2, 4, 64, 64, 2, [10], 1)
     with pytest.raises(RuntimeError, match="one logit per query head"):
         run_op(x, True, torch.zeros(3))
+
+
+def test_prefill_batch_must_be_one():
+    """register_custom_ops.py:478-482: prefill q / k / v batch must be 1."""
+    x = make_case(2, 2, 4, 64, 64, 2, [0, 0], 16)
+    with pytest.raises(RuntimeError, match="batch size"):
+        run_op(x, False)

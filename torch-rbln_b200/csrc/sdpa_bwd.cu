@@ -88,23 +88,6 @@ __device__ __forceinline__ float bias_value(const void* base, int dt, int64_t i)
   }
 }
 
-// Score (log2 domain, before subtracting lse) of key t for query l, or -inf
-// when masked. `s` is the raw q.k product. Rows l >= L (tile padding) and
-// keys t >= S are masked before the mask is read.
-__device__ __forceinline__ float masked_score(const BwdArgs& a, float s, int t, int l, int64_t mrow) {
-  if (t >= a.S || l >= a.L || (a.causal && t > l)) return neg_inf();
-  float x = s * a.qk_mult;
-  if (a.mask) {
-    const float mv = bias_value(a.mask, a.mask_dtype, mrow + (int64_t)l * a.m_l + t);
-    if (a.mask_additive) {
-      x = fmaf(mv, kLog2e, x);
-    } else if (!(mv > 0.f)) {
-      x = neg_inf();
-    }
-  }
-  return x;
-}
-
 // ---------------------------------------------------------------------------
 // per-row pre-pass
 // ---------------------------------------------------------------------------

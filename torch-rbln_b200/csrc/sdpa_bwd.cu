@@ -30,9 +30,8 @@
 //                         over the first 64 columns of their own buffers, and
 //                           dV += P^T dO, dK += dS^T Q
 //                         read those as the A operand straight from TMEM.
-//   sdpa_bwd_q_kernel     one CTA per (128-query tile, query head, batch), two
-//                         CTAs per SM (256 TMEM columns each): Q and dO stay,
-//                         64-key K and V tiles stream; S = Q K^T, dP = dO V^T,
+//   sdpa_bwd_q_kernel     one CTA per (128-query tile, query head, batch): Q and
+//                         dO stay, K and V tiles stream; S = Q K^T, dP = dO V^T,
 //                         dS over S's buffer, dQ += dS K.
 // No atomics: every output element has one writer.
 //
@@ -477,36 +476,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------------------------
 // dQ
 // ---------------------------------------------------------------------------
-// 64-key tiles and 256 TMEM columns (S 64, dP 64, dQ up to 128), so two CTAs
-// share an SM: the handoff latencies of one CTA's serial chain
-// (S, dP -> dS -> dQ) are covered by the other CTA's work. Single-stage K/V
-// (16 KB each at D = 128) keeps two CTAs within the SM's shared memory.
-constexpr int BK = 64;                  // keys per tile
-constexpr int kPanel64 = 64 * 128;      // 64 rows x 64 16-bit elements
-constexpr int kQThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 compute
-
 template <int D>
 struct QLayout {
   static constexpr int NP = D / 64;
   static constexpr int Q = 0;
   static constexpr int DO = Q + NP * kPanel;
-  static constexpr int K = DO + NP * kPanel;
-  static constexpr int V = K + NP * kPanel64;
-  static constexpr int BAR = V + NP * kPanel64;
+  static constexpr int K0 = DO + NP * kPanel;  // stage s at K0 + s * NP * kPanel
+  static constexpr int V0 = K0 + 2 * NP * kPanel;
+  static constexpr int BAR = V0 + 2 * NP * kPanel;
   static constexpr int TMEM_SLOT = BAR + 16 * 8;
   static constexpr int ABORT = TMEM_SLOT + 8;
   static constexpr int TOTAL = ABORT + 8;
-  // at least 80 KB so that no more than two CTAs (256 TMEM columns each) are
-  // resident per SM
-  static constexpr int ALLOC = (TOTAL + 1024 > 80 * 1024) ? TOTAL + 1024 : 80 * 1024;
+  static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
 };
 
-enum QBar { QB_Q = 0, QB_KF, QB_KE, QB_SF, QB_PF, QB_DONE, QB_COUNT };
+enum QBar { QB_Q = 0, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SFA, QB_SFB, QB_PFA, QB_PFB, QB_DONE, QB_COUNT };
 
 template <int D, bool BF16, bool MASK>
-__global__ void __launch_bounds__(kQThreads, 2)
-    sdpa_bwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k64,
-                      const __grid_constant__ CUtensorMap tm_v64, const __grid_constant__ CUtensorMap tm_do,
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    sdpa_bwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                       const BwdArgs a) {
   using Lay = QLayout<D>;
   constexpr int NP = Lay::NP;
@@ -522,29 +511,30 @@ __global__ void __launch_bounds__(kQThreads, 2)
   const int qt = gridDim.x - 1 - blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
   const int h = hq / a.G;
   const int l0 = qt * BT;
-  const int nk_all = (a.S + BK - 1) / BK;
-  const int nk = a.causal ? min(nk_all, (l0 + BT - 1) / BK + 1) : nk_all;
+  const int nk_all = (a.S + BT - 1) / BT;
+  const int nk = a.causal ? min(nk_all, (l0 + BT - 1) / BT + 1) : nk_all;
 
   if (threadIdx.x == 0) {
     *abort = 0;
-    for (int i = 0; i < QB_COUNT; ++i) mbar_init(bar(i), i == QB_PF ? 4u : 1u);
+    for (int i = 0; i < QB_COUNT; ++i)
+      mbar_init(bar(i), (i == QB_PFA || i == QB_PFB) ? (uint32_t)(kComputeWarps / 2) : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_dp = tmem + 64, t_dq = tmem + 128;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0 && nk > 0) {
       prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k64);
-      prefetch_tmap(&tm_v64);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
       prefetch_tmap(&tm_do);
       mbar_arrive_expect_tx(bar(QB_Q), 2 * NP * kPanel);
       for (int p = 0; p < NP; ++p) {
@@ -553,11 +543,12 @@ __global__ void __launch_bounds__(kQThreads, 2)
       }
       int issued = 0;
       for (int j = 0; j < nk; ++j) {
-        if (j >= 1 && !mbar_wait(bar(QB_KE), (j - 1) & 1, abort)) break;
-        mbar_arrive_expect_tx(bar(QB_KF), 2 * NP * kPanel64);
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(bar(QB_KE0 + st), ((j >> 1) - 1) & 1, abort)) break;
+        mbar_arrive_expect_tx(bar(QB_KF0 + st), 2 * NP * kPanel);
         for (int p = 0; p < NP; ++p) {
-          tma_load_4d(sbase + Lay::K + p * kPanel64, &tm_k64, bar(QB_KF), p * 64, j * BK, h, b);
-          tma_load_4d(sbase + Lay::V + p * kPanel64, &tm_v64, bar(QB_KF), p * 64, j * BK, h, b);
+          tma_load_4d(sbase + Lay::K0 + (st * NP + p) * kPanel, &tm_k, bar(QB_KF0 + st), p * 64, j * BT, h, b);
+          tma_load_4d(sbase + Lay::V0 + (st * NP + p) * kPanel, &tm_v, bar(QB_KF0 + st), p * 64, j * BT, h, b);
         }
         issued = j + 1;
       }
@@ -565,51 +556,76 @@ __global__ void __launch_bounds__(kQThreads, 2)
         const long long c0 = clock64();
         while (!mbar_try_wait(bar(QB_Q), 0) && clock64() - c0 < 2000000) {
         }
-        if (issued > 0) {
+        for (int j = max(0, issued - 2); j < issued; ++j) {
           const long long c1 = clock64();
-          while (!mbar_try_wait(bar(QB_KF), (issued - 1) & 1) && clock64() - c1 < 2000000) {
+          while (!mbar_try_wait(bar(QB_KF0 + (j & 1)), (j >> 1) & 1) && clock64() - c1 < 2000000) {
           }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && nk > 0) {
-      const uint32_t id_s = idesc_f16(BF16, BT, BK, false);  // S, dP: both operands K-major over D
-      const uint32_t id_dq = idesc_f16(BF16, BT, D, true);   // B (K) MN-major
-      bool ok = mbar_wait(bar(QB_Q), 0, abort);
-      for (int j = 0; ok && j < nk; ++j) {
-        if (!mbar_wait(bar(QB_KF), j & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // (the previous tile's dQ MMAs read dS from S's columns; tcgen05.mma
-        // runs in issue order, so these writes follow)
+      const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S, dP halves (64 keys each)
+      const uint32_t id_dq = idesc_f16(BF16, BT, D, true);       // B (K) MN-major
+      auto issue_s = [&](int j, int hh) {  // S, dP of keys [64 hh, 64 hh + 64) of tile j
+        const int st = j & 1;
+        const uint32_t kb = sbase + Lay::K0 + st * NP * kPanel + hh * 8192;
+        const uint32_t vb = sbase + Lay::V0 + st * NP * kPanel + hh * 8192;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qoff = (kk >> 2) * kPanel + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * kPanel64 + (kk & 3) * 32;
-          umma_f16_ss(t_s, sw128_desc(sbase + Lay::Q + qoff, 16, 1024), sw128_desc(sbase + Lay::K + koff, 16, 1024),
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_s + 64 * hh, sw128_desc(sbase + Lay::Q + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
                       id_s, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qoff = (kk >> 2) * kPanel + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * kPanel64 + (kk & 3) * 32;
-          umma_f16_ss(t_dp, sw128_desc(sbase + Lay::DO + qoff, 16, 1024),
-                      sw128_desc(sbase + Lay::V + koff, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+          umma_f16_ss(t_dp + 64 * hh, sw128_desc(sbase + Lay::DO + off, 16, 1024), sw128_desc(vb + off, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar(QB_SF));
-        if (!mbar_wait(bar(QB_PF), j & 1, abort)) {
+        umma_commit(bar(QB_SFA + hh));
+      };
+      auto issue_dq = [&](int j, int hh) {  // dQ += dS K over half hh's 64 keys
+        const uint32_t kb = sbase + Lay::K0 + (j & 1) * NP * kPanel;
+#pragma unroll
+        for (int k4 = 0; k4 < BT / 32; ++k4) {
+          const int kk = hh * (BT / 32) + k4;
+          umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      // the same two-half software pipeline as the dK/dV kernel
+      bool ok = mbar_wait(bar(QB_Q), 0, abort) && mbar_wait(bar(QB_KF0), 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(0, 1);
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        const int st = j & 1;
+        const bool more = j + 1 < nk;
+        if (!mbar_wait(bar(QB_PFA), j & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma_f16_ts(t_dq, t_s + kk * 8, sw128_desc(sbase + Lay::K + kk * 16 * 128, kPanel64, 1024), id_dq,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar(QB_KE));
+        issue_dq(j, 0);
+        if (more) {
+          if (!mbar_wait(bar(QB_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(j + 1, 0);
+        }
+        if (!mbar_wait(bar(QB_PFB), j & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_dq(j, 1);
+        umma_commit(bar(QB_KE0 + st));
+        if (more) issue_s(j + 1, 1);
       }
       umma_commit(bar(QB_DONE));
       if (!ok) {
@@ -620,6 +636,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
     }
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // query row == TMEM lane
     const int l = l0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -627,14 +644,15 @@ __global__ void __launch_bounds__(kQThreads, 2)
     const int64_t mrow = MASK ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h + (int64_t)min(l, a.L - 1) * a.m_l : 0;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
-      const int kt0 = j * BK;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SF), j & 1, abort))) {
+      const int kt0 = j * BT;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SFA + half), j & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int c4 = 0; c4 < BK / 32; ++c4) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c4 = half == 0 ? 1 - cc : 2 + cc;
         uint32_t sv[32], dv[32];
         __syncwarp();
         tmem_ld32(t_s + lane_off + c4 * 32, sv);
@@ -673,13 +691,12 @@ __global__ void __launch_bounds__(kQThreads, 2)
             dk[e] = pack2<BF16>(dd[0], dd[1]);
           }
         }
-        // columns [16 c4, 16 c4 + 16) were read by this chunk or the one before
-        tmem_st16(t_s + lane_off + c4 * 16, dk);
+        tmem_st16(t_s + lane_off + kPackOff + c4 * 16, dk);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(QB_PF));
+      if (lane == 0) mbar_arrive(bar(QB_PFA + half));
     }
 
     ok = __all_sync(0xffffffffu, ok);
@@ -688,7 +705,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
     if (ok && a.dq) {
       char* qrow = a.dq + b * a.dq_b + hq * a.dq_h + (int64_t)l * a.dq_l;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t ov[32];
         if (nk > 0) {
           __syncwarp();
@@ -718,7 +735,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
   if (*abort && threadIdx.x == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -733,8 +750,7 @@ size_t rows_bytes(const rbln_sdpa_bwd_params_t* p) {
 }
 
 struct BwdMaps {
-  CUtensorMap q, k, v, dout;  // 128-row boxes
-  CUtensorMap k64, v64;       // 64-row boxes (dQ kernel)
+  CUtensorMap q, k, v, dout;
 };
 
 template <int D, bool BF16, bool MASK, bool DBIAS>
@@ -753,7 +769,7 @@ int launch_q(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   auto* k = sdpa_bwd_q_kernel<D, BF16, MASK>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
   dim3 grid((a.L + BT - 1) / BT, a.H, a.B);
-  k<<<grid, kQThreads, sm, st>>>(m.q, m.k64, m.v64, m.dout, a);
+  k<<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -782,8 +798,7 @@ int launch_bwd(const rbln_sdpa_bwd_params_t* p, const BwdMaps& m, const BwdArgs&
 }
 
 static_assert(KvLayout<128>::ALLOC <= 227 * 1024, "kv kernel shared memory");
-static_assert(2 * QLayout<128>::ALLOC <= 228 * 1024, "two dQ CTAs per SM");
-static_assert(3 * QLayout<64>::ALLOC > 228 * 1024, "at most two dQ CTAs per SM (TMEM)");
+static_assert(QLayout<128>::ALLOC <= 227 * 1024, "q kernel shared memory");
 
 }  // namespace
 }  // namespace rbln
@@ -824,9 +839,7 @@ int rbln_sdpa_bwd(const rbln_sdpa_bwd_params_t* p, cudaStream_t stream) {
   if (!map_kv(&m.q, p->q, p->dtype, B, H, L, D, p->q_stride[0], p->q_stride[1], p->q_stride[2], BT) ||
       !map_kv(&m.dout, p->dout, p->dtype, B, H, L, D, p->dout_stride[0], p->dout_stride[1], p->dout_stride[2], BT) ||
       !map_kv(&m.k, p->k, p->dtype, B, Hkv, S, D, p->k_stride[0], p->k_stride[1], p->k_stride[2], BT) ||
-      !map_kv(&m.v, p->v, p->dtype, B, Hkv, S, D, p->v_stride[0], p->v_stride[1], p->v_stride[2], BT) ||
-      !map_kv(&m.k64, p->k, p->dtype, B, Hkv, S, D, p->k_stride[0], p->k_stride[1], p->k_stride[2], BK) ||
-      !map_kv(&m.v64, p->v, p->dtype, B, Hkv, S, D, p->v_stride[0], p->v_stride[1], p->v_stride[2], BK))
+      !map_kv(&m.v, p->v, p->dtype, B, Hkv, S, D, p->v_stride[0], p->v_stride[1], p->v_stride[2], BT))
     return RBLN_ERR_LAUNCH;
   BwdArgs a{};
   a.B = B;

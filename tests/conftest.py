@@ -14,9 +14,15 @@ def pytest_sessionstart(session):
     checkout); nvcc cross-compiles for sm_100a without a GPU."""
     lib = os.path.join(ROOT, "torch-rbln_b200", "torch_rbln_b200", "_lib", "librbln_attn_torch.so")
     if not os.path.exists(lib):
-        from torch_rbln_b200 import _build
+        # loaded from its file: importing it through the package would run
+        # the package's check that the libraries already exist
+        import importlib.util
 
-        _build.build()
+        path = os.path.join(ROOT, "torch-rbln_b200", "torch_rbln_b200", "_build.py")
+        spec = importlib.util.spec_from_file_location("torch_rbln_b200_build", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.build()
 
 
 def pytest_configure(config):

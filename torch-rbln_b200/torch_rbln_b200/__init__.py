@@ -13,7 +13,7 @@ Importing this package:
 
 There is no CPU fallback: the ops have CUDA kernels only, and importing
 fails if the native libraries have not been built (run
-`python -m torch_rbln_b200._build` or `__graft_entry__.build()`).
+`python torch-rbln_b200/torch_rbln_b200/_build.py` or `__graft_entry__.build()`).
 """
 
 from __future__ import annotations
@@ -29,7 +29,7 @@ TORCH_LIBRARY = os.path.join(_LIB_DIR, "librbln_attn_torch.so")
 if not (os.path.exists(CABI_LIBRARY) and os.path.exists(TORCH_LIBRARY)):
     raise ImportError(
         "torch_rbln_b200: native libraries are missing from "
-        f"{_LIB_DIR}; build them with `python -m torch_rbln_b200._build`")
+        f"{_LIB_DIR}; build them with `python torch-rbln_b200/torch_rbln_b200/_build.py`")
 
 torch.ops.load_library(TORCH_LIBRARY)
 

@@ -140,7 +140,8 @@ def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
         if not os.path.exists(_LIB_PATH):
-            raise RuntimeError(f"{_LIB_PATH} is missing; build with `python -m torch_rbln_b200._build`")
+            raise RuntimeError(f"{_LIB_PATH} is missing; build with "
+                               "`python torch-rbln_b200/torch_rbln_b200/_build.py`")
         L = ctypes.CDLL(_LIB_PATH)
         for name, (res, args) in ENTRY_POINTS.items():
             fn = getattr(L, name)

@@ -26,13 +26,17 @@
 //                         2-stage TMA ring. Per tile, in TMEM:
 //                           S^T = K Q^T and dP^T = V dO^T (128 x 128 each),
 //                         the compute warps (thread = key row = TMEM lane)
-//                         turn them into P^T and dS^T as bf16/f16 written back
-//                         over the first 64 columns of their own buffers, and
+//                         turn them into P^T and dS^T as bf16/f16 pairs
+//                         written back over columns 32-95 of their own
+//                         buffers (see kPackOff), and
 //                           dV += P^T dO, dK += dS^T Q
 //                         read those as the A operand straight from TMEM.
+//                         Each tile is handled in two halves of 64 query rows
+//                         with their own barriers, pipelined across tiles.
 //   sdpa_bwd_q_kernel     one CTA per (128-query tile, query head, batch): Q and
 //                         dO stay, K and V tiles stream; S = Q K^T, dP = dO V^T,
-//                         dS over S's buffer, dQ += dS K.
+//                         dS over S's buffer, dQ += dS K (two halves of 64 keys,
+//                         pipelined the same way).
 // No atomics: every output element has one writer.
 //
 // Warp roles in both tile kernels (320 threads): warp 0 issues the TMA copies

@@ -120,6 +120,20 @@ def test_fake_kernels_give_q_metadata():
         assert out.shape == q.shape and out.dtype == q.dtype
 
 
+def test_fake_kernel_of_the_kv_write():
+    """rbln_attn::paged_kv_write traces under fake tensors (it returns nothing)."""
+    import torch
+    import torch_rbln_b200  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        k = torch.empty(2, 8, 1, 4, 64, dtype=torch.bfloat16)
+        kc = torch.empty(16, 8, 1, 16, 64, dtype=torch.float8_e4m3fn)
+        sc = torch.empty(16, 8)
+        assert torch.ops.rbln_attn.paged_kv_write(k, k, kc, kc, torch.empty(2, dtype=torch.int32),
+                                                  torch.empty(2, 4, dtype=torch.int32), 16, sc, sc) is None
+
+
 def test_cpu_tensors_are_rejected_no_fallback():
     """No CPU fallback: the ops have no CPU kernel."""
     import torch

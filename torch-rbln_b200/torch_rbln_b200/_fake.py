@@ -24,3 +24,11 @@ def _like_q(q, *args, **kwargs):
 for _name in _NAMES:
     if hasattr(torch.ops.rbln_custom_ops, _name):
         torch.library.register_fake(f"rbln_custom_ops::{_name}", _like_q)
+
+
+def _writes_only(*args, **kwargs):
+    """paged_kv_write mutates its caches (and scales) and returns nothing."""
+    return None
+
+
+torch.library.register_fake("rbln_attn::paged_kv_write", _writes_only)

@@ -300,3 +300,72 @@ def test_kv_write_matches_reference_prefill_writes(idx):
             kc[:, :, :, :s1], vc[:, :, :, :s1] = c["kpre"], c["vpre"]
         opa.kv_write(c["k"], c["v"], kc, vc, torch.tensor([[s0]], dtype=torch.int32), bt, ms)
         assert _sha(kc) == c["results"][key]["kc"] and _sha(vc) == c["results"][key]["vc"]
+
+
+def test_kv_write_fp8_oracle_properties():
+    """The fp8 write rule (oracle.kv_write; the reference has no fp8 cache, so
+    it is checked by its defining properties): every touched (block, head)
+    scale is max(amax of its valid rows, 1e-6) / 448; the new rows dequantize
+    to within e4m3 rounding (relative 2^-4, absolute 2^-9 * scale near 0);
+    rows past the write are untouched; repeating a write changes nothing."""
+    g = torch.Generator().manual_seed(11)
+    B, Hkv, D, bs, S = 2, 2, 64, 16, 21
+    nblk, mb = 12, 5
+    bt = torch.randperm(nblk, generator=g)[: B * mb].reshape(B, mb).to(torch.int32)
+    kc = opa.quantize_fp8(torch.randn(nblk, Hkv, 1, bs, D, generator=g), torch.ones(1))
+    vc, ks, vs = kc.clone(), torch.ones(nblk, Hkv), torch.ones(nblk, Hkv)
+    seq = torch.tensor([3, 16], dtype=torch.int32)  # mid-block start with held rows; block-aligned start
+    k = torch.randn(B, Hkv, 1, S, D, generator=g).to(torch.bfloat16) * 3
+    v = torch.randn(B, Hkv, 1, S, D, generator=g).to(torch.bfloat16)
+    before = kc.clone()
+    held_deq = {}
+    for b in range(B):
+        s0 = int(seq[b])
+        blk = int(bt[b, s0 // bs])
+        held_deq[b] = kc[blk, :, 0, : s0 % bs].float() * ks[blk].reshape(Hkv, 1, 1)
+    opa.kv_write(k, v, kc, vc, seq, bt, bs, ks, vs)
+    for b in range(B):
+        s0 = int(seq[b])
+        for i in range(S):
+            p = s0 + i
+            blk, row = int(bt[b, p // bs]), p % bs
+            deq = kc[blk, :, 0, row].float() * ks[blk].reshape(Hkv, 1)
+            x = k[b, :, 0, i].float()
+            tol = 2.0 ** -4 * x.abs() + 2.0 ** -9 * ks[blk].reshape(Hkv, 1)
+            assert bool(((deq - x).abs() <= tol).all())
+        for bi in range(s0 // bs, (s0 + S - 1) // bs + 1):
+            blk = int(bt[b, bi])
+            lo, hi = max(s0, bi * bs) - bi * bs, min(s0 + S, (bi + 1) * bs) - bi * bs
+            new = k[b, :, 0, bi * bs + lo - s0: bi * bs + hi - s0].float().abs().amax(dim=(1, 2))
+            if bi == s0 // bs and s0 % bs:
+                new = torch.maximum(new, held_deq[b].abs().amax(dim=(1, 2)))
+            assert torch.equal(ks[blk], torch.clamp(new, min=1e-6) / opa.FP8_MAX)
+            assert torch.equal(kc[blk, :, 0, hi:].view(torch.uint8), before[blk, :, 0, hi:].view(torch.uint8))
+    snap = (kc.clone(), vc.clone(), ks.clone(), vs.clone())
+    opa.kv_write(k, v, kc, vc, seq, bt, bs, ks, vs)
+    assert torch.equal(kc.view(torch.uint8), snap[0].view(torch.uint8))
+    assert torch.equal(vc.view(torch.uint8), snap[1].view(torch.uint8))
+    assert torch.equal(ks, snap[2]) and torch.equal(vs, snap[3])
+
+
+def test_sinks_decode_oracle_fully_masked_and_limits():
+    """Decode with sinks: a sequence with no visible position gives 0 (all
+    softmax mass on the sink) where it gives NaN without sinks; a sink of
+    -inf changes nothing; a very large sink drives every output to 0."""
+    c = NAIVE[2]  # a decode case
+    assert c["decode"]
+    scale = 1.0 / math.sqrt(c["D"])
+    seq_idx = torch.tensor([[c["s0"]]], dtype=torch.int32)
+    bt = torch.tensor([[0]], dtype=torch.int16)
+    H = c["Hkv"] * c["G"]
+
+    def run(mask, s):
+        kv = c["kv_cache"].clone()
+        return opa.flash_attention_naive(c["q"], c["k"], c["v"], kv, mask, scale, seq_idx, bt, s, decode=True)
+
+    none = torch.zeros_like(c["mask"])
+    assert torch.isnan(run(none, None)).all()
+    assert torch.count_nonzero(run(none, torch.zeros(H))) == 0
+    base = run(c["mask"], None)
+    assert torch.equal(run(c["mask"], torch.full([H], -float("inf"))), base)
+    assert run(c["mask"], torch.full([H], 1e4)).abs().max() < 1e-30

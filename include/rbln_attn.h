@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define RBLN_ATTN_ABI_VERSION 2
+#define RBLN_ATTN_ABI_VERSION 3
 
 typedef enum {
   RBLN_OK = 0,
@@ -281,7 +281,11 @@ int rbln_sdpa_bwd(const rbln_sdpa_bwd_params_t* p, cudaStream_t stream);
  * on every GPU that loads it until the process exits. Requests that need
  * more return RBLN_ERR_SCRATCH_LIMIT and launch nothing.
  * The first call on each device looks up the array's device address (with
- * that device current); make that first call before any stream capture.
+ * that device current); make that first call before any stream capture. A
+ * lookup that fails returns RBLN_ERR_LAUNCH and is tried again on the next
+ * call; a successful one is kept for the life of the process, so do not call
+ * this entry point after cudaDeviceReset (the kept address belongs to the
+ * context that the reset destroyed).
  * All calls share the one array: calls that overlap on the GPU (other
  * streams, other threads) race on it and must be serialised by the caller.
  * Nothing in it needs to start at zero: every partial the merge step reads
@@ -294,10 +298,13 @@ int rbln_paged_causal_attn_decode_noalloc(const rbln_paged_attn_params_t* p, cud
  * all-gather through ProcessGroupRBLN, torch_rbln/csrc/distributed/c10d/rbln/
  * ProcessGroupRBLN.cpp:754-830): one process per GPU owns a slice of the KV
  * heads, and the decode kernels store each final head output straight into
- * every rank's full output buffer (peer memory mapped with CUDA IPC), then a
- * one-warp kernel exchanges a per-call epoch through every rank's flag array
- * and waits (bounded, RBLN_DEVERR_TIMEOUT on expiry) until all ranks' writes
- * are in. This replaces the decode + all-gather + re-layout copy. */
+ * every rank's full output buffer (peer memory mapped with CUDA IPC), then
+ * the last CTA of the merge kernel (or, on the per-sequence split grid, a
+ * one-warp kernel) exchanges a per-call epoch through every rank's flag
+ * array and waits until all ranks' writes are in. The wait is bounded by
+ * wait_limit_us: on expiry it ORs RBLN_DEVERR_TIMEOUT into p->error_flags
+ * and returns, and the remote heads of that call's output are not valid.
+ * This replaces the decode + all-gather + re-layout copy. */
 #define RBLN_IPC_HANDLE_BYTES 64
 typedef struct rbln_peer_out {
   void* const* out;       /* device array [n]: every rank's full output buffer, mapped on this GPU */
@@ -306,7 +313,11 @@ typedef struct rbln_peer_out {
   int32_t rank;           /* this rank */
   int32_t head0;          /* first KV head of this rank in the full output */
   uint32_t epoch;         /* this call's epoch; strictly increasing over calls (flags start at 0) */
+  uint32_t wait_limit_us; /* longest wait for the peers' epochs, in microseconds of GPU time;
+                             0 = 2,000,000 (2 s). ABI version 3 added this field. */
 } rbln_peer_out_t;
+
+size_t rbln_peer_out_sizeof(void);
 
 /* Device memory that other processes can map: cudaMalloc of `bytes` (zeroed)
  * and its IPC handle (RBLN_IPC_HANDLE_BYTES bytes). Free with rbln_ipc_free. */

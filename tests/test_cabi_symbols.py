@@ -41,13 +41,15 @@ def test_abi_version_and_struct_size():
     from torch_rbln_b200 import cabi
 
     L = cabi.lib()
-    assert L.rbln_attn_abi_version() == 2
+    assert L.rbln_attn_abi_version() == 3
     assert L.rbln_paged_attn_params_sizeof() == ctypes.sizeof(cabi.PagedAttnParams)
+    assert L.rbln_peer_out_sizeof() == ctypes.sizeof(cabi.PeerOut)
 
 
 @pytest.mark.parametrize("cname,pyname", [("rbln_paged_attn_params_t", "PagedAttnParams"),
                                           ("rbln_sdpa_params_t", "SdpaParams"),
-                                          ("rbln_sdpa_bwd_params_t", "SdpaBwdParams")])
+                                          ("rbln_sdpa_bwd_params_t", "SdpaBwdParams"),
+                                          ("rbln_peer_out_t", "PeerOut")])
 def test_struct_field_offsets_match_c(cname, pyname):
     from torch_rbln_b200 import cabi
 

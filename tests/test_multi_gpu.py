@@ -122,6 +122,11 @@ def _worker_p2p(rank, world, port, q):
             except AssertionError as e:
                 err = f"call {it}: " + str(e)[:300]
                 break
+        if err is None:
+            try:
+                peer.check()  # no exchange timed out
+            except sharding.ShardedDecodeError as e:
+                err = str(e)
         dist.barrier()
         peer.close()
         dist.destroy_process_group()

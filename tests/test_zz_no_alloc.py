@@ -52,6 +52,14 @@ def _run(cabi, L, d, noalloc, num_splits=0):
     return keep["out"].cpu(), x["kcache"].cpu(), x["vcache"].cpu()
 
 
+def _check(cabi, L, d, num_splits):
+    ref = _run(cabi, L, d, noalloc=False, num_splits=num_splits)
+    got = _run(cabi, L, d, noalloc=True, num_splits=num_splits)
+    torch.testing.assert_close(got[0].float(), ref[0].float(), rtol=RTOL, atol=ATOL)
+    assert torch.equal(got[1].view(torch.uint8), ref[1].view(torch.uint8))
+    assert torch.equal(got[2].view(torch.uint8), ref[2].view(torch.uint8))
+
+
 def test_noalloc_decode_matches_allocating_entry_point(lib):
     cabi, L = lib
     workloads = [
@@ -59,11 +67,20 @@ def test_noalloc_decode_matches_allocating_entry_point(lib):
         make_decode(3, 8, 8, 128, 16, [900, 2500, 64], seed=22, fp8=True),                   # fp8, G = 8
     ]
     for d in workloads:  # two calls in a row share the fixed scratch
-        ref = _run(cabi, L, d, noalloc=False, num_splits=9)
-        got = _run(cabi, L, d, noalloc=True, num_splits=9)
-        torch.testing.assert_close(got[0].float(), ref[0].float(), rtol=RTOL, atol=ATOL)
-        assert torch.equal(got[1].view(torch.uint8), ref[1].view(torch.uint8))
-        assert torch.equal(got[2].view(torch.uint8), ref[2].view(torch.uint8))
+        _check(cabi, L, d, num_splits=9)
+
+
+def test_noalloc_balanced_schedule_over_stale_scratch(lib):
+    """The default schedule (num_splits = 0: equal token chunks over the
+    batch) keeps a length prefix and [Hkv, chunks + B, G, D] partials in the
+    scratch, laid out unlike the per-sequence grid. Run it right after a
+    per-sequence call, so that it starts over that call's leftovers, then
+    twice more in a row."""
+    cabi, L = lib
+    _check(cabi, L, make_decode(4, 2, 4, 128, 16, [3000, 17, 1500, 4000], seed=23), num_splits=9)
+    lens = [129, 4096, 1, 2000, 37, 3333, 640, 16]
+    _check(cabi, L, make_decode(8, 8, 4, 128, 16, lens, seed=24), num_splits=0)
+    _check(cabi, L, make_decode(8, 8, 4, 128, 16, lens[::-1], seed=25, fp8=True), num_splits=0)
 
 
 def test_noalloc_rejects_requests_over_the_scratch_limit(lib):
@@ -78,4 +95,4 @@ def test_noalloc_rejects_requests_over_the_scratch_limit(lib):
     # 64 * 8 * 63 splits * 16 * 129 * 4 bytes = 266 MB, far above 16 MiB: rejected, nothing launched
     rc = L.rbln_paged_causal_attn_decode_noalloc(ctypes.byref(p),
                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert rc == -6  # RBLN_ERR_SCRATCH_LIMIT
+    assert rc == cabi.ERR_SCRATCH_LIMIT

@@ -103,6 +103,12 @@ struct DecodeArgs {
   int n_peers;
   int head0;  // first head of this rank in the full output
   const float* sinks;  // optional [Hkv * G] sink logits (natural-log units), index h * G + g
+  // epoch exchange in the last CTA of the balanced merge kernel (nullptr: none)
+  uint32_t* const* peer_flags;
+  int peer_rank;
+  uint32_t epoch;
+  uint64_t wait_ns;
+  int* merge_ctr;  // balanced workspace: merge CTAs done (zeroed by the decode kernel)
 };
 
 // Sink logit of local query head (h, g) in the log2 domain of the scores,
@@ -601,7 +607,10 @@ __device__ __forceinline__ int balanced_prefix(const DecodeArgs& a, int* P) {
   const int W = max(a.min_w, ((T + a.nchunk - 1) / a.nchunk + 15) & ~15);
   if (blockIdx.x == 0 && blockIdx.y == 0) {
     for (int i = tid; i <= a.B; i += kThreads) a.prefix[i] = P[i];
-    if (tid == 0) a.prefix[a.B + 1] = W;
+    if (tid == 0) {
+      a.prefix[a.B + 1] = W;
+      a.prefix[a.B + 2] = 0;  // merge CTAs done: counted by the merge kernel
+    }
   }
   return W;
 }
@@ -701,9 +710,40 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const Deco
   merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, sw);
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Epoch exchange after a head-sharded decode, run by one warp whose stores
+// (and all stores it has observed) are done: lane t announces to rank t that
+// this rank's outputs are in (release at system scope), then waits until
+// rank t has announced this epoch to this rank (acquire). A wait gives up
+// after limit_ns of GPU time with RBLN_DEVERR_TIMEOUT.
+__device__ __forceinline__ void peer_epoch_exchange(uint32_t* const* flags, int n, int rank, uint32_t epoch,
+                                                    uint64_t limit_ns, uint32_t* err) {
+  const int t = threadIdx.x & 31;
+  if (t >= n) return;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags[t] + rank), "r"(epoch) : "memory");
+  const uint32_t* mine = flags[rank] + t;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if ((int32_t)(v - epoch) >= 0) break;  // a rank may already be one epoch ahead
+    if (global_ns() - t0 > limit_ns) {
+      flag_error(err, RBLN_DEVERR_TIMEOUT);
+      break;
+    }
+  }
+}
+
 // Merge of the balanced kernel's partials for one (KV head, sequence). Also
 // finishes the sequences that no chunk covers (no visible position: the new
 // token is still appended and the output is NaN, as softmax of all -inf).
+// On the head-sharded path the last merge CTA to finish runs the epoch
+// exchange, so the call needs no separate barrier launch.
 template <int D, int KV, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(const DecodeArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -719,37 +759,35 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
       store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n)));
     }
     if (a.out_peers) __threadfence_system();
-    return;
-  }
-  const int W = a.prefix[a.B + 1];
-  const int cf = a.prefix[b] / W, cl = (a.prefix[b + 1] - 1) / W;
-  if (cf == cl) return;  // one chunk held the whole sequence and wrote the output
-  extern __shared__ float sw[];
-  merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw);
-}
-
-// Epoch exchange after a head-sharded decode (one warp): thread t announces
-// to rank t that this rank's output stores are done (release at system
-// scope; they were made by earlier kernels of this stream), then waits until
-// rank t has announced this epoch to this rank (acquire). Waits give up after
-// about 2 s of SM clock with RBLN_DEVERR_TIMEOUT.
-constexpr long long kPeerWaitLimitCycles = 4000000000LL;
-__global__ void __launch_bounds__(32) peer_epoch_barrier_kernel(uint32_t* const* flags, int n, int rank,
-                                                                uint32_t epoch, uint32_t* err) {
-  const int t = threadIdx.x;
-  if (t >= n) return;
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags[t] + rank), "r"(epoch) : "memory");
-  const uint32_t* mine = flags[rank] + t;
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-    if ((int32_t)(v - epoch) >= 0) break;  // a rank may already be one epoch ahead
-    if (clock64() - t0 > kPeerWaitLimitCycles) {
-      flag_error(err, RBLN_DEVERR_TIMEOUT);
-      break;
+  } else {
+    const int W = a.prefix[a.B + 1];
+    const int cf = a.prefix[b] / W, cl = (a.prefix[b + 1] - 1) / W;
+    // cf == cl: one chunk held the whole sequence and wrote the output
+    if (cf != cl) {
+      extern __shared__ float sw[];
+      merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw);
     }
   }
+  if (a.peer_flags == nullptr) return;
+  // every thread's peer stores are fenced at system scope (here, in
+  // merge_partials, or in the decode kernel this grid waited for)
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // the CTA's stores, seen through the barrier, before its arrival
+    last = atomicAdd(a.merge_ctr, 1) == (int)(gridDim.x * gridDim.y) - 1;
+    __threadfence();         // the other CTAs' arrivals (and their stores) before the exchange
+  }
+  __syncthreads();
+  if (last && threadIdx.x < 32)
+    peer_epoch_exchange(a.peer_flags, a.n_peers, a.peer_rank, a.epoch, a.wait_ns, a.err);
+}
+
+// The epoch exchange as a kernel of its own (one warp), after the
+// per-sequence split grid's kernels.
+__global__ void __launch_bounds__(32) peer_epoch_barrier_kernel(uint32_t* const* flags, int n, int rank,
+                                                                uint32_t epoch, uint64_t limit_ns, uint32_t* err) {
+  peer_epoch_exchange(flags, n, rank, epoch, limit_ns, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -817,6 +855,10 @@ const DecodeEnv& decode_env() {
 
 constexpr int kBalancedMaxBatch = 2048;
 
+// Balanced workspace head: the padded-length prefix [B + 1], the chunk size
+// W and the merge kernel's arrival counter, rounded up to 256 bytes.
+size_t prefix_bytes(int batch) { return ((size_t)(batch + 3) * sizeof(int) + 255) / 256 * 256; }
+
 int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
   if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 ||
       p->max_blocks <= 0 || p->num_blocks <= 0)
@@ -849,7 +891,7 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
     pl->nchunk = std::max(1, (148 * per_sm * waves + p->num_kv_heads - 1) / p->num_kv_heads);
     pl->min_w = env.min_w >= 16 ? env.min_w / 16 * 16 : 256;
     const size_t slots = (size_t)p->num_kv_heads * (pl->nchunk + p->batch) * p->group;
-    pl->ws_bytes = ((size_t)(p->batch + 2) * sizeof(int) + 255) / 256 * 256 + slots * p->head_dim * sizeof(float) +
+    pl->ws_bytes = prefix_bytes(p->batch) + slots * p->head_dim * sizeof(float) +
                    slots * sizeof(float) + 256;
   } else if (pl->max_splits > 1) {
     const size_t slots = (size_t)p->batch * p->num_kv_heads * pl->max_splits * p->group;
@@ -1016,7 +1058,7 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
   if (pl.balanced) {
     uintptr_t w = (reinterpret_cast<uintptr_t>(p->workspace) + 255) & ~uintptr_t(255);
     a.prefix = reinterpret_cast<int*>(w);
-    w += ((size_t)(p->batch + 2) * sizeof(int) + 255) / 256 * 256;
+    w += prefix_bytes(p->batch);
     const size_t slots = (size_t)p->num_kv_heads * (pl.nchunk + p->batch) * p->group;
     a.part_o = reinterpret_cast<float*>(w);
     a.part_lse = a.part_o + slots * p->head_dim;
@@ -1028,18 +1070,29 @@ int run_decode(const rbln_paged_attn_params_t* p, cudaStream_t st, bool require_
   }
   a.err = p->error_flags;
   a.sinks = p->sinks;
+  uint64_t wait_ns = 0;
   if (peers) {
+    // the error word is where a timed-out exchange is reported: required
     if (peers->n < 1 || peers->n > 32 || peers->rank < 0 || peers->rank >= peers->n || peers->head0 < 0 ||
-        !peers->out || !peers->flags)
+        !peers->out || !peers->flags || !p->error_flags)
       return RBLN_ERR_INVALID_ARGUMENT;
     a.out_peers = reinterpret_cast<char* const*>(peers->out);
     a.n_peers = peers->n;
     a.head0 = peers->head0;
+    wait_ns = (uint64_t)(peers->wait_limit_us ? peers->wait_limit_us : 2000000u) * 1000u;
+    if (pl.balanced) {  // the merge kernel's last CTA runs the exchange
+      a.peer_flags = peers->flags;
+      a.peer_rank = peers->rank;
+      a.epoch = peers->epoch;
+      a.wait_ns = wait_ns;
+      a.merge_ctr = a.prefix + p->batch + 2;
+    }
   }
   const int lrc = p->head_dim == 128 ? launch_d<128>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events)
                                      : launch_d<64>(a, pl, p->kv_dtype, p->q_dtype, st, p->prof_events);
-  if (lrc != RBLN_OK || !peers) return lrc;
-  peer_epoch_barrier_kernel<<<1, 32, 0, st>>>(peers->flags, peers->n, peers->rank, peers->epoch, p->error_flags);
+  if (lrc != RBLN_OK || !peers || pl.balanced) return lrc;
+  peer_epoch_barrier_kernel<<<1, 32, 0, st>>>(peers->flags, peers->n, peers->rank, peers->epoch, wait_ns,
+                                              p->error_flags);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -1051,6 +1104,8 @@ extern "C" {
 int rbln_attn_abi_version(void) { return RBLN_ATTN_ABI_VERSION; }
 
 size_t rbln_paged_attn_params_sizeof(void) { return sizeof(rbln_paged_attn_params_t); }
+
+size_t rbln_peer_out_sizeof(void) { return sizeof(rbln_peer_out_t); }
 
 int rbln_paged_decode_workspace_size(const rbln_paged_attn_params_t* p, size_t* bytes) {
   if (!bytes) return RBLN_ERR_INVALID_ARGUMENT;
@@ -1103,22 +1158,31 @@ int rbln_ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess
 
 namespace {
 constexpr int kNoallocMaxDevices = 64;
-std::once_flag g_noalloc_once[kNoallocMaxDevices];
-void* g_noalloc_addr[kNoallocMaxDevices];
-cudaError_t g_noalloc_status[kNoallocMaxDevices];
+std::mutex g_noalloc_mu[kNoallocMaxDevices];
+std::atomic<void*> g_noalloc_addr[kNoallocMaxDevices];
 
-// Device address of the fixed scratch on the current device (looked up once
-// per device, with that device current).
+// Device address of the fixed scratch on the current device, looked up with
+// that device current. Only a successful lookup is kept: a failed one (for
+// example a first call made while a stream is being captured) is tried
+// again on the next call.
 int noalloc_scratch(void** addr) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) return RBLN_ERR_NO_DEVICE;
-  std::call_once(g_noalloc_once[dev], [dev] {
-    void* a = nullptr;
-    g_noalloc_status[dev] = cudaGetSymbolAddress(&a, rbln_noalloc_scratch);
-    g_noalloc_addr[dev] = a;
-  });
-  if (g_noalloc_status[dev] != cudaSuccess || g_noalloc_addr[dev] == nullptr) return RBLN_ERR_LAUNCH;
-  *addr = g_noalloc_addr[dev];
+  void* a = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (a == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu[dev]);
+    a = g_noalloc_addr[dev].load(std::memory_order_relaxed);
+    if (a == nullptr) {
+      void* found = nullptr;
+      if (cudaGetSymbolAddress(&found, rbln_noalloc_scratch) != cudaSuccess || found == nullptr) {
+        cudaGetLastError();  // the failed lookup leaves no sticky error behind
+        return RBLN_ERR_LAUNCH;
+      }
+      g_noalloc_addr[dev].store(found, std::memory_order_release);
+      a = found;
+    }
+  }
+  *addr = a;
   return RBLN_OK;
 }
 }  // namespace

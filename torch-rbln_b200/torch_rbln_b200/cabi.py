@@ -22,10 +22,13 @@ ERR_INVALID_ARGUMENT = -1
 ERR_UNSUPPORTED = -2
 ERR_WORKSPACE = -3
 ERR_LAUNCH = -4
+ERR_NO_DEVICE = -5
+ERR_SCRATCH_LIMIT = -6
 
 DT_F32, DT_F16, DT_BF16, DT_FP8_E4M3, DT_I16, DT_I32, DT_I64, DT_BOOL = range(8)
 DEVERR_BLOCK_ID_RANGE = 0x1
 DEVERR_SEQ_RANGE = 0x2
+DEVERR_TIMEOUT = 0x4
 
 _DT = {
     torch.float32: DT_F32,
@@ -104,7 +107,7 @@ class SdpaBwdParams(ctypes.Structure):
 class PeerOut(ctypes.Structure):
     """rbln_peer_out_t: every rank's output buffer and flag array, as mapped on this GPU."""
     _fields_ = [("out", c_vp), ("flags", c_vp), ("n", c_i32), ("rank", c_i32), ("head0", c_i32),
-                ("epoch", ctypes.c_uint32)]
+                ("epoch", ctypes.c_uint32), ("wait_limit_us", ctypes.c_uint32)]
 
 
 IPC_HANDLE_BYTES = 64
@@ -113,6 +116,7 @@ IPC_HANDLE_BYTES = 64
 ENTRY_POINTS = {
     "rbln_attn_abi_version": (ctypes.c_int, []),
     "rbln_paged_attn_params_sizeof": (ctypes.c_size_t, []),
+    "rbln_peer_out_sizeof": (ctypes.c_size_t, []),
     "rbln_paged_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams),
                                                         ctypes.POINTER(ctypes.c_size_t)]),
     "rbln_paged_causal_attn_decode": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
@@ -131,6 +135,7 @@ ENTRY_POINTS = {
     "rbln_ipc_close": (ctypes.c_int, [c_vp]),
     "rbln_paged_causal_attn_decode_peers": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams),
                                                            ctypes.POINTER(PeerOut), c_vp]),
+    "rbln_paged_causal_attn_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagedAttnParams), c_vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -149,6 +154,8 @@ def lib() -> ctypes.CDLL:
             fn.argtypes = args
         if L.rbln_paged_attn_params_sizeof() != ctypes.sizeof(PagedAttnParams):
             raise RuntimeError("rbln_paged_attn_params_t layout mismatch between ctypes and the library")
+        if L.rbln_peer_out_sizeof() != ctypes.sizeof(PeerOut):
+            raise RuntimeError("rbln_peer_out_t layout mismatch between ctypes and the library")
         _lib = L
     return _lib
 

@@ -1,36 +1,59 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 attention hot path (paged decode by default).
+"""Benchmark of the B200 attention hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|decode_fp8|decode_long|prefill|sdpa|sdpa_bf16]
+                    [--workload suite|decode|decode_fp8|decode_long|prefill|sdpa|sdpa_bf16|sdpa_bwd|...]
 
-Default workload (N = 1): paged-attention decode, bf16, batch 64, 32 query /
-8 KV heads, head_dim 128, block_size 16, context length per sequence
-uniform in [128, 4096], block table = seeded random permutation of a
-20,000-block KV pool, K/V ~ N(0,1)*0.5, one new token per sequence.
-Metric: algorithmic HBM bytes per step / time (GB/s).
+Default (`--workload suite`): one JSON line whose headline is the paged
+decode (bf16, batch 64, 32 query / 8 KV heads, head_dim 128, block_size 16,
+context length per sequence uniform in [128, 4096], block table = seeded
+random permutation of a 20,000-block KV pool, K/V ~ N(0,1)*0.5, one new
+token per sequence; metric: algorithmic HBM bytes per step / time, GB/s),
+and whose `workloads` object carries one record per other workload of the
+metric, each with its own value, roofline, e2e, clocks, parity and (rank 0,
+one GPU) CPU baseline:
 
-A step is one call of rbln_custom_ops.paged_causal_attn_decode over the
-batch (append + attention). `value` times K steps with inputs resident in
-HBM (the KV pool, 1.3 GB, is far larger than the 126 MB L2, so no flush is
-needed); `e2e` times the same op through the public torch op with the
-step's inputs (q, k, v, seq, block_table) copied from pinned host memory
-and the output copied back inside the timed region. `roofline` is the main
-kernel alone, timed with CUDA events recorded on its launch stream around
-that kernel (C-ABI measurement hook).
+  long_context_decode  batch 32, 64 query / 8 KV heads, context 32768, bf16;
+                       KV heads sharded over the ranks, the head outputs
+                       stored into every rank's buffer by the decode kernels
+                       (strong scaling; run at every N)
+  fp8_decode           fp8-e4m3 KV with per-(block, head) scales, batch 256,
+                       context ~U[512, 8192]; the batch split by sequence
+                       over the ranks, each with its own pool and block
+                       table (strong scaling, global batch 256 at every N)
+  chunked_prefill      batch 8 x 512 new tokens, cached context ~U[0, 8192],
+                       32 / 8 heads, head_dim 128, causal (TFLOP/s; N = 1)
+  sdpa_f32             causal GQA SDPA fp32, 1 x 32 / 8 heads x 512 x 64 (N = 1)
+  sdpa_backward        causal GQA SDPA backward bf16, 2 x 32 / 8 x 4096 x 128 (N = 1)
+  kv_write_fp8         the standalone fp8 KV-cache write (N = 1)
 
-Under torchrun (N > 1) every rank runs its own batch of the same workload
-(sequences are independent; no collective on the data path) and the JSON
-line reports the whole-job aggregate over max-over-ranks time.
+A decode step is one call of the op over the batch (append + attention).
+`value` times K steps with inputs resident in HBM (CUDA events around the
+whole loop, no events inside it); `roofline` times the main kernel alone in
+a separate loop, with CUDA events that the C-ABI records on the launch
+stream around that kernel; `e2e` times the public torch API with the step's
+inputs copied from pinned host memory and the result copied back inside the
+timed region. Decode pools are far larger than the 126 MB L2; the compute
+workloads flush L2 (a 256 MB write) before each timed iteration.
 
---impl reference times the reference's CPU algorithm for the same workload
-on this host's cores (the oracle's restatement of the reference CPU op,
-oracle/paged_attention.py, on a bounded sample of sequences).
+Under torchrun (N > 1) the headline runs N replicas of the decode batch
+(sequences are independent; no collective on the data path); every number
+is whole-job work over the max-over-ranks device time.
+
+`parity` in each record compares the output of the last timed call with the
+CPU oracle (oracle/paged_attention.py, oracle/sdpa.py) on a seeded subset of
+the sequences, on every rank; for the head-sharded decode every rank's full
+output buffer must also be bit-identical to every other rank's.
+
+--impl reference times the reference's CPU algorithm for the same workloads
+on this host's cores (the oracle's restatement of the reference CPU ops, on
+bounded samples), rank 0 only.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -47,91 +70,110 @@ import torch  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+RTOL, ATOL = 1e-3, 1.2e-2  # the reference's tolerance, test/rbln/test_custom_kernel.py:654-655
 
 
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
+# shard: how a workload is split over N > 1 ranks ("replicas": every rank its
+# own batch; "heads": KV heads sharded; "batch": sequences split)
 WORKLOADS = {
     "decode": dict(desc="paged decode bf16 B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=20000",
-                   B=64, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=20000, fp8=False),
+                   B=64, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=20000, fp8=False, shard="replicas"),
     "decode_fp8": dict(desc="paged decode fp8-e4m3 KV B=256 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
-                       B=256, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
-    # profiling case for ncu --set full: inputs still larger than L2, ~0.35 GB on the device
-    "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
-                         B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False),
-    # long context, KV heads sharded over the ranks; each rank's kernels store its heads'
-    # outputs into every rank's output buffer over NVLink (no separate all-gather)
-    # profiling case for the fp8 path (~0.6 GB of fp8 KV on the device)
-    "decode_fp8_small": dict(desc="paged decode fp8-e4m3 KV B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
-                             B=64, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True),
+                       B=256, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True, shard="batch"),
     "decode_long": dict(desc="paged decode bf16 B=32 Hq=64 Hkv=8 D=128 bs=16 L=32768 pool=65536",
                         B=32, Hkv=8, G=8, D=128, bs=16, lmin=32768, lmax=32768, pool=65536, fp8=False,
                         shard="heads"),
+    # profiling cases for ncu --set full: inputs still larger than L2, well under 1 GB on the device
+    "decode_small": dict(desc="paged decode bf16 B=16 Hq=32 Hkv=8 D=128 bs=16 L~U[128,4096] pool=5000",
+                         B=16, Hkv=8, G=4, D=128, bs=16, lmin=128, lmax=4096, pool=5000, fp8=False,
+                         shard="replicas"),
+    "decode_fp8_small": dict(desc="paged decode fp8-e4m3 KV B=64 Hq=32 Hkv=8 D=128 bs=16 L~U[512,8192]",
+                             B=64, Hkv=8, G=4, D=128, bs=16, lmin=512, lmax=8192, pool=None, fp8=True,
+                             shard="replicas"),
 }
 
+COMPUTE = {
+    "prefill": dict(kind="prefill", B=8, Hkv=8, G=4, D=128, bs=16, S=512, cmin=0, cmax=8192,
+                    desc="paged chunked prefill bf16 B=8 Hq=32 Hkv=8 D=128 S_q=512 new tokens, "
+                         "cached ctx~U[0,8192], bs=16, causal"),
+    "prefill_small": dict(kind="prefill", B=2, Hkv=8, G=4, D=128, bs=16, S=512, cmin=2048, cmax=6144,
+                          desc="paged chunked prefill bf16 B=2 Hq=32 Hkv=8 D=128 S_q=512 ctx~U[2048,6144]"),
+    "sdpa": dict(kind="sdpa", B=1, Hq=32, Hkv=8, L=512, D=64, dtype=torch.float32,
+                 desc="SDPA causal GQA fp32 B=1 Hq=32 Hkv=8 L=S=512 D=64 (Llama-3.2-1B attention shape)"),
+    "sdpa_bf16": dict(kind="sdpa", B=4, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
+                      desc="SDPA causal GQA bf16 B=4 Hq=32 Hkv=8 L=S=4096 D=128"),
+    "sdpa_bwd": dict(kind="sdpa_bwd", B=2, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
+                     desc="SDPA backward causal GQA bf16 B=2 Hq=32 Hkv=8 L=S=4096 D=128 (dq, dk, dv)"),
+    "sdpa_bwd_small": dict(kind="sdpa_bwd", B=1, Hq=32, Hkv=8, L=2048, D=128, dtype=torch.bfloat16,
+                           desc="SDPA backward causal GQA bf16 B=1 Hq=32 Hkv=8 L=S=2048 D=128 (dq, dk, dv)"),
+}
 
-def build_decode(wl: dict, device, seed: int = 0, pool_seed: int = None):
-    """Seeded synthetic decode inputs. Lengths / block table on the CPU
-    generator; the KV pool is drawn on the device (seed + 1, or pool_seed)."""
-    g = torch.Generator().manual_seed(seed)
-    B, Hkv, G, D, bs = wl["B"], wl["Hkv"], wl["G"], wl["D"], wl["bs"]
-    lens = torch.randint(wl["lmin"], wl["lmax"] + 1, (B,), generator=g)
-    max_blocks = int(math.ceil(int(lens.max()) / bs))
-    nblk = wl["pool"] or int(sum(math.ceil(int(x) / bs) for x in lens)) + B
-    nblk = max(nblk, B * max_blocks)
-    perm = torch.randperm(nblk, generator=g)
-    # each sequence takes its blocks from the permutation in turn
-    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
-    cursor = 0
-    for b in range(B):
-        n = int(math.ceil(int(lens[b]) / bs))
-        bt[b, :n] = perm[cursor:cursor + n].to(torch.int32)
-        cursor += n
-    q = torch.randn([B, Hkv, G, 1, D], generator=g).to(torch.bfloat16)
-    k = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
-    v = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
-    seq = (lens - 1).to(torch.int32).reshape(B, 1)
-    gd = torch.Generator(device=device).manual_seed(seed + 1 if pool_seed is None else pool_seed)
-    shape = [nblk, Hkv, 1, bs, D]
-    if wl["fp8"]:
-        kc, ks = _fp8_pool(shape, gd, device)
-        vc, vs = _fp8_pool(shape, gd, device)
-    else:
-        kc = (torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5)
-        vc = (torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5)
-        ks = vs = None
-    return dict(q=q, k=k, v=v, seq=seq, bt=bt, kcache=kc, vcache=vc, k_scale=ks, v_scale=vs, lens=lens,
-                scale=1.0 / math.sqrt(D), bs=bs, B=B, Hkv=Hkv, G=G, D=D, fp8=wl["fp8"])
+KVWRITE = {
+    "kv_write_fp8": dict(B=64, Hkv=8, D=128, bs=16, S=512, cmax=4096,
+                         desc="paged KV write bf16 -> fp8-e4m3 cache, per-(block, head) scale recompute: B=64 "
+                              "sequences x 512 new rows, Hkv=8, D=128, bs=16, start ~U[0,4096]"),
+    "kv_write_fp8_small": dict(B=16, Hkv=8, D=128, bs=16, S=512, cmax=4096,
+                               desc="paged KV write bf16 -> fp8-e4m3 cache: B=16 sequences x 512 new rows, Hkv=8, "
+                                    "D=128, bs=16"),
+}
 
-
-def _fp8_pool(shape, gd, device):
-    x = torch.randn(shape, generator=gd, device=device, dtype=torch.float32)
-    amax = x.abs().amax(dim=(2, 3, 4)).clamp_min(1e-6)
-    sc = (amax / 448.0).contiguous()
-    q = (x / sc[:, :, None, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
-    del x
-    return q, sc
-
-
-def decode_bytes(d: dict) -> int:
-    """Algorithmic HBM bytes of one decode step: every attended K/V element
-    read once, q read, output written, new k/v read and written to the
-    cache, block-table entries and (fp8) scales read."""
-    lens = d["lens"].to(torch.int64)
-    Hkv, G, D, bs = d["Hkv"], d["G"], d["D"], d["bs"]
-    el = 1 if d["fp8"] else 2
-    kv = int(lens.sum()) * Hkv * D * el * 2
-    blocks = int(((lens + bs - 1) // bs).sum())
-    scales = blocks * Hkv * 4 * 2 if d["fp8"] else 0
-    qo = d["B"] * Hkv * G * D * 2 * 2
-    new = d["B"] * Hkv * D * (2 * 2 + el * 2)
-    return kv + scales + qo + new + blocks * 4
+# the default line: headline workload, then the records of `workloads`
+# (name in the line -> workload, and whether it runs at N > 1)
+SUITE_HEADLINE = "decode"
+SUITE = [("long_context_decode", "decode_long", True), ("fp8_decode", "decode_fp8", True),
+         ("chunked_prefill", "prefill", False), ("sdpa_f32", "sdpa", False),
+         ("sdpa_backward", "sdpa_bwd", False), ("kv_write_fp8", "kv_write_fp8", False)]
 
 
 # ---------------------------------------------------------------------------
-# helpers
+# run context (one process per GPU)
 # ---------------------------------------------------------------------------
+class Ctx:
+    def __init__(self, with_gpu: bool = True):
+        self.ws = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
+        self.stream = None
+        self.pg = False
+        if with_gpu:
+            torch.cuda.set_device(self.local)
+            self.dev = torch.device("cuda", self.local)
+            self.stream = torch.cuda.current_stream(self.dev)
+            if self.ws > 1:
+                import torch.distributed as dist
+                from datetime import timedelta
+
+                dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.dev)
+                self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def reduce(self, values, op="max"):
+        """Element-wise max / min / sum of a list of floats over the ranks."""
+        if not self.pg:
+            return list(values)
+        import torch.distributed as dist
+
+        t = torch.tensor([float(x) for x in values], dtype=torch.float64, device=self.dev)
+        dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
+        return t.tolist()
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -194,198 +236,6 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dist_env():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
-
-
-# ---------------------------------------------------------------------------
-# our arm
-# ---------------------------------------------------------------------------
-def run_ours(args, wl_name):
-    import torch.distributed as dist
-
-    ws, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    import torch_rbln_b200  # noqa: F401
-    from torch_rbln_b200 import cabi
-
-    wl = WORKLOADS[wl_name]
-    head_shard = wl.get("shard") == "heads" and ws > 1
-    if head_shard:
-        # every rank sees the same sequences and block table; it holds only its
-        # slice of the KV heads (and their query heads)
-        from torch_rbln_b200 import sharding
-
-        sharding.kv_head_range(wl["Hkv"], rank, ws)
-        wl = dict(wl, Hkv=wl["Hkv"] // ws)
-        d = build_decode(wl, dev, seed=0, pool_seed=1 + rank)
-    else:
-        d = build_decode(wl, dev, seed=1000 * rank)
-    q, k, v = d["q"].to(dev), d["k"].to(dev), d["v"].to(dev)
-    seq, bt = d["seq"].to(dev), d["bt"].to(dev)
-    kc, vc = d["kcache"], d["vcache"]
-    ks, vs = d["k_scale"], d["v_scale"]
-    scale_t = torch.tensor(d["scale"])
-    nbytes = decode_bytes(d)
-    ops = torch.ops.rbln_custom_ops
-
-    peer = None
-    if head_shard:
-        # every rank's full output buffers, written by all ranks' kernels over NVLink
-        peer = sharding.PeerHeadOutput((q.shape[0], q.shape[1] * ws) + tuple(q.shape[2:]), q.dtype, rank, ws)
-        head0 = rank * q.shape[1]
-        e2e_ws = {}
-
-    def op_call(qq, kk, vv, ss, bb):
-        if d["fp8"]:
-            return ops.paged_causal_attn_decode_kvfp8(qq, kk, vv, kc, vc, ks, vs, ss, scale_t, bb, d["bs"])
-        if head_shard:
-            return sharding.head_sharded_paged_decode_p2p(qq, kk, vv, kc, vc, ss, d["scale"], bb, d["bs"], peer,
-                                                          workspace=e2e_ws, q_is_local=True)
-        return ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
-
-    # C-ABI parameter block with the timing hook around the main kernel
-    p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs,
-                                out=peer.outputs[0] if head_shard else None)
-    cabi.attach_workspace(p, dev, keep)
-    L = cabi.lib()
-    stream = torch.cuda.current_stream(dev)
-    entry = L.rbln_paged_causal_attn_decode
-    import ctypes
-
-    pref = ctypes.byref(p)
-    sh = ctypes.c_void_p(stream.cuda_stream)
-    ws_bytes = p.workspace_bytes
-
-    def cabi_step(ev0=None, ev1=None):
-        p.prof_events[0] = ev0.cuda_event if ev0 is not None else None
-        p.prof_events[1] = ev1.cuda_event if ev1 is not None else None
-        if head_shard:
-            # decode of the local heads, outputs stored into every rank's buffer, epoch exchange
-            out, po = peer.next(head0)
-            p.out = out.data_ptr()
-            rc = L.rbln_paged_causal_attn_decode_peers(pref, ctypes.byref(po), sh)
-        else:
-            rc = entry(pref, sh)
-        if rc != 0:
-            raise RuntimeError(f"rbln_paged_causal_attn_decode failed: {rc}")
-
-    for _ in range(args.warmup):
-        cabi_step()
-        op_call(q, k, v, seq, bt)
-    torch.cuda.synchronize()
-
-    # ---- value: device-resident inputs, K steps, events around the whole op
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for e0, e1 in kev:  # create the events on the device before timing
-        e0.record(stream)
-        e1.record(stream)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t0.record(stream)
-        for i in range(args.steps):
-            cabi_step(*kev[i])
-        t1.record(stream)
-        torch.cuda.synchronize()
-        if ws > 1:
-            dist.barrier()
-    ms_total = t0.elapsed_time(t1)
-    kern_ms = [a.elapsed_time(b) for a, b in kev]
-    ms_step = ms_total / args.steps
-
-    # ---- e2e: public torch op, host buffers, H2D + D2H inside the timed region
-    pin = lambda t: t.cpu().pin_memory()
-    hq, hk, hv, hs, hb = pin(d["q"]), pin(d["k"]), pin(d["v"]), pin(d["seq"]), pin(d["bt"])
-    out_heads = q.shape[1] * (ws if head_shard else 1)
-    hout = torch.empty((q.shape[0], out_heads) + tuple(q.shape[2:]), dtype=q.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs, hb))
-    d2h = hout.numel() * hout.element_size()
-    for _ in range(max(2, args.warmup)):
-        o = op_call(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
-                    hs.to(dev, non_blocking=True), hb.to(dev, non_blocking=True))
-        hout.copy_(o, non_blocking=True)
-    torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        o = op_call(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
-                    hs.to(dev, non_blocking=True), hb.to(dev, non_blocking=True))
-        hout.copy_(o, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-
-    # max over ranks
-    if ws > 1:
-        tt = torch.tensor([ms_step, e2e_ms, statistics.mean(kern_ms)], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_step, e2e_ms, kmean = tt.tolist()
-    else:
-        kmean = statistics.mean(kern_ms)
-
-    hbm_peak, tf_peak, peak_src = load_peaks()
-    achieved = nbytes / (kmean * 1e-3) / 1e9
-    value = ws * nbytes / (ms_step * 1e-3) / 1e9
-    launches_per_step = 1 + (1 if ws_bytes > 0 else 0)
-    line = {
-        "metric": "paged decode HBM GB/s",
-        "value": round(value, 1),
-        "unit": "GB/s",
-        "n_gpus": ws,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True,
-        "scaling": "strong" if head_shard else "weak",
-        "vs_baseline": None,
-        "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
-        "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
-        "config": {"workload": WORKLOADS[wl_name]["desc"], "global_batch": d["B"] if head_shard else d["B"] * ws,
-                   "parallelism": (f"kv-head-sharded x{ws}, head outputs stored into every rank's buffer by the decode kernels (NVLink P2P) + epoch barrier" if head_shard
-                                   else f"batch-sharded x{ws}"),
-                   "l2": "inputs larger than L2 (KV pool " + f"{kc.numel() * kc.element_size() * 2 / 1e9:.2f} GB)",
-                   "bytes_per_step_per_gpu": nbytes},
-        "e2e": {"value": round(ws * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "torch.ops.rbln_custom_ops.paged_causal_attn_decode" + ("_kvfp8" if d["fp8"] else "")},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
-                     "kernel": "paged_decode_balanced_kernel (equal token chunks over the batch, mma.sync)", "kernel_ms": round(kmean, 4),
-                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
-                     else "fallback 6.65 TB/s"},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
-    }
-    traffic = _traffic_from_profiles(wl_name)
-    if traffic is not None:
-        line["roofline"]["traffic"] = traffic
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl_name, d, budget_s=args.cpu_budget)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if ws > 1:
-        dist.barrier()  # every rank is past its last call before any buffer is unmapped
-    if peer is not None:
-        peer.close()
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
 def _traffic_from_profiles(wl_name):
     """DRAM bytes per launch of the main kernel, from the committed ncu summary
     (a `traffic_bytes_per_launch[<workload>]: N` line), if one exists."""
@@ -402,12 +252,365 @@ def _traffic_from_profiles(wl_name):
     return None
 
 
+def _event_pairs(n, stream):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for a, b in ev:  # create the events on the device before timing
+        a.record(stream)
+        b.record(stream)
+    return ev
+
+
+def _tolerance_stats(got: torch.Tensor, ref: torch.Tensor, rtol: float, atol: float):
+    got, ref = got.float(), ref.float()
+    both_nan = torch.isnan(got) & torch.isnan(ref)
+    d = (got - ref).abs().masked_fill(both_nan, 0.0)
+    ok = bool(((d <= atol + rtol * ref.abs().masked_fill(both_nan, 0.0)) | both_nan).all())
+    scale = float(ref.abs().masked_fill(both_nan, 0.0).max()) or 1.0
+    return ok, float(d.max()) if d.numel() else 0.0, float(d.max()) / scale if d.numel() else 0.0
+
+
 # ---------------------------------------------------------------------------
-# CPU baseline / reference arm
+# decode inputs
 # ---------------------------------------------------------------------------
-def cpu_sample(d: dict, n_seq: int, device_pool: bool = True):
+def decode_layout(wl: dict, seed: int, Hkv: int = None):
+    """Seeded lengths, block table (over a pool of `nblk` blocks) and
+    q / k / v on the CPU. Each sequence takes its blocks from a seeded random
+    permutation of the pool, in turn."""
+    g = torch.Generator().manual_seed(seed)
+    B, G, D, bs = wl["B"], wl["G"], wl["D"], wl["bs"]
+    Hkv = Hkv or wl["Hkv"]
+    lens = torch.randint(wl["lmin"], wl["lmax"] + 1, (B,), generator=g)
+    max_blocks = int(math.ceil(int(lens.max()) / bs))
+    nblk = wl["pool"] or int(sum(math.ceil(int(x) / bs) for x in lens)) + B
+    nblk = max(nblk, B * max_blocks)
+    perm = torch.randperm(nblk, generator=g)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    cursor = 0
+    for b in range(B):
+        n = int(math.ceil(int(lens[b]) / bs))
+        bt[b, :n] = perm[cursor:cursor + n].to(torch.int32)
+        cursor += n
+    q = torch.randn([B, Hkv, G, 1, D], generator=g).to(torch.bfloat16)
+    k = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn([B, Hkv, 1, 1, D], generator=g) * 0.5).to(torch.bfloat16)
+    seq = (lens - 1).to(torch.int32).reshape(B, 1)
+    return dict(q=q, k=k, v=v, seq=seq, bt=bt, lens=lens, nblk=nblk)
+
+
+def decode_pool(nblk, Hkv, bs, D, fp8, device, seed):
+    """The KV pool, drawn on `device` (N(0,1) * 0.5 for bf16; N(0,1)
+    quantised per (block, head) with scale = amax / 448 for fp8)."""
+    gd = torch.Generator(device=device).manual_seed(seed)
+    shape = [nblk, Hkv, 1, bs, D]
+    if fp8:
+        kc, ks = _fp8_pool(shape, gd, device)
+        vc, vs = _fp8_pool(shape, gd, device)
+        return kc, vc, ks, vs
+    kc = torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5
+    vc = torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16) * 0.5
+    return kc, vc, None, None
+
+
+def _fp8_pool(shape, gd, device):
+    x = torch.randn(shape, generator=gd, device=device, dtype=torch.float32)
+    amax = x.abs().amax(dim=(2, 3, 4)).clamp_min(1e-6)
+    sc = (amax / 448.0).contiguous()
+    q = (x / sc[:, :, None, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    del x
+    return q, sc
+
+
+def build_decode(wl: dict, device, seed: int = 0, pool_seed: int = None):
+    """Replicated / single-GPU decode inputs: layout from `seed`, pool from
+    seed + 1 (or pool_seed)."""
+    lay = decode_layout(wl, seed)
+    kc, vc, ks, vs = decode_pool(lay["nblk"], wl["Hkv"], wl["bs"], wl["D"], wl["fp8"], device,
+                                 seed + 1 if pool_seed is None else pool_seed)
+    return _decode_dict(wl, lay, kc, vc, ks, vs)
+
+
+def _decode_dict(wl, lay, kc, vc, ks, vs):
+    return dict(q=lay["q"], k=lay["k"], v=lay["v"], seq=lay["seq"], bt=lay["bt"], kcache=kc, vcache=vc,
+                k_scale=ks, v_scale=vs, lens=lay["lens"], scale=1.0 / math.sqrt(wl["D"]), bs=wl["bs"],
+                B=lay["q"].shape[0], Hkv=lay["q"].shape[1], G=wl["G"], D=wl["D"], fp8=wl["fp8"])
+
+
+def build_decode_sharded(wl: dict, mode: str, rank: int, ws: int, device):
+    """This rank's decode inputs under `mode` (see WORKLOADS)."""
+    if mode == "replicas":
+        return build_decode(wl, device, seed=1000 * rank)
+    if mode == "heads":
+        # same sequences and block table on every rank; rank r holds KV heads
+        # [r * Hkv / N, (r + 1) * Hkv / N) of the pool (and their query heads)
+        from torch_rbln_b200 import sharding
+
+        sharding.kv_head_range(wl["Hkv"], rank, ws)
+        return build_decode(dict(wl, Hkv=wl["Hkv"] // ws), device, seed=0, pool_seed=1 + rank)
+    if mode == "batch":
+        # rank r holds its share of the sequences (equal counts, near-equal
+        # tokens), its own pool of just their blocks and its own block table
+        from torch_rbln_b200 import sharding
+
+        lay = decode_layout(wl, seed=0)
+        idx = sharding.batch_partition(lay["lens"], ws)[rank]
+        blocks, table = sharding.shard_batch(lay["seq"], lay["bt"], wl["bs"], idx)
+        sub = dict(q=lay["q"][idx].contiguous(), k=lay["k"][idx].contiguous(), v=lay["v"][idx].contiguous(),
+                   seq=lay["seq"][idx].contiguous(), bt=table, lens=lay["lens"][idx], nblk=int(blocks.numel()))
+        kc, vc, ks, vs = decode_pool(sub["nblk"], wl["Hkv"], wl["bs"], wl["D"], wl["fp8"], device, 1 + rank)
+        d = _decode_dict(wl, sub, kc, vc, ks, vs)
+        d["global_index"] = idx
+        return d
+    raise ValueError(mode)
+
+
+def decode_bytes(d: dict) -> int:
+    """Algorithmic HBM bytes of one decode step: every attended K/V element
+    read once, q read, output written, new k/v read and written to the
+    cache, block-table entries and (fp8) scales read."""
+    lens = d["lens"].to(torch.int64)
+    Hkv, G, D, bs = d["Hkv"], d["G"], d["D"], d["bs"]
+    el = 1 if d["fp8"] else 2
+    kv = int(lens.sum()) * Hkv * D * el * 2
+    blocks = int(((lens + bs - 1) // bs).sum())
+    scales = blocks * Hkv * 4 * 2 if d["fp8"] else 0
+    qo = d["B"] * Hkv * G * D * 2 * 2
+    new = d["B"] * Hkv * D * (2 * 2 + el * 2)
+    return kv + scales + qo + new + blocks * 4
+
+
+def decode_config(wl_name, ws, mode, global_batch, pool_bytes, step_bytes):
+    """The `config` object of a decode line (rank 0's sizes); the reference
+    arm prints the same."""
+    wl = WORKLOADS[wl_name]
+    par = {"single": "single GPU",
+           "replicas": f"replicas x{ws}: every rank its own batch of {wl['B']} sequences, no collective",
+           "heads": (f"kv-head-sharded x{ws}: head outputs stored into every rank's buffer by the decode "
+                     f"kernels (NVLink peer stores) + epoch exchange in the merge kernel"),
+           "batch": f"batch-sharded x{ws}: each rank its share of the {wl['B']} sequences, own pool and table"}[mode]
+    return {"workload": wl["desc"], "global_batch": global_batch, "parallelism": par,
+            "l2": f"inputs larger than L2 (KV pool {pool_bytes / 1e9:.2f} GB per GPU)",
+            "bytes_per_step_per_gpu": step_bytes}
+
+
+def _global_batch(wl, mode, ws, local_B):
+    return {"replicas": local_B * ws, "heads": local_B, "batch": wl["B"], "single": local_B}[mode]
+
+
+# ---------------------------------------------------------------------------
+# decode measurement (our arm)
+# ---------------------------------------------------------------------------
+def decode_record(args, ctx: Ctx, wl_name: str, n_parity: int = 8, cpu_leg: bool = True) -> dict:
+    import torch_rbln_b200  # noqa: F401
+    from torch_rbln_b200 import cabi, sharding
+
+    wl = WORKLOADS[wl_name]
+    ws, rank, dev, stream = ctx.ws, ctx.rank, ctx.dev, ctx.stream
+    if ws == 1:
+        mode = "single"
+        d = build_decode_sharded(wl, "batch", 0, 1, dev) if wl["shard"] == "batch" else build_decode(wl, dev, seed=0)
+    else:
+        mode = wl["shard"]
+        d = build_decode_sharded(wl, mode, rank, ws, dev)
+    q, k, v = d["q"].to(dev), d["k"].to(dev), d["v"].to(dev)
+    seq, bt = d["seq"].to(dev), d["bt"].to(dev)
+    kc, vc, ks, vs = d["kcache"], d["vcache"], d["k_scale"], d["v_scale"]
+    scale_t = torch.tensor(d["scale"])
+    nbytes = decode_bytes(d)
+    total_bytes = int(ctx.reduce([nbytes], "sum")[0])
+    global_batch = _global_batch(wl, mode, ws, d["B"])
+    pool_bytes = kc.numel() * kc.element_size() * 2
+    ops = torch.ops.rbln_custom_ops
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    peer, head0, e2e_ws = None, 0, {}
+    if mode == "heads":
+        peer = sharding.PeerHeadOutput((q.shape[0], q.shape[1] * ws) + tuple(q.shape[2:]), q.dtype, rank, ws)
+        head0 = rank * q.shape[1]
+
+    def op_call(qq, kk, vv, ss, bb):
+        if d["fp8"]:
+            return ops.paged_causal_attn_decode_kvfp8(qq, kk, vv, kc, vc, ks, vs, ss, scale_t, bb, d["bs"])
+        if peer is not None:
+            return sharding.head_sharded_paged_decode_p2p(qq, kk, vv, kc, vc, ss, d["scale"], bb, d["bs"], peer,
+                                                          workspace=e2e_ws, q_is_local=True)
+        return ops.paged_causal_attn_decode(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"])
+
+    # C-ABI parameter block (with the kernel timing hook for the roofline loop)
+    p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], k_scale=ks, v_scale=vs,
+                                out=peer.outputs[0] if peer is not None else None)
+    cabi.attach_workspace(p, dev, keep)
+    p.error_flags = (peer.error_word if peer is not None else err).data_ptr()
+    L = cabi.lib()
+    pref, sh = ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)
+    last_out = [keep["out"]]
+
+    def cabi_step(ev0=None, ev1=None):
+        p.prof_events[0] = ev0.cuda_event if ev0 is not None else None
+        p.prof_events[1] = ev1.cuda_event if ev1 is not None else None
+        if peer is not None:
+            out, po = peer.next(head0)
+            p.out = out.data_ptr()
+            last_out[0] = out
+            rc = L.rbln_paged_causal_attn_decode_peers(pref, ctypes.byref(po), sh)
+        else:
+            rc = L.rbln_paged_causal_attn_decode(pref, sh)
+        if rc != 0:
+            raise RuntimeError(f"rbln_paged_causal_attn_decode failed: {rc}")
+
+    for _ in range(args.warmup):
+        cabi_step()
+        op_call(q, k, v, seq, bt)
+    torch.cuda.synchronize()
+
+    # ---- value: K steps back to back, events around the loop only
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(ctx.local) as clk:
+        t0.record(stream)
+        for _ in range(args.steps):
+            cabi_step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ctx.barrier()
+    ms_step = t0.elapsed_time(t1) / args.steps
+
+    # ---- roofline: the main kernel alone, events the C-ABI records around it
+    kev = _event_pairs(args.steps, stream)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        cabi_step(*kev[i])
+    torch.cuda.synchronize()
+    ctx.barrier()
+    kmean = statistics.mean(a.elapsed_time(b) for a, b in kev)
+
+    # ---- e2e: public torch op, host buffers, H2D + D2H inside the timed region
+    pin = lambda t: t.cpu().pin_memory()
+    hq, hk, hv, hs, hb = pin(d["q"]), pin(d["k"]), pin(d["v"]), pin(d["seq"]), pin(d["bt"])
+    out_heads = q.shape[1] * (ws if peer is not None else 1)
+    hout = torch.empty((q.shape[0], out_heads) + tuple(q.shape[2:]), dtype=q.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs, hb))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        o = op_call(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
+                    hs.to(dev, non_blocking=True), hb.to(dev, non_blocking=True))
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    # ---- one more C-ABI call, whose output the parity check reads
+    cabi_step()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    if peer is not None:
+        peer.check()  # raises ShardedDecodeError if any exchange timed out
+    dev_err = int((peer.error_word if peer is not None else err).item())
+    parity = decode_parity(ctx, d, last_out[0], head0, n_parity, peer is not None)
+    parity["device_error_bits"] = int(ctx.reduce([dev_err], "max")[0])
+    parity["ok"] = parity["ok"] and parity["device_error_bits"] == 0
+
+    ms_step, e2e_ms, kmean = ctx.reduce([ms_step, e2e_ms, kmean], "max")
+    hbm_peak, _, peak_src = load_peaks()
+    achieved = nbytes / (kmean * 1e-3) / 1e9
+    rec = {
+        "metric": "paged decode HBM GB/s",
+        "value": round(total_bytes / (ms_step * 1e-3) / 1e9, 1),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if mode in ("heads", "batch") else "weak",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
+        "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
+        "config": decode_config(wl_name, ws, mode, global_batch, pool_bytes, nbytes),
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": ("torch_rbln_b200.sharding.head_sharded_paged_decode_p2p" if peer is not None else
+                        "torch.ops.rbln_custom_ops.paged_causal_attn_decode" + ("_kvfp8" if d["fp8"] else ""))},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": _traffic_from_profiles(wl_name),
+                     "kernel": "paged_decode_balanced_kernel (equal token chunks over the batch, mma.sync)",
+                     "kernel_ms": round(kmean, 4),
+                     "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs), of measured" if peak_src == "measured"
+                                     else "fallback 6.65 TB/s")},
+        # decode + merge per step (the exchange runs inside the merge kernel)
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+        "parity": parity,
+    }
+    if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_decode_baseline(d, budget_s=args.cpu_budget)
+    ctx.barrier()  # every rank is past its last call before any buffer is unmapped
+    if peer is not None:
+        peer.close()
+    ctx.barrier()
+    del d, kc, vc, ks, vs, keep
+    torch.cuda.empty_cache()
+    return rec
+
+
+def decode_parity(ctx: Ctx, d, out, head0, n, heads_sharded):
+    """The last call's output against the fp32 oracle on a seeded subset of
+    this rank's sequences (each rank its own; results combined over ranks).
+    With the heads sharded, every rank's full output must also equal every
+    other rank's, bit for bit."""
+    from oracle import paged_attention as opa
+    from torch_rbln_b200 import sharding
+
+    B = d["B"]
+    n = min(n, B)
+    idx = torch.randperm(B, generator=torch.Generator().manual_seed(7 + ctx.rank))[:n].sort().values
+    blocks, table = sharding.shard_batch(d["seq"], d["bt"], d["bs"], idx)
+    dv = d["kcache"].device
+    kc = d["kcache"][blocks.to(dv)].cpu()
+    vc = d["vcache"][blocks.to(dv)].cpu()
+    ks = d["k_scale"][blocks.to(dv)].cpu() if d["fp8"] else None
+    vs = d["v_scale"][blocks.to(dv)].cpu() if d["fp8"] else None
+    ref = opa.paged_decode(d["q"][idx], d["k"][idx], d["v"][idx], kc, vc, d["seq"][idx], d["scale"], table, d["bs"],
+                           k_scale=ks, v_scale=vs, mode="fp32")
+    got = out[idx.to(out.device), head0:head0 + d["Hkv"]].cpu()
+    ok, max_abs, max_rel = _tolerance_stats(got, ref, RTOL, ATOL)
+    agree = True
+    if heads_sharded and ctx.pg:
+        import torch.distributed as dist
+
+        buf = torch.empty((ctx.ws,) + tuple(out.shape), dtype=out.dtype, device=out.device)
+        dist.all_gather_into_tensor(buf, out.contiguous())
+        agree = all(torch.equal(buf[r], out) for r in range(ctx.ws))
+    okf, agreef = ctx.reduce([float(ok), float(agree)], "min")
+    max_abs, max_rel = ctx.reduce([max_abs, max_rel], "max")
+    n_total = int(ctx.reduce([n], "sum")[0])
+    res = {"ok": bool(okf) and bool(agreef), "max_abs": round(max_abs, 6), "max_rel": round(max_rel, 6),
+           "n_checked": n_total, "checked": f"{n_total} sequences (seeded subset, every rank), all their heads",
+           "tolerance": f"rtol {RTOL}, atol {ATOL} (the reference's, test_custom_kernel.py:654-655)",
+           "oracle": "oracle.paged_attention.paged_decode, fp32"}
+    if heads_sharded:
+        res["ranks_agree"] = bool(agreef)
+    return res
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm (decode)
+# ---------------------------------------------------------------------------
+def cpu_sample(d: dict, n_seq: int):
     """First n_seq sequences, gathered into the reference's contiguous
-    per-sequence layout [n, Hkv, 1, max_seq, D] (gather not timed)."""
+    per-sequence layout [n, Hkv, 1, max_seq, D] (gather not timed; fp8
+    dequantised to bf16 first)."""
     from oracle import paged_attention as opa
 
     n = n_seq
@@ -437,92 +640,110 @@ def cpu_sample(d: dict, n_seq: int, device_pool: bool = True):
             torch.tensor(d["scale"]), opa, decode_bytes(sub))
 
 
-def cpu_baseline(wl_name, d, budget_s=20.0, steps=None):
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    # size the sample: time one sequence, then take as many as fit the budget
+def _cpu_decode_sample_size(d, budget_s, mem_cap=1.5e9):
+    """Sequences that fit the time budget (from one timed sequence) and a cap
+    on the gathered caches' memory."""
     q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, 1)
     t = time.perf_counter()
     opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
     one = max(time.perf_counter() - t, 1e-4)
-    n = int(max(1, min(d["B"], budget_s / 4 / one)))
+    per_seq_mem = 2 * kc.numel() * kc.element_size() * 2  # caches and their per-step copies
+    return int(max(1, min(d["B"], budget_s / one, mem_cap / per_seq_mem)))
+
+
+def cpu_decode_times(d, n, reps, warmup=1):
+    """Wall-clock times of the reference's CPU decode on the first n
+    sequences (the caches are re-copied outside the timed region)."""
     q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, n)
+    for _ in range(warmup):
+        opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
     times = []
-    reps = steps if steps is not None else 3
-    opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)  # warm-up
     for _ in range(reps):
         kk, vv = kc.clone(), vc.clone()
         t = time.perf_counter()
         opa.mock_decode_contiguous(q, k, v, kk, vv, seq, sc)
         times.append(time.perf_counter() - t)
+    return times, nb
+
+
+def _cpu_stats_note(times):
+    return (f"median of {len(times)} runs ({statistics.median(times) * 1e3:.1f} ms; min {min(times) * 1e3:.1f}, "
+            f"max {max(times) * 1e3:.1f}: a shared host, so the spread is reported)")
+
+
+def cpu_decode_baseline(d, budget_s=20.0, reps=5):
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    n = _cpu_decode_sample_size(d, budget_s / (reps + 1))
+    times, nb = cpu_decode_times(d, n, reps)
     med = statistics.median(times)
     return {"value": round(nb / med / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"{n} of {d['B']} sequences of the same workload, reference CPU algorithm "
                       f"(oracle.paged_attention.mock_decode_contiguous, bf16 over the gathered per-sequence "
-                      f"layout), median of {reps} runs, {med * 1e3:.1f} ms per sample",
+                      f"layout), {_cpu_stats_note(times)}",
             "ms_per_sample": round(med * 1e3, 2), "bytes_per_sample": nb}
 
 
-def run_reference(args, wl_name):
-    ws, rank, local = dist_env()
-    if rank != 0:
-        return
+def reference_decode_inputs(wl: dict, mode: str, ws: int, kv_cap_bytes: float = 1.5e9):
+    """Rank 0's share of a decode workload on the CPU, as the reference arm
+    needs it: the full layout's sizes (for the config) and the inputs of
+    its first sequences only, as many as fit kv_cap_bytes of KV (the CPU
+    sample never reads more), with a pool of just their blocks."""
+    from torch_rbln_b200 import sharding
+
+    Hkv = wl["Hkv"] // ws if mode == "heads" else wl["Hkv"]
+    lay = decode_layout(wl, seed=0, Hkv=Hkv)
+    seq, bt, lens = lay["seq"], lay["bt"], lay["lens"]
+    if wl["shard"] == "batch":
+        idx = sharding.batch_partition(lens, ws)[0]
+        blocks, bt = sharding.shard_batch(seq, bt, wl["bs"], idx)
+        lay = dict(lay, q=lay["q"][idx], k=lay["k"][idx], v=lay["v"][idx], seq=seq[idx], bt=bt, lens=lens[idx],
+                   nblk=int(blocks.numel()))
+    el = 1 if wl["fp8"] else 2
+    full = dict(lens=lay["lens"], Hkv=Hkv, G=wl["G"], D=wl["D"], bs=wl["bs"], fp8=wl["fp8"], B=lay["q"].shape[0])
+    pool_bytes = lay["nblk"] * Hkv * wl["bs"] * wl["D"] * el * 2
+    per_token = Hkv * wl["D"] * el * 2
+    n = int(max(1, min(full["B"], (torch.cumsum(lay["lens"], 0) * per_token <= kv_cap_bytes).sum())))
+    first = torch.arange(n)
+    blocks, table = sharding.shard_batch(lay["seq"], lay["bt"], wl["bs"], first)
+    sub = dict(q=lay["q"][:n].contiguous(), k=lay["k"][:n].contiguous(), v=lay["v"][:n].contiguous(),
+               seq=lay["seq"][:n].contiguous(), bt=table, lens=lay["lens"][:n], nblk=int(blocks.numel()))
+    kc, vc, ks, vs = decode_pool(sub["nblk"], Hkv, wl["bs"], wl["D"], wl["fp8"], torch.device("cpu"), 1)
+    return _decode_dict(wl, sub, kc, vc, ks, vs), full, pool_bytes
+
+
+def reference_decode_line(args, ctx: Ctx, wl_name: str, per_step_budget=None) -> dict:
+    """--impl reference for a decode workload: the reference's CPU algorithm
+    on rank 0's data, each step a bounded sample of sequences."""
     wl = WORKLOADS[wl_name]
-    dev = torch.device("cpu")
-    d = build_decode(wl, dev, seed=0)
+    ws = ctx.ws
+    mode = wl["shard"] if ws > 1 else "single"
+    d, full, pool_bytes = reference_decode_inputs(wl, mode, ws)
+    global_batch = _global_batch(wl, mode, ws, full["B"])
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, 1)
-    t = time.perf_counter()
-    opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
-    one = max(time.perf_counter() - t, 1e-4)
-    per_step_budget = max(0.5, 120.0 / max(1, args.steps + args.warmup))
-    n = int(max(1, min(d["B"], per_step_budget / one)))
-    q, k, v, kc, vc, seq, sc, opa, nb = cpu_sample(d, n)
-    for _ in range(args.warmup):
-        opa.mock_decode_contiguous(q, k, v, kc.clone(), vc.clone(), seq, sc)
-    times = []
-    for _ in range(args.steps):
-        kk, vv = kc.clone(), vc.clone()
-        t = time.perf_counter()
-        opa.mock_decode_contiguous(q, k, v, kk, vv, seq, sc)
-        times.append(time.perf_counter() - t)
-    ms = statistics.mean(times) * 1e3
-    val = nb / (ms * 1e-3) / 1e9
-    sample = (f"{n} of {d['B']} sequences per step, reference CPU algorithm (oracle restatement of "
-              f"test_custom_kernel.py paged_causal_attn_decode on the per-sequence layout), wall clock")
-    line = {"impl": "reference", "metric": "paged decode HBM GB/s", "value": round(val, 3), "unit": "GB/s",
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "global_batch": d["B"]},
+    budget = per_step_budget or max(0.5, 120.0 / max(1, args.steps + args.warmup))
+    n = _cpu_decode_sample_size(d, budget)
+    times, nb = cpu_decode_times(d, n, args.steps, warmup=args.warmup)
+    med = statistics.median(times)
+    val = nb / med / 1e9
+    sample = (f"{n} of {full['B']} sequences per step, reference CPU algorithm (oracle restatement of "
+              f"test_custom_kernel.py paged_causal_attn_decode on the per-sequence layout), wall clock, "
+              f"{_cpu_stats_note(times)}")
+    return {"impl": "reference", "metric": "paged decode HBM GB/s", "value": round(val, 3), "unit": "GB/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong" if mode in ("heads", "batch") else "weak",
+            "vs_baseline": None, "dtype": "fp8e4m3-kv/bf16" if d["fp8"] else "bf16",
+            "data": "synthetic (seeded N(0,1)*0.5 KV pool, seeded lengths and block-table permutation)",
+            "config": decode_config(wl_name, ws, mode, global_batch, pool_bytes, decode_bytes(full)),
             "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
 # compute-bound workloads: chunked prefill and SDPA
 # ---------------------------------------------------------------------------
-COMPUTE = {
-    "prefill": dict(kind="prefill", B=8, Hkv=8, G=4, D=128, bs=16, S=512, cmin=0, cmax=8192,
-                    desc="paged chunked prefill bf16 B=8 Hq=32 Hkv=8 D=128 S_q=512 new tokens, "
-                         "cached ctx~U[0,8192], bs=16, causal"),
-    # profiling case for ncu --set full (same per-CTA work, fewer sequences)
-    "prefill_small": dict(kind="prefill", B=2, Hkv=8, G=4, D=128, bs=16, S=512, cmin=2048, cmax=6144,
-                          desc="paged chunked prefill bf16 B=2 Hq=32 Hkv=8 D=128 S_q=512 ctx~U[2048,6144]"),
-    "sdpa": dict(kind="sdpa", B=1, Hq=32, Hkv=8, L=512, D=64, dtype=torch.float32,
-                 desc="SDPA causal GQA fp32 B=1 Hq=32 Hkv=8 L=S=512 D=64 (Llama-3.2-1B attention shape)"),
-    "sdpa_bf16": dict(kind="sdpa", B=4, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
-                      desc="SDPA causal GQA bf16 B=4 Hq=32 Hkv=8 L=S=4096 D=128"),
-    "sdpa_bwd": dict(kind="sdpa_bwd", B=2, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
-                     desc="SDPA backward causal GQA bf16 B=2 Hq=32 Hkv=8 L=S=4096 D=128 (dq, dk, dv)"),
-    # profiling case for ncu --set full
-    "sdpa_bwd_small": dict(kind="sdpa_bwd", B=1, Hq=32, Hkv=8, L=2048, D=128, dtype=torch.bfloat16,
-                           desc="SDPA backward causal GQA bf16 B=1 Hq=32 Hkv=8 L=S=2048 D=128 (dq, dk, dv)"),
-}
-
-
 def build_prefill(wl, device, seed=0):
     g = torch.Generator().manual_seed(seed)
     B, Hkv, G, D, bs, S = wl["B"], wl["Hkv"], wl["G"], wl["D"], wl["bs"], wl["S"]
@@ -570,7 +791,7 @@ def _timed_kernel_loop(args, stream, step, kernel_step, flush):
     (`step`) and, in separate iterations, around the main kernel alone
     (`kernel_step`), each preceded by an L2 flush outside the timed window."""
     def timed(fn):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        ev = _event_pairs(args.steps, stream)
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(stream)
@@ -582,26 +803,16 @@ def _timed_kernel_loop(args, stream, step, kernel_step, flush):
     return timed(step), timed(kernel_step)
 
 
-def run_compute_ours(args, wl_name):
-    import ctypes
-
-    import torch.distributed as dist
-
-    ws, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
     import torch_rbln_b200  # noqa: F401
     from torch_rbln_b200 import cabi
 
+    ws, rank, dev, stream = ctx.ws, ctx.rank, ctx.dev, ctx.stream
     wl = COMPUTE[wl_name]
-    stream = torch.cuda.current_stream(dev)
     sh = ctypes.c_void_p(stream.cuda_stream)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
     L = cabi.lib()
+    result = {}
     if wl["kind"] == "prefill":
         d = build_prefill(wl, dev, seed=1000 * rank)
         q, k, v, seq, bt = (d[x].to(dev) for x in ("q", "k", "v", "seq", "bt"))
@@ -634,7 +845,7 @@ def run_compute_ours(args, wl_name):
         launches = 3  # schedule pre-pass, append, attention
         kernel = "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)"
         dtype = "bf16"
-        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
+        result["parity"] = lambda: prefill_parity(d, keep["out"])
     elif wl["kind"] == "sdpa_bwd":
         d = build_sdpa(wl, seed=0)
         q, k, v, dout = (d[x].to(dev) for x in ("q", "k", "v", "dout"))
@@ -655,7 +866,6 @@ def run_compute_ours(args, wl_name):
                 raise RuntimeError(f"rbln_sdpa_bwd failed: {rc}")
 
         kernel_step = step
-
         e0t = torch.empty(0, device=dev)
 
         def op_call(qq, kk, vv, oo, gg, ll):
@@ -670,7 +880,6 @@ def run_compute_ours(args, wl_name):
         kernel = ("sdpa_bwd_kv_kernel<128, bf16> + sdpa_bwd_q_kernel<128, bf16> + row pre-pass "
                   "(tcgen05/TMEM/TMA; whole backward timed)")
         dtype = "bf16"
-        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
     else:
         d = build_sdpa(wl, seed=0)
         q, k, v = (d[x].to(dev) for x in ("q", "k", "v"))
@@ -699,17 +908,16 @@ def run_compute_ours(args, wl_name):
                   if wl["dtype"] == torch.float32
                   else "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)")
         dtype = "f32" if wl["dtype"] == torch.float32 else "bf16"
-        l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
+        result["parity"] = lambda: sdpa_parity(d, out)
+    l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    with ClockSampler(local) as clk:
+    ctx.barrier()
+    with ClockSampler(ctx.local) as clk:
         op_ms, k_ms = _timed_kernel_loop(args, stream, step, kernel_step, flush)
-    if ws > 1:
-        dist.barrier()
+    ctx.barrier()
 
     # e2e through the public torch API with host buffers
     pinned = [t.cpu().pin_memory() for t in host_inputs]
@@ -735,21 +943,24 @@ def run_compute_ours(args, wl_name):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    if ws > 1:
-        tt = torch.tensor([op_ms, e2e_ms, k_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        op_ms, e2e_ms, k_ms = tt.tolist()
+    parity = None
+    if "parity" in result:
+        step()  # the output the check reads
+        torch.cuda.synchronize()
+        parity = result["parity"]()
+    op_ms, e2e_ms, k_ms = ctx.reduce([op_ms, e2e_ms, k_ms], "max")
 
-    hbm_peak, tf_peak, peak_src = load_peaks()
+    _, tf_peak, peak_src = load_peaks()
     flops = d["flops"]
     achieved = flops / (k_ms * 1e-3) / 1e12
-    line = {
+    rec = {
         "metric": metric, "value": round(ws * flops / (op_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(op_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded N(0,1) inputs" + (", seeded cached lengths and block-table permutation)"
                                                      if wl["kind"] == "prefill" else ")"),
-        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}", "l2": l2, "flops_per_step": flops},
+        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                   "l2": l2, "flops_per_step": flops},
         "e2e": {"value": round(ws * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": {"prefill": "torch.ops.rbln_custom_ops.paged_causal_attn_prefill",
@@ -758,18 +969,52 @@ def run_compute_ours(args, wl_name):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_peak, "unit": "TFLOP/s",
                      "frac": round(achieved / tf_peak, 4), "traffic": _traffic_from_profiles(wl_name),
                      "kernel": kernel, "kernel_ms": round(k_ms, 4),
-                     "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peak_src == "measured"
-                                     else "fallback 1.59 PFLOP/s")},
+                     "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst), of measured"
+                                     if peak_src == "measured" else "fallback 1.59 PFLOP/s")},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_compute(wl, d, args.cpu_budget)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if parity is not None:
+        rec["parity"] = parity
+    if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_baseline_compute(wl, d, args.cpu_budget)
+    del d
+    torch.cuda.empty_cache()
+    return rec
+
+
+def prefill_parity(d, out):
+    """The chunked prefill of the sequence with the median cached context
+    against the fp32 oracle (its blocks gathered, caches hold the appended
+    rows, which the oracle writes again)."""
+    from oracle import paged_attention as opa
+
+    b = int(torch.argsort(d["ctx"])[len(d["ctx"]) // 2])
+    nb = int(math.ceil((int(d["ctx"][b]) + d["S"]) / d["bs"]))
+    blocks = d["bt"][b, :nb].long()
+    dv = d["kcache"].device
+    kc, vc = d["kcache"][blocks.to(dv)].cpu(), d["vcache"][blocks.to(dv)].cpu()
+    table = torch.arange(nb, dtype=torch.int32).reshape(1, nb)
+    ref = opa.paged_prefill(d["q"][b:b + 1], d["k"][b:b + 1], d["v"][b:b + 1], kc, vc, d["seq"][b:b + 1],
+                            d["scale"], table, d["bs"], causal=True, mode="fp32")
+    ok, max_abs, max_rel = _tolerance_stats(out[b:b + 1].cpu(), ref, RTOL, ATOL)
+    return {"ok": ok, "max_abs": round(max_abs, 6), "max_rel": round(max_rel, 6), "n_checked": 1,
+            "checked": f"sequence {b} (median cached context {int(d['ctx'][b])}), all 32 heads x 512 rows",
+            "tolerance": f"rtol {RTOL}, atol {ATOL}", "oracle": "oracle.paged_attention.paged_prefill, fp32"}
+
+
+def sdpa_parity(d, out):
+    """fp32 SDPA against the reference's CPU path (repeat_kv + CPU SDPA):
+    ||a - b||_inf / ||b||_inf <= 1e-5."""
+    from oracle import sdpa as osd
+
+    ref = osd.sdpa_reference(d["q"], d["k"], d["v"], None, 0.0, True, d["scale"]).float()
+    got = out.cpu().float()
+    rel = float((got - ref).abs().max() / ref.abs().max())
+    return {"ok": rel <= 1e-5 if d["q"].dtype == torch.float32 else rel <= 3e-2,
+            "max_abs": round(float((got - ref).abs().max()), 8), "max_rel": rel, "n_checked": 1,
+            "checked": "the whole output", "tolerance": "||a-b||_inf / ||b||_inf <= 1e-5 (fp32)",
+            "oracle": "oracle.sdpa.sdpa_reference (the reference's _sdpa_cpu_fallback path)"}
 
 
 def _cpu_prefill_sample(d, b):
@@ -825,52 +1070,39 @@ def _cpu_compute_times(wl, d, reps, budget_s):
         times.append(time.perf_counter() - t)
         if time.perf_counter() > t_end:
             break
-    return statistics.median(times), flops, sample, len(times)
+    return times, flops, sample
 
 
 def cpu_baseline_compute(wl, d, budget_s):
-    med, flops, sample, n = _cpu_compute_times(wl, d, 5, budget_s)
+    times, flops, sample = _cpu_compute_times(wl, d, 5, budget_s)
+    med = statistics.median(times)
     return {"value": round(flops / med / 1e12, 5), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": sample + f", median of {n} runs, {med * 1e3:.1f} ms", "ms_per_sample": round(med * 1e3, 2)}
+            "sample": sample + ", " + _cpu_stats_note(times), "ms_per_sample": round(med * 1e3, 2)}
 
 
-def run_reference_compute(args, wl_name):
-    ws, rank, local = dist_env()
-    if rank != 0:
-        return
+def reference_compute_line(args, ctx: Ctx, wl_name: str, budget_s=120.0) -> dict:
     wl = COMPUTE[wl_name]
     d = build_prefill(wl, torch.device("cpu"), seed=0) if wl["kind"] == "prefill" else build_sdpa(wl, seed=0)
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 1)):
         _cpu_compute_times(wl, d, 1, 1e9)
-    med, flops, sample, n = _cpu_compute_times(wl, d, args.steps, 120.0)
+    times, flops, sample = _cpu_compute_times(wl, d, args.steps, budget_s)
+    med = statistics.median(times)
     val = flops / med / 1e12
-    unit = "TFLOP/s"
     metric = {"prefill": "paged chunked prefill TFLOP/s", "sdpa_bwd": "SDPA backward TFLOP/s"}.get(wl["kind"],
                                                                                                  "SDPA TFLOP/s")
-    line = {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": unit, "n_gpus": ws, "steps": n,
-            "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32" if wl["kind"] != "prefill" and wl["dtype"] == torch.float32 else "bf16",
-            "data": "synthetic (seeded)", "config": {"workload": wl["desc"]},
-            "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    dtype = "f32" if wl["kind"] != "prefill" and wl["dtype"] == torch.float32 else "bf16"
+    return {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": "TFLOP/s", "n_gpus": ctx.ws,
+            "steps": len(times), "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)",
+            "config": {"workload": wl["desc"]},
+            "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": sample + ", " + _cpu_stats_note(times)},
+            "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 # ---------------------------------------------------------------------------
 # standalone KV-cache write (HBM-bound)
 # ---------------------------------------------------------------------------
-KVWRITE = {
-    "kv_write_fp8": dict(B=64, Hkv=8, D=128, bs=16, S=512, cmax=4096,
-                         desc="paged KV write bf16 -> fp8-e4m3 cache, per-(block, head) scale recompute: B=64 "
-                              "sequences x 512 new rows, Hkv=8, D=128, bs=16, start ~U[0,4096]"),
-    # profiling case for ncu --set full
-    "kv_write_fp8_small": dict(B=16, Hkv=8, D=128, bs=16, S=512, cmax=4096,
-                               desc="paged KV write bf16 -> fp8-e4m3 cache: B=16 sequences x 512 new rows, Hkv=8, "
-                                    "D=128, bs=16"),
-}
-
-
 def build_kv_write(wl, seed=0):
     g = torch.Generator().manual_seed(seed)
     B, Hkv, D, bs, S = wl["B"], wl["Hkv"], wl["D"], wl["bs"], wl["S"]
@@ -889,7 +1121,7 @@ def build_kv_write(wl, seed=0):
 
 
 def _cpu_kv_write(d, budget_s):
-    """oracle.paged_attention.kv_write on one sequence (all KV heads)."""
+    """oracle.paged_attention.kv_write on one sequence (all KV heads) per run."""
     from oracle import paged_attention as opa
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -908,35 +1140,14 @@ def _cpu_kv_write(d, budget_s):
         if time.perf_counter() > t_end or len(times) >= d["B"]:
             break
     med = statistics.median(times)
-    return per_seq / med / 1e9, med, len(times)
+    return per_seq / med / 1e9, med, times
 
 
-def run_kv_write(args, wl_name):
-    import ctypes
-
-    ws, rank, local = dist_env()
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        wl = KVWRITE[wl_name]
-        d = build_kv_write(wl)
-        val, med, n = _cpu_kv_write(d, max(10.0, args.cpu_budget))
-        sample = f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, median of {n} runs"
-        print(json.dumps({"impl": "reference", "metric": "paged KV write GB/s", "value": round(val, 4),
-                          "unit": "GB/s", "n_gpus": ws, "steps": n, "warmup": args.warmup,
-                          "ms_per_step": round(med * 1e3 * d["B"], 3), "higher_is_better": True, "scaling": "weak",
-                          "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)",
-                          "config": {"workload": wl["desc"]},
-                          "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
-                                           "kind": "port", "sample": sample},
-                          "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                                  "d2h_bytes_per_step": 0}}), flush=True)
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
     import torch_rbln_b200  # noqa: F401
     from torch_rbln_b200 import cabi
 
+    ws, rank, dev, stream = ctx.ws, ctx.rank, ctx.dev, ctx.stream
     wl = KVWRITE[wl_name]
     d = build_kv_write(wl, seed=1000 * rank)
     k, v, seq, bt = (d[x].to(dev) for x in ("k", "v", "seq", "bt"))
@@ -948,7 +1159,6 @@ def run_kv_write(args, wl_name):
     qshape = torch.empty([d["B"], d["Hkv"], 1, d["S"], d["D"]], dtype=torch.bfloat16, device=dev)
     p, keep = cabi.paged_params(qshape, k, v, kc, vc, seq, bt, d["bs"], 1.0, k_scale=ks, v_scale=vs)
     L = cabi.lib()
-    stream = torch.cuda.current_stream(dev)
     sh = ctypes.c_void_p(stream.cuda_stream)
     pref = ctypes.byref(p)
 
@@ -961,7 +1171,8 @@ def run_kv_write(args, wl_name):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    ctx.barrier()
+    with ClockSampler(ctx.local) as clk:
         op_ms, _ = _timed_kernel_loop(args, stream, step, step, flush)
     # e2e: the torch op with k / v / seq / block_table from pinned host memory, the scales read back
     pinned = [d[x].pin_memory() for x in ("k", "v", "seq", "bt")]
@@ -986,33 +1197,106 @@ def run_kv_write(args, wl_name):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    op_ms, e2e_ms = ctx.reduce([op_ms, e2e_ms], "max")
     hbm_peak, _, peak_src = load_peaks()
     gbs = d["bytes"] / (op_ms * 1e-3) / 1e9
-    line = {
+    rec = {
         "metric": "paged KV write GB/s", "value": round(ws * gbs, 1), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(op_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded N(0,1) rows, seeded starts and block-table permutation)",
-        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}",
+        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
                    "l2": "L2 flushed between iterations (256 MB write, outside the timed events)",
                    "bytes_per_step": d["bytes"]},
         "e2e": {"value": round(ws * d["bytes"] / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "torch.ops.rbln_attn.paged_kv_write"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(gbs / hbm_peak, 4), "traffic": None,
+                     "frac": round(gbs / hbm_peak, 4), "traffic": _traffic_from_profiles(wl_name),
                      "kernel": "paged_kv_write_kernel<bf16, fp8>", "kernel_ms": round(op_ms, 4),
-                     "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                     "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs), of measured" if peak_src == "measured"
                                      else "fallback 6.65 TB/s")},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        val, med, n = _cpu_kv_write(build_kv_write(wl), args.cpu_budget)
-        line["cpu_baseline"] = {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
-                                "sample": f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, "
-                                          f"median of {n} runs, {med * 1e3:.1f} ms"}
-    if rank == 0:
+    if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:
+        val, med, times = _cpu_kv_write(build_kv_write(wl), min(args.cpu_budget, 10.0))
+        rec["cpu_baseline"] = {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, "
+                                         f"{_cpu_stats_note(times)}"}
+    del kc, vc
+    torch.cuda.empty_cache()
+    return rec
+
+
+def reference_kv_write_line(args, ctx: Ctx, wl_name: str, budget_s=10.0) -> dict:
+    wl = KVWRITE[wl_name]
+    d = build_kv_write(wl)
+    val, med, times = _cpu_kv_write(d, budget_s)
+    sample = f"oracle.paged_attention.kv_write, 1 sequence (all KV heads) per run, {_cpu_stats_note(times)}"
+    return {"impl": "reference", "metric": "paged KV write GB/s", "value": round(val, 4),
+            "unit": "GB/s", "n_gpus": ctx.ws, "steps": len(times), "warmup": args.warmup,
+            "ms_per_step": round(med * 1e3 * d["B"], 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)",
+            "config": {"workload": wl["desc"]},
+            "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------
+# entry points
+# ---------------------------------------------------------------------------
+def ours_record(args, ctx, wl_name, cpu_leg=True):
+    if wl_name in KVWRITE:
+        return kv_write_record(args, ctx, wl_name, cpu_leg)
+    if wl_name in COMPUTE:
+        return compute_record(args, ctx, wl_name, cpu_leg)
+    return decode_record(args, ctx, wl_name, n_parity=4 if wl_name == "decode_long" else 8, cpu_leg=cpu_leg)
+
+
+def reference_record(args, ctx, wl_name, per_step_budget=None):
+    if wl_name in KVWRITE:
+        return reference_kv_write_line(args, ctx, wl_name)
+    if wl_name in COMPUTE:
+        return reference_compute_line(args, ctx, wl_name, budget_s=30.0 if per_step_budget else 120.0)
+    return reference_decode_line(args, ctx, wl_name, per_step_budget)
+
+
+def _strip(rec):
+    """A workload record inside the headline line (no repeated run keys)."""
+    return {k: v for k, v in rec.items() if k not in ("n_gpus", "steps", "warmup", "vs_baseline")}
+
+
+def run_suite_ours(args):
+    ctx = Ctx()
+    line = ours_record(args, ctx, SUITE_HEADLINE)
+    line["workloads"] = {}
+    for name, wl_name, multi in SUITE:
+        if ctx.ws > 1 and not multi:
+            continue  # a one-GPU configuration: measured at N = 1
+        line["workloads"][name] = _strip(ours_record(args, ctx, wl_name))
+    if ctx.ws > 1:
+        line["workloads_note"] = ("at N > 1 only the sharded configurations run (long-context decode sharded by "
+                                  "KV head, fp8 decode split by sequence); the others are one-GPU configurations")
+    line["gpu_launches"] = line["gpu_launches"] + sum(r.get("gpu_launches", 0) for r in line["workloads"].values())
+    if ctx.rank == 0:
         print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def run_suite_reference(args):
+    ctx = Ctx(with_gpu=False)
+    if ctx.rank != 0:
+        return  # rank 0 alone times the CPU path
+    line = reference_record(args, ctx, SUITE_HEADLINE)
+    line["workloads"] = {}
+    for name, wl_name, multi in SUITE:
+        if ctx.ws > 1 and not multi:
+            continue
+        small = argparse.Namespace(**vars(args))
+        small.steps, small.warmup = 3, 1
+        line["workloads"][name] = _strip(reference_record(small, ctx, wl_name, per_step_budget=5.0))
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -1021,20 +1305,26 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(COMPUTE) + sorted(KVWRITE))
+    ap.add_argument("--workload", default="suite",
+                    choices=["suite"] + sorted(WORKLOADS) + sorted(COMPUTE) + sorted(KVWRITE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in KVWRITE:
-        run_kv_write(args, args.workload)
-    elif args.workload in COMPUTE:
-        (run_reference_compute if args.impl == "reference" else run_compute_ours)(args, args.workload)
-    elif args.impl == "reference":
-        run_reference(args, args.workload)
-    else:
-        run_ours(args, args.workload)
+    if args.workload == "suite":
+        (run_suite_reference if args.impl == "reference" else run_suite_ours)(args)
+        return
+    if args.impl == "reference":
+        ctx = Ctx(with_gpu=False)
+        if ctx.rank == 0:
+            print(json.dumps(reference_record(args, ctx, args.workload)), flush=True)
+        return
+    ctx = Ctx()
+    rec = ours_record(args, ctx, args.workload)
+    if ctx.rank == 0:
+        print(json.dumps(rec), flush=True)
+    ctx.close()
 
 
 if __name__ == "__main__":

@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this folder from the reference's own CPU code.
 
 Run where a checkout of RBLN-SW/torch-rbln is available (it is not needed to
-run the tests):
+run the tests), naming its root with --reference or TORCH_RBLN_REFERENCE:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <torch-rbln checkout>
 
 Sources executed:
   * the reference's CPU definitions of the paged ops and of
@@ -275,8 +275,11 @@ def sdpa_config1(fallback):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TORCH_RBLN_REFERENCE"),
+                    help="root of a RBLN-SW/torch-rbln checkout (default: $TORCH_RBLN_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or TORCH_RBLN_REFERENCE")
     fallback, backward = load_reference(args.reference)
     torch.manual_seed(0)
     gen = torch.Generator().manual_seed(1234)

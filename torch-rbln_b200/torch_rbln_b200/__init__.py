@@ -4,12 +4,13 @@ Importing this package:
   * loads librbln_attn_torch.so, which defines the rbln_custom_ops schemas
     (identical to the reference's, test/rbln/test_custom_kernel.py:31-486) and
     registers their CUDA kernels; those call the C-ABI in librbln_attn.so
-    (include/rbln_attn.h);
+    (include/rbln_attn.h). The same library registers the SDPA route: CUDA
+    kernels for aten::_scaled_dot_product_fused_attention_overrideable and
+    its backward, and a CUDA _fused_sdp_choice that selects them, mirroring
+    the reference's registration (aten/src/ATen/native/RBLNRegisterOps.cpp:
+    89-105);
   * registers shape-only (fake) implementations for tracing, as the
-    reference does with `register_fake` (test_custom_kernel.py:95-135 ...);
-  * installs the SDPA route (torch_rbln_b200.sdpa), mirroring the
-    reference's aten::_scaled_dot_product_fused_attention_overrideable
-    registration (aten/src/ATen/native/RBLNRegisterOps.cpp:89-105).
+    reference does with `register_fake` (test_custom_kernel.py:95-135 ...).
 
 There is no CPU fallback: the ops have CUDA kernels only, and importing
 fails if the native libraries have not been built (run

@@ -121,6 +121,17 @@ __device__ __forceinline__ void flag_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
 }
 
+// Every kernel of the decode chain is launched as a programmatic dependent
+// of the previous launch on its stream. It first waits until that grid has
+// completed and its writes are visible (a no-op when the previous launch
+// was not made that way), then lets the next grid on the stream be
+// scheduled onto the SMs as this grid's CTAs retire; that grid waits here in
+// the same way, so nothing it reads or writes is touched early.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Stores 4 output elements (one 8-byte pair of pairs) of (b, local head h,
 // query head g, column d4): to `out`, or to every rank's buffer when the
 // heads are sharded over GPUs.
@@ -561,6 +572,7 @@ __device__ __forceinline__ int seq_len(const DecodeArgs& a, int b, int& pos) {
 template <int D, int KV, bool Q_BF16, int NT, bool LA>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_split_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
+  pdl_enter();
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   int pos, L, nsplit;
   decode_extent(a, b, pos, L, nsplit);
@@ -623,6 +635,7 @@ __device__ __forceinline__ int balanced_prefix(const DecodeArgs& a, int* P) {
 template <int D, int KV, bool Q_BF16, int NT, bool LA>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanced_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) unsigned char dsm[];
+  pdl_enter();
   int* P = reinterpret_cast<int*>(dsm + segment_smem<D, NT>());
   const int c = blockIdx.x, h = blockIdx.y;
   const int W = balanced_prefix(a, P);
@@ -701,7 +714,7 @@ template <int D, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
   // launched as a programmatic dependent of the split kernel: wait here until
   // that grid has completed and its writes are visible
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_enter();
   const int h = blockIdx.x, b = blockIdx.y;
   int pos, L, nsplit;
   decode_extent(a, b, pos, L, nsplit);
@@ -746,7 +759,7 @@ __device__ __forceinline__ void peer_epoch_exchange(uint32_t* const* flags, int 
 // exchange, so the call needs no separate barrier launch.
 template <int D, int KV, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(const DecodeArgs a) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_enter();
   const int h = blockIdx.x, b = blockIdx.y;
   int pos;
   const int L = seq_len(a, b, pos);
@@ -922,8 +935,9 @@ bool allow_smem(const void* kernel, int bytes, SmemOptIn& opt) {
 }
 
 // Launches `kernel` as a programmatic dependent of the previous launch on
-// `st`: its grid is set up while that one drains and waits in-kernel
-// (griddepcontrol.wait) for its completion.
+// `st`: its CTAs may be scheduled while that grid drains (once all of that
+// grid's CTAs have signalled launch_dependents) and wait in-kernel
+// (pdl_enter) for its completion.
 int launch_dependent(void (*kernel)(DecodeArgs), dim3 grid, size_t smem, cudaStream_t st, const DecodeArgs& a) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -946,7 +960,9 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
     static SmemOptIn done;
     if (!allow_smem(reinterpret_cast<const void*>(paged_decode_balanced_kernel<D, KV, QB, NT, LA>), (int)smem, done))
       return RBLN_ERR_LAUNCH;
-    paged_decode_balanced_kernel<D, KV, QB, NT, LA><<<dim3(pl.nchunk, a.Hkv), kThreads, smem, st>>>(a);
+    const int drc =
+        launch_dependent(paged_decode_balanced_kernel<D, KV, QB, NT, LA>, dim3(pl.nchunk, a.Hkv), smem, st, a);
+    if (drc != RBLN_OK) return drc;
     if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
     // a sequence spans at most nchunk + 1 chunks
     const size_t msmem = ((size_t)(pl.nchunk + 1) * a.G + a.G) * sizeof(float);
@@ -961,8 +977,9 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
   if (!allow_smem(reinterpret_cast<const void*>(paged_decode_split_kernel<D, KV, QB, NT, LA>), segment_smem<D, NT>(),
                   sdone))
     return RBLN_ERR_LAUNCH;
-  paged_decode_split_kernel<D, KV, QB, NT, LA>
-      <<<dim3(pl.max_splits, a.Hkv, a.B), kThreads, segment_smem<D, NT>(), st>>>(a);
+  const int drc = launch_dependent(paged_decode_split_kernel<D, KV, QB, NT, LA>, dim3(pl.max_splits, a.Hkv, a.B),
+                                   segment_smem<D, NT>(), st, a);
+  if (drc != RBLN_OK) return drc;
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
     const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);

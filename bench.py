@@ -101,6 +101,14 @@ COMPUTE = {
                          "cached ctx~U[0,8192], bs=16, causal"),
     "prefill_small": dict(kind="prefill", B=2, Hkv=8, G=4, D=128, bs=16, S=512, cmin=2048, cmax=6144,
                           desc="paged chunked prefill bf16 B=2 Hq=32 Hkv=8 D=128 S_q=512 ctx~U[2048,6144]"),
+    # the same chunks through paged_attn_prefill with an offset-causal keep-mask [B, 1, 1, S_q, span]
+    # (key t kept for query row s when t <= ctx_b + s), as the reference's tests drive that op
+    "prefill_mask": dict(kind="prefill", keep_mask=True, B=8, Hkv=8, G=4, D=128, bs=16, S=512, cmin=0, cmax=8192,
+                         desc="paged chunked prefill with a keep-mask (paged_attn_prefill) bf16 B=8 Hq=32 Hkv=8 "
+                              "D=128 S_q=512 new tokens, cached ctx~U[0,8192], bs=16, offset-causal bf16 mask"),
+    "prefill_mask_small": dict(kind="prefill", keep_mask=True, B=2, Hkv=8, G=4, D=128, bs=16, S=512, cmin=2048,
+                               cmax=6144, desc="paged chunked prefill with a keep-mask bf16 B=2 Hq=32 Hkv=8 D=128 "
+                                               "S_q=512 ctx~U[2048,6144]"),
     "sdpa": dict(kind="sdpa", B=1, Hq=32, Hkv=8, L=512, D=64, dtype=torch.float32,
                  desc="SDPA causal GQA fp32 B=1 Hq=32 Hkv=8 L=S=512 D=64 (Llama-3.2-1B attention shape)"),
     "sdpa_bf16": dict(kind="sdpa", B=4, Hq=32, Hkv=8, L=4096, D=128, dtype=torch.bfloat16,
@@ -124,7 +132,8 @@ KVWRITE = {
 # (name in the line -> workload, and whether it runs at N > 1)
 SUITE_HEADLINE = "decode"
 SUITE = [("long_context_decode", "decode_long", True), ("fp8_decode", "decode_fp8", True),
-         ("chunked_prefill", "prefill", False), ("sdpa_f32", "sdpa", False),
+         ("chunked_prefill", "prefill", False), ("chunked_prefill_keep_mask", "prefill_mask", False),
+         ("sdpa_f32", "sdpa", False),
          ("sdpa_backward", "sdpa_bwd", False), ("kv_write_fp8", "kv_write_fp8", False)]
 
 
@@ -766,8 +775,14 @@ def build_prefill(wl, device, seed=0):
     vc = torch.randn(shape, generator=gd, device=device, dtype=torch.bfloat16)
     Hq = Hkv * G
     flops = sum(4 * D * Hq * (S * int(c) + S * (S + 1) // 2) for c in ctx)
-    return dict(q=q, k=k, v=v, kcache=kc, vcache=vc, seq=ctx.to(torch.int32).reshape(B, 1), bt=bt, bs=bs,
-                ctx=ctx, flops=flops, scale=1.0 / math.sqrt(D), B=B, Hkv=Hkv, G=G, D=D, S=S)
+    d = dict(q=q, k=k, v=v, kcache=kc, vcache=vc, seq=ctx.to(torch.int32).reshape(B, 1), bt=bt, bs=bs,
+             ctx=ctx, flops=flops, scale=1.0 / math.sqrt(D), B=B, Hkv=Hkv, G=G, D=D, S=S)
+    if wl.get("keep_mask"):
+        span = max_blocks * bs
+        t = torch.arange(span).reshape(1, 1, span)
+        qi = torch.arange(S).reshape(1, S, 1) + ctx.reshape(B, 1, 1)
+        d["mask"] = (t <= qi).to(torch.bfloat16).reshape(B, 1, 1, S, span)
+    return d
 
 
 def build_sdpa(wl, seed=0):
@@ -786,21 +801,26 @@ def build_sdpa(wl, seed=0):
     return d
 
 
-def _timed_kernel_loop(args, stream, step, kernel_step, flush):
+def _timed_kernel_loop(args, stream, step, kernel_step, flush, kernel_events=False):
     """Per-iteration CUDA events on the launch stream around the whole op
     (`step`) and, in separate iterations, around the main kernel alone
-    (`kernel_step`), each preceded by an L2 flush outside the timed window."""
-    def timed(fn):
+    (`kernel_step`; with kernel_events it takes the event pair and has the
+    C-ABI record it right around the kernel), each preceded by an L2 flush
+    outside the timed window."""
+    def timed(fn, inner=False):
         ev = _event_pairs(args.steps, stream)
         for i in range(args.steps):
             flush.zero_()
+            if inner:
+                fn(*ev[i])
+                continue
             ev[i][0].record(stream)
             fn()
             ev[i][1].record(stream)
         torch.cuda.synchronize()
         return statistics.mean(a.elapsed_time(b) for a, b in ev)
 
-    return timed(step), timed(kernel_step)
+    return timed(step), timed(kernel_step, kernel_events)
 
 
 def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
@@ -817,36 +837,46 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
         d = build_prefill(wl, dev, seed=1000 * rank)
         q, k, v, seq, bt = (d[x].to(dev) for x in ("q", "k", "v", "seq", "bt"))
         kc, vc = d["kcache"], d["vcache"]
-        p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
-        # the same call without new rows to append launches the attention kernel alone
-        pk, keepk = cabi.paged_params(q, None, None, kc, vc, seq, bt, d["bs"], d["scale"], causal=1)
+        masked = "mask" in d
+        mask = d["mask"].to(dev) if masked else None
+        entry = L.rbln_paged_attn_prefill if masked else L.rbln_paged_causal_attn_prefill
+        p, keep = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"], causal=1, mask=mask)
         cabi.attach_workspace(p, dev, keep, prefill=True)
-        cabi.attach_workspace(pk, dev, keepk, prefill=True)
-        pref, pkref = ctypes.byref(p), ctypes.byref(pk)
+        pref = ctypes.byref(p)
         scale_t = torch.tensor(d["scale"])
 
         def step():
-            rc = L.rbln_paged_causal_attn_prefill(pref, sh)
+            p.prof_events[0] = p.prof_events[1] = None
+            rc = entry(pref, sh)
             if rc != 0:
-                raise RuntimeError(f"rbln_paged_causal_attn_prefill failed: {rc}")
+                raise RuntimeError(f"paged prefill failed: {rc}")
 
-        def kernel_step():
-            rc = L.rbln_paged_causal_attn_prefill(pkref, sh)
+        def kernel_step(ev0, ev1):  # the whole call; events recorded around the attention kernel
+            p.prof_events[0], p.prof_events[1] = ev0.cuda_event, ev1.cuda_event
+            rc = entry(pref, sh)
             if rc != 0:
-                raise RuntimeError(f"rbln_paged_causal_attn_prefill failed: {rc}")
+                raise RuntimeError(f"paged prefill failed: {rc}")
 
-        def op_call(qq, kk, vv, ss, bb):
-            return torch.ops.rbln_custom_ops.paged_causal_attn_prefill(qq, kk, vv, kc, vc, ss, scale_t, bb, d["bs"],
-                                                                       False)
+        if masked:
+            def op_call(qq, kk, vv, ss, bb, mm):
+                return torch.ops.rbln_custom_ops.paged_attn_prefill(qq, kk, vv, mm, kc, vc, ss, scale_t, bb, d["bs"])
+        else:
+            def op_call(qq, kk, vv, ss, bb):
+                return torch.ops.rbln_custom_ops.paged_causal_attn_prefill(qq, kk, vv, kc, vc, ss, scale_t, bb,
+                                                                           d["bs"], False)
 
-        host_inputs = [d["q"], d["k"], d["v"], d["seq"], d["bt"]]
+        host_inputs = [d["q"], d["k"], d["v"], d["seq"], d["bt"]] + ([d["mask"]] if masked else [])
         out_shape, out_dtype = q.shape, q.dtype
         metric = "paged chunked prefill TFLOP/s"
-        launches = 3  # schedule pre-pass, append, attention
-        kernel = "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)"
+        # append, schedule pre-pass, attention (+ the mask pre-pass's bits and lists)
+        launches = 5 if masked else 3
+        kernel = ("attn_fwd_tc3_kernel<128, bf16" + (", masked" if masked else "") +
+                  "> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)")
         dtype = "bf16"
+        kernel_events = True
         result["parity"] = lambda: prefill_parity(d, keep["out"])
     elif wl["kind"] == "sdpa_bwd":
+        kernel_events = False
         d = build_sdpa(wl, seed=0)
         q, k, v, dout = (d[x].to(dev) for x in ("q", "k", "v", "dout"))
         fwd = torch.ops.aten._scaled_dot_product_fused_attention_overrideable(q, k, v, None, 0.0, True, False,
@@ -881,6 +911,7 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
                   "(tcgen05/TMEM/TMA; whole backward timed)")
         dtype = "bf16"
     else:
+        kernel_events = False
         d = build_sdpa(wl, seed=0)
         q, k, v = (d[x].to(dev) for x in ("q", "k", "v"))
         out = torch.empty_like(q)
@@ -916,7 +947,7 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
     torch.cuda.synchronize()
     ctx.barrier()
     with ClockSampler(ctx.local) as clk:
-        op_ms, k_ms = _timed_kernel_loop(args, stream, step, kernel_step, flush)
+        op_ms, k_ms = _timed_kernel_loop(args, stream, step, kernel_step, flush, kernel_events)
     ctx.barrier()
 
     # e2e through the public torch API with host buffers
@@ -963,7 +994,8 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
                    "l2": l2, "flops_per_step": flops},
         "e2e": {"value": round(ws * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "api": {"prefill": "torch.ops.rbln_custom_ops.paged_causal_attn_prefill",
+                "api": {"prefill": ("torch.ops.rbln_custom_ops.paged_attn_prefill" if wl.get("keep_mask") else
+                                    "torch.ops.rbln_custom_ops.paged_causal_attn_prefill"),
                         "sdpa_bwd": "torch.ops.aten._scaled_dot_product_fused_attention_overrideable_backward"}.get(
                             wl["kind"], "torch.nn.functional.scaled_dot_product_attention")},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_peak, "unit": "TFLOP/s",
@@ -995,8 +1027,9 @@ def prefill_parity(d, out):
     dv = d["kcache"].device
     kc, vc = d["kcache"][blocks.to(dv)].cpu(), d["vcache"][blocks.to(dv)].cpu()
     table = torch.arange(nb, dtype=torch.int32).reshape(1, nb)
+    mask = d["mask"][b:b + 1] if "mask" in d else None  # a keep-mask run checks against the same mask
     ref = opa.paged_prefill(d["q"][b:b + 1], d["k"][b:b + 1], d["v"][b:b + 1], kc, vc, d["seq"][b:b + 1],
-                            d["scale"], table, d["bs"], causal=True, mode="fp32")
+                            d["scale"], table, d["bs"], mask=mask, causal=True, mode="fp32")
     ok, max_abs, max_rel = _tolerance_stats(out[b:b + 1].cpu(), ref, RTOL, ATOL)
     return {"ok": ok, "max_abs": round(max_abs, 6), "max_rel": round(max_rel, 6), "n_checked": 1,
             "checked": f"sequence {b} (median cached context {int(d['ctx'][b])}), all 32 heads x 512 rows",

@@ -88,7 +88,13 @@ struct AttnArgs {
   uint32_t* err;
   const int* work;  // optional: items (b * q_tiles + tile) in launch order, longest first
   int* counter;     // optional: next unit of a persistent launch (zeroed by the schedule pre-pass)
-  const float* sinks;  // optional [Hkv * G] sink logits (natural-log units), index h * G + g; v1 kernel only
+  const float* sinks;  // optional [Hkv * G] sink logits (natural-log units), index h * G + g
+  // 128-key kernel with a keep rule other than plain causal / bidirectional
+  // (a keep-mask, or a position mask): written by the mask pre-pass
+  const uint4* kbits;  // [B][S_q][nkt]: bit e of word w keeps key 128 * kt + 32 * w + e for that query row
+  const int* tlist;    // [items][nkt]: each item's key tiles with a kept key, bit 31 set when not all kept
+  const int* tcount;   // [items]: entries of each item's list
+  int nkt;             // key tiles per row, ceil(span / 128)
 };
 
 __device__ __forceinline__ float mask_value(const void* base, int dt, int64_t i) {
@@ -1034,6 +1040,7 @@ enum Bar3 {
 // order. Every role of a CTA derives the same units, in the same order.
 struct Unit3 {
   int b, h, s0, seq_off, kv_end, ntiles;
+  const int* list;  // masked launch: the item's key tiles (entry j: tile, bit 31 = not all kept); else null
 };
 __device__ __forceinline__ Unit3 unit3(const AttnArgs& a, int u) {
   Unit3 t;
@@ -1051,14 +1058,35 @@ __device__ __forceinline__ Unit3 unit3(const AttnArgs& a, int u) {
   t.s0 = qtile * 2 * a.QT;
   t.seq_off = a.seq ? a.seq[t.b * a.seq_stride] : 0;
   t.kv_end = 0;
+  t.list = nullptr;
   if (t.seq_off >= 0) {
     const int s_hi = min(t.s0 + 2 * a.QT, a.S_q);
-    int end = (a.mask_mode == MM_CAUSAL) ? t.seq_off + s_hi : ((a.bt == nullptr) ? a.kv_extra : t.seq_off + a.S_q);
+    int end = (a.mask_mode == MM_CAUSAL) ? t.seq_off + s_hi
+              : (a.mask_mode == MM_KEEP) ? a.mask_len
+              : ((a.bt == nullptr) ? a.kv_extra : t.seq_off + a.S_q);
     if (a.bt == nullptr) end = min(end, a.kv_extra);
     t.kv_end = max(0, min(end, a.span));
   }
-  t.ntiles = (t.kv_end + BN3 - 1) / BN3;
+  if (a.tcount) {
+    // the mask pre-pass listed the tiles with a kept key (none for seq < 0)
+    const int it = t.b * a.q_tiles + qtile;
+    t.ntiles = a.tcount[it];
+    t.list = a.tlist + (int64_t)it * a.nkt;
+  } else {
+    t.ntiles = (t.kv_end + BN3 - 1) / BN3;
+  }
   return t;
+}
+
+// Key tile (index) and "not every key kept" flag of entry j of a unit.
+__device__ __forceinline__ int unit3_tile(const Unit3& t, int j, bool& mixed) {
+  if (t.list == nullptr) {
+    mixed = false;
+    return j;
+  }
+  const int e = t.list[j];
+  mixed = e < 0;
+  return e & 0x7fffffff;
 }
 
 // Persistent: one CTA per SM. The producer takes the next unit from the
@@ -1071,7 +1099,7 @@ __device__ __forceinline__ Unit3 unit3(const AttnArgs& a, int u) {
 // one. Q is reloaded after the previous unit's last QK (E_QE); a unit's
 // first PV overwrites O only after the softmax has read the previous O
 // (E_OEA/B).
-template <int D, bool BF16, int POLY>
+template <int D, bool BF16, int POLY, bool MASKED>
 __global__ void __launch_bounds__(kThreads3, 1)
     attn_fwd_tc3_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_units) {
@@ -1157,7 +1185,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
         // lane i < nbox fetches rows [i*rpb, (i+1)*rpb) of the tile
         int blk = a.num_blocks;  // out of range -> zero fill
         int row = 0;
-        const int key = j * BN3 + lane * rpb;
+        bool mixed;
+        const int key = (MASKED ? unit3_tile(t, j, mixed) : j) * BN3 + lane * rpb;
         if (lane < nbox && key < t.kv_end) {
           if (a.bt == nullptr) {
             blk = t.b;
@@ -1333,15 +1362,20 @@ __global__ void __launch_bounds__(kThreads3, 1)
 
       for (int j = 0; j < ntiles; ++j) {
         const int Tj = T + j;
+        bool mixed = false;
+        const int t0 = (MASKED ? unit3_tile(t, j, mixed) : j) * BN3;
+        // a partly kept tile: the row's keep bits, loaded before the wait for S
+        uint4 kb = make_uint4(0u, 0u, 0u, 0u);
+        if (MASKED && mixed && row_ok) kb = a.kbits[((int64_t)t.b * a.S_q + s) * a.nkt + t0 / BN3];
         if (!__all_sync(0xffffffffu, mbar_wait(bar(bar_sf), Tj & 1, abort))) {
           ok = false;
           break;
         }
         tc_fence_after();
         __syncwarp();
-        const int t0 = j * BN3;
-        const bool interior = (a.mask_mode == MM_CAUSAL) ? (t0 + BN3 - 1 <= tile_first_q) && (t0 + BN3 <= kv_end)
-                                                         : (t0 + BN3 <= kv_end);
+        const bool interior = MASKED ? !mixed
+                              : (a.mask_mode == MM_CAUSAL) ? (t0 + BN3 - 1 <= tile_first_q) && (t0 + BN3 <= kv_end)
+                                                           : (t0 + BN3 <= kv_end);
         const int lim = (a.mask_mode == MM_CAUSAL) ? min(qpos + 1, kv_end) : min(none_limit, kv_end);
         // the row's 128 scores: four loads, one wait
         float xv[BN3];
@@ -1368,9 +1402,16 @@ __global__ void __launch_bounds__(kThreads3, 1)
           for (int e = 0; e < BN3; e += 2) mul2(xv[e], xv[e + 1], qk_mult, qk_mult);
         }
         if (!(interior && row_ok)) {
+          if constexpr (MASKED) {  // keep bits of the row (all zero for a row outside the chunk)
+            const uint32_t kw[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-          for (int e = 0; e < BN3; ++e)
-            if (!(row_ok && t0 + e < lim)) xv[e] = neg_inf();
+            for (int e = 0; e < BN3; ++e)
+              if (!((kw[e >> 5] >> (e & 31)) & 1u)) xv[e] = neg_inf();
+          } else {
+#pragma unroll
+            for (int e = 0; e < BN3; ++e)
+              if (!(row_ok && t0 + e < lim)) xv[e] = neg_inf();
+          }
         }
         float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
 #pragma unroll
@@ -1433,10 +1474,10 @@ __global__ void __launch_bounds__(kThreads3, 1)
           tmem_st16(t_s(x) + lane_off + c4 * 16, pk);
         }
         tmem_wait_st();
-        // keys past kv_end in the last tile may hold unwritten memory: tile A's
-        // warpgroup zeroes their V rows before its P is released (both PV MMAs
-        // of this tile come after that release)
-        if (x == 0 && j == ntiles - 1 && t0 + BN3 > kv_end) {
+        // keys past kv_end in the tile that holds kv_end may be unwritten
+        // memory: tile A's warpgroup zeroes their V rows before its P is
+        // released (both PV MMAs of this tile come after that release)
+        if (x == 0 && t0 < kv_end && t0 + BN3 > kv_end) {
           const int sv = Tj % VS;
           if (!__all_sync(0xffffffffu, mbar_wait(bar(E_VF0 + sv), (Tj / VS) & 1, abort))) {
             ok = false;
@@ -1462,7 +1503,11 @@ __global__ void __launch_bounds__(kThreads3, 1)
       if (ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(bar_o), act & 1, abort));
       if (!ok) break;
       tc_fence_after();
-      const float inv = 1.f / l_run;
+      // an attention sink adds e^{sink} (relative to the running max) to the
+      // denominator only; a row with no visible key then gives 0, not NaN
+      float lsum = l_run;
+      if (a.sinks && row_ok) lsum += exp2f(a.sinks[t.h * a.G + g] * kLog2e - m_run);
+      const float inv = 1.f / lsum;
       char* orow = a.out + t.b * a.os_b + t.h * a.os_h + g * a.os_g + (int64_t)s * a.os_s;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -1518,11 +1563,15 @@ __global__ void __launch_bounds__(kThreads3, 1)
 // ranks items by counting the items that go before them.
 __global__ void __launch_bounds__(256) prefill_schedule_kernel(const int32_t* seq, int64_t seq_stride, int B,
                                                                int q_tiles, int S_q, int tile_tokens, int span,
-                                                               int causal, int* work) {
+                                                               int causal, const int* tcount, int* work) {
   extern __shared__ int cost[];
   const int n = B * q_tiles;
   if (threadIdx.x == 0) work[n] = 0;  // unit counter of a persistent launch
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    if (tcount) {  // masked launch: the key tiles the mask pre-pass listed
+      cost[i] = tcount[i];
+      continue;
+    }
     const int b = i / q_tiles, t = i - b * q_tiles;
     const int off = max(0, seq[b * seq_stride]);
     const int hi = min((t + 1) * tile_tokens, S_q);
@@ -1538,6 +1587,72 @@ __global__ void __launch_bounds__(256) prefill_schedule_kernel(const int32_t* se
     }
     work[rank] = i;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Mask pre-pass of the 128-key kernel. For a keep rule other than plain
+// causal / bidirectional (a keep-mask with value > 0 keeping a key, or a
+// position mask on top of causal / bidirectional), every query row of the
+// chunk gets 128 keep bits per 128-key tile, and every (item, key tile) a
+// class: no key kept (the tile is skipped), every key of every row kept
+// (no masking), or mixed (the softmax applies the row's bits). Each mask
+// element is read once; a key at or past the span is never kept, nor is any
+// key of a sequence whose start offset is negative.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool keep_key(const AttnArgs& a, int b, int s, int t, int seq_off) {
+  if (seq_off < 0 || t >= a.span) return false;
+  bool keep;
+  if (a.mask_mode == MM_KEEP) {
+    keep = t < a.mask_len && mask_value(a.mask, a.mask_dtype, b * a.m_b + (int64_t)s * a.m_s + t) > 0.f;
+  } else if (a.mask_mode == MM_CAUSAL) {
+    keep = t <= seq_off + s;
+  } else {
+    keep = t < seq_off + a.S_q;
+  }
+  if (keep && a.pmask) keep = t < a.pmask_len && mask_value(a.pmask, a.pmask_dtype, b * a.pm_b + t) > 0.f;
+  return keep;
+}
+
+// grid (nkt, items), 8 warps: rows [s0, s0 + 2 QT) of item (b, query-tile
+// pair) x keys [128 kt, 128 kt + 128). A warp takes one (row, 32-key word)
+// at a time: lane l tests key 32 w + l (coalesced) and a ballot makes the
+// word. Class: 0 no key kept, 1 all kept, 2 mixed (over the chunk's rows).
+__global__ void __launch_bounds__(256) prefill_mask_bits_kernel(const AttnArgs a, uint4* kbits, uint8_t* cls) {
+  const int kt = blockIdx.x, item = blockIdx.y;
+  const int b = item / a.q_tiles, qp = item - b * a.q_tiles;
+  const int s0 = qp * 2 * a.QT;
+  const int rows = min(2 * a.QT, a.S_q - s0);
+  const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool any_keep = false, any_drop = false;
+  for (int task = warp; task < rows * 4; task += 8) {
+    const int i = task >> 2, w = task & 3;
+    const int s = s0 + i;
+    const uint32_t bits = __ballot_sync(0xffffffffu, keep_key(a, b, s, kt * 128 + w * 32 + lane, seq_off));
+    if (lane == 0) reinterpret_cast<uint32_t*>(kbits + ((int64_t)b * a.S_q + s) * a.nkt + kt)[w] = bits;
+    any_keep |= bits != 0u;
+    any_drop |= bits != 0xffffffffu;
+  }
+  any_keep = __syncthreads_or(any_keep);
+  any_drop = __syncthreads_or(any_drop);
+  if (threadIdx.x == 0) cls[(int64_t)item * a.nkt + kt] = any_keep ? (any_drop ? 2 : 1) : 0;
+}
+
+// One warp per item: the key tiles with a kept key, in order, as
+// tile | (mixed << 31), and their number.
+__global__ void __launch_bounds__(256) prefill_mask_list_kernel(const uint8_t* cls, int nkt, int items, int* tlist,
+                                                                int* tcount) {
+  const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (item >= items) return;
+  int n = 0;
+  for (int k0 = 0; k0 < nkt; k0 += 32) {
+    const int kt = k0 + lane;
+    const int c = kt < nkt ? cls[(int64_t)item * nkt + kt] : 0;
+    const uint32_t m = __ballot_sync(0xffffffffu, c != 0);
+    if (c) tlist[(int64_t)item * nkt + n + __popc(m & ((1u << lane) - 1u))] = kt | (c == 2 ? (int)0x80000000 : 0);
+    n += __popc(m);
+  }
+  if (lane == 0) tcount[item] = n;
 }
 
 // Writes the chunk's new k/v rows into the paged cache at [seq[b], seq[b]+S_q).
@@ -1624,18 +1739,18 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int D, bool BF16, int POLY>
+template <int D, bool BF16, int POLY, bool MASKED>
 int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
   using SL = SmemLayout3<D>;
   // The warpgroups' setmaxnreg split assumes 168 registers per thread at
   // launch; with fewer, a warpgroup raising its count would never be served.
   static const bool regs_ok = [] {
     cudaFuncAttributes fa{};
-    return cudaFuncGetAttributes(&fa, attn_fwd_tc3_kernel<D, BF16, POLY>) == cudaSuccess &&
+    return cudaFuncGetAttributes(&fa, attn_fwd_tc3_kernel<D, BF16, POLY, MASKED>) == cudaSuccess &&
            2 * 128 * kRegsSoftmax3 + 128 * kRegsOther3 <= (uint32_t)fa.numRegs * kThreads3;
   }();
   if (!regs_ok) return RBLN_ERR_LAUNCH;
-  if (cudaFuncSetAttribute(attn_fwd_tc3_kernel<D, BF16, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(attn_fwd_tc3_kernel<D, BF16, POLY, MASKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            SL::ALLOC) != cudaSuccess)
     return RBLN_ERR_LAUNCH;
   const long long n = (long long)Lc.a.q_tiles * Lc.a.B * Lc.a.Hkv;
@@ -1643,7 +1758,7 @@ int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
   // persistent: one CTA per SM, each striding through the units
   const int grid = (int)std::min<long long>(n, sm_count());
   if (grid == 0) return RBLN_OK;
-  attn_fwd_tc3_kernel<D, BF16, POLY><<<grid, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n);
+  attn_fwd_tc3_kernel<D, BF16, POLY, MASKED><<<grid, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -1662,14 +1777,18 @@ int prefill_poly() {
 template <int D, bool BF16>
 int launch_tc3_poly(const TcLaunch& Lc, cudaStream_t st) {
   switch (prefill_poly()) {
-    case 2: return launch_tc3<D, BF16, 2>(Lc, st);
-    case 4: return launch_tc3<D, BF16, 4>(Lc, st);
-    case 8: return launch_tc3<D, BF16, 8>(Lc, st);
-    default: return launch_tc3<D, BF16, 0>(Lc, st);
+    case 2: return launch_tc3<D, BF16, 2, false>(Lc, st);
+    case 4: return launch_tc3<D, BF16, 4, false>(Lc, st);
+    case 8: return launch_tc3<D, BF16, 8, false>(Lc, st);
+    default: return launch_tc3<D, BF16, 0, false>(Lc, st);
   }
 }
 
 int launch_tc3_any(const TcLaunch& Lc, cudaStream_t st) {
+  if (Lc.a.tcount) {  // masked launch (mask pre-pass lists): the default exponential split only
+    if (Lc.D == 128) return Lc.bf16 ? launch_tc3<128, true, 8, true>(Lc, st) : launch_tc3<128, false, 8, true>(Lc, st);
+    return Lc.bf16 ? launch_tc3<64, true, 8, true>(Lc, st) : launch_tc3<64, false, 8, true>(Lc, st);
+  }
   if (Lc.D == 128) return Lc.bf16 ? launch_tc3_poly<128, true>(Lc, st) : launch_tc3_poly<128, false>(Lc, st);
   return Lc.bf16 ? launch_tc3_poly<64, true>(Lc, st) : launch_tc3_poly<64, false>(Lc, st);
 }
@@ -1711,12 +1830,49 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Items ranked by prefill_schedule_kernel (its shared memory holds one int each).
 constexpr int kMaxScheduledItems = 8192;
 
-int prefill_ws_bytes(const rbln_paged_attn_params_t* p) {
-  if (!p || p->group <= 0 || p->group > BM || p->batch <= 0 || p->q_len <= 0) return 0;
+constexpr size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace of a two-tile (128-key kernel) prefill launch, 256-byte regions:
+//   work     items + 1 ints (longest-first order, then the unit counter),
+//            when items <= kMaxScheduledItems
+//   masked launches (p->mask set) also:
+//   tcount   items ints; tlist items x nkt ints; cls items x nkt bytes;
+//   kbits    B x S_q x nkt x 16 bytes
+struct PrefillWs {
+  size_t work = 0, tcount = 0, tlist = 0, cls = 0, kbits = 0, total = 0;
+  long long items = 0;
+  int nkt = 0;
+};
+
+PrefillWs prefill_ws_layout(const rbln_paged_attn_params_t* p) {
+  PrefillWs w;
+  if (!p || p->group <= 0 || p->group > BM || p->batch <= 0 || p->q_len <= 0 || p->max_blocks <= 0 ||
+      p->block_size <= 0)
+    return w;
   const int QT = BM / p->group;
-  const long long n = (long long)p->batch * ((p->q_len + 2 * QT - 1) / (2 * QT));
-  return n <= kMaxScheduledItems ? (int)((n + 1) * sizeof(int)) : 0;  // items, then the unit counter
+  w.items = (long long)p->batch * ((p->q_len + 2 * QT - 1) / (2 * QT));
+  size_t off = 0;
+  if (w.items <= kMaxScheduledItems) {
+    w.work = off;
+    off += round256((size_t)(w.items + 1) * sizeof(int));
+  }
+  if (p->mask) {
+    const long long span = (long long)p->max_blocks * p->block_size;
+    w.nkt = (int)((span + BN3 - 1) / BN3);
+    w.tcount = off;
+    off += round256((size_t)w.items * sizeof(int));
+    w.tlist = off;
+    off += round256((size_t)w.items * w.nkt * sizeof(int));
+    w.cls = off;
+    off += round256((size_t)w.items * w.nkt);
+    w.kbits = off;
+    off += round256((size_t)p->batch * p->q_len * w.nkt * 16);
+  }
+  w.total = off ? off + 256 : 0;  // + slack to align the base to 256 bytes
+  return w;
 }
+
+size_t prefill_ws_bytes(const rbln_paged_attn_params_t* p) { return prefill_ws_layout(p).total; }
 
 int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_mask_op) {
   if (!p || p->batch < 0 || p->num_kv_heads <= 0 || p->group <= 0 || p->block_size <= 0 || p->max_blocks <= 0 ||
@@ -1768,14 +1924,26 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
     if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
   }
 
-  // 2) attention
+  // 2) attention: the 128-key kernel (3) unless RBLN_ATTN_PREFILL_KERNEL=2
+  // picks the 64-key one; a keep-mask or position mask needs the mask
+  // pre-pass and its workspace, and falls back to the one-tile kernel (1)
+  // without it (as do sinks on the 64-key kernel)
   TcLaunch Lc{};
   Lc.D = D;
   Lc.bf16 = p->q_dtype == RBLN_DT_BF16;
   const int mfk = mask_free_kernel();
-  const bool two_tile = !keep_mask_op && !p->mask && !p->sinks &&
-                        (mfk == 3 || (bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0));
-  const int rpb = std::min(bs, (two_tile && mfk == 2) ? BN2 : BN);
+  const bool masked = keep_mask_op || p->mask != nullptr;
+  const PrefillWs wl = prefill_ws_layout(p);
+  const bool ws_ok = p->workspace != nullptr && wl.total > 0 && p->workspace_bytes >= wl.total;
+  int kern;
+  if (masked)
+    kern = (mfk == 3 && ws_ok && wl.nkt > 0 && wl.items <= 65535) ? 3 : 1;
+  else if (mfk == 3)
+    kern = 3;
+  else
+    kern = (!p->sinks && ((bs >= 8 && bs <= BN2 && BN2 % bs == 0) || (bs >= BN2 && bs % BN2 == 0))) ? 2 : 1;
+  const bool two_tile = kern != 1;
+  const int rpb = std::min(bs, kern == 2 ? BN2 : BN);
   if (!map_q(&Lc.tq, p->q, p->q_dtype, p->batch, p->num_kv_heads, G, p->q_len, D, p->q_stride, QT))
     return RBLN_ERR_LAUNCH;
   if (!map_kv(&Lc.tk, p->kcache, p->kv_dtype, p->num_blocks, p->num_kv_heads, bs, D, p->cache_stride[0],
@@ -1827,18 +1995,33 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
   a.scale_dev = p->scale_dev;
   a.err = p->error_flags;
   a.sinks = p->sinks;
-  if (two_tile && p->workspace) {
-    const int n = p->batch * a.q_tiles;
-    if (n <= kMaxScheduledItems && p->workspace_bytes >= (size_t)(n + 1) * sizeof(int)) {
-      prefill_schedule_kernel<<<1, 256, n * sizeof(int), st>>>(p->seq, p->seq_stride, p->batch, a.q_tiles, p->q_len,
-                                                               2 * QT, (int)span64, p->causal, (int*)p->workspace);
+  if (two_tile && ws_ok) {
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p->workspace) + 255) & ~uintptr_t(255));
+    const int n = p->batch * a.q_tiles;  // == wl.items
+    if (kern == 3 && masked) {
+      // keep bits and tile classes, then each item's list of key tiles
+      a.nkt = wl.nkt;
+      a.kbits = reinterpret_cast<const uint4*>(base + wl.kbits);
+      a.tlist = reinterpret_cast<const int*>(base + wl.tlist);
+      a.tcount = reinterpret_cast<const int*>(base + wl.tcount);
+      prefill_mask_bits_kernel<<<dim3(wl.nkt, n), 256, 0, st>>>(a, reinterpret_cast<uint4*>(base + wl.kbits),
+                                                                 reinterpret_cast<uint8_t*>(base + wl.cls));
+      prefill_mask_list_kernel<<<(n + 7) / 8, 256, 0, st>>>(reinterpret_cast<const uint8_t*>(base + wl.cls), wl.nkt,
+                                                            n, reinterpret_cast<int*>(base + wl.tlist),
+                                                            reinterpret_cast<int*>(base + wl.tcount));
       if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
-      a.work = static_cast<const int*>(p->workspace);
-      a.counter = static_cast<int*>(p->workspace) + n;
+    }
+    if (n <= kMaxScheduledItems) {
+      int* work = reinterpret_cast<int*>(base + wl.work);
+      prefill_schedule_kernel<<<1, 256, n * sizeof(int), st>>>(p->seq, p->seq_stride, p->batch, a.q_tiles, p->q_len,
+                                                               2 * QT, (int)span64, p->causal, a.tcount, work);
+      if (cudaGetLastError() != cudaSuccess) return RBLN_ERR_LAUNCH;
+      a.work = work;
+      a.counter = work + n;
     }
   }
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
-  const int rc = two_tile ? (mfk == 3 ? launch_tc3_any(Lc, st) : launch_tc2_any(Lc, st)) : launch_tc_any(Lc, st);
+  const int rc = kern == 3 ? launch_tc3_any(Lc, st) : kern == 2 ? launch_tc2_any(Lc, st) : launch_tc_any(Lc, st);
   if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
   return rc;
 }

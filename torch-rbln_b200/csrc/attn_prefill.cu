@@ -1613,23 +1613,54 @@ __device__ __forceinline__ bool keep_key(const AttnArgs& a, int b, int s, int t,
   return keep;
 }
 
-// grid (nkt, items), 8 warps: rows [s0, s0 + 2 QT) of item (b, query-tile
-// pair) x keys [128 kt, 128 kt + 128). A warp takes one (row, 32-key word)
-// at a time: lane l tests key 32 w + l (coalesced) and a ballot makes the
-// word. Class: 0 no key kept, 1 all kept, 2 mixed (over the chunk's rows).
+// 32 keep bits from 32 16-bit mask values (bf16 or f16 bit patterns, 4
+// x 16-byte words): value > 0 <=> sign clear, not zero, not NaN, i.e. the
+// pattern lies in [1, +inf].
+__device__ __forceinline__ uint32_t keep_bits16(const uint4* src, uint32_t inf_bits) {
+  uint32_t bits = 0;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const uint4 x = src[v];
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t h = (w[k >> 1] >> (16 * (k & 1))) & 0xffffu;
+      bits |= (uint32_t)(h - 1u < inf_bits) << (v * 8 + k);
+    }
+  }
+  return bits;
+}
+
+// grid (nkt, items), 256 threads: rows [s0, s0 + 2 QT) of item (b,
+// query-tile pair) x keys [128 kt, 128 kt + 128). A thread makes one
+// (row, 32-key word) at a time with all 32 tests independent, so its loads
+// are in flight together; a bf16 / f16 keep-mask whose row segment is
+// 16-byte aligned and inside the mask is read as four 16-byte words.
+// Class: 0 no key kept, 1 all kept, 2 mixed (over the chunk's rows).
 __global__ void __launch_bounds__(256) prefill_mask_bits_kernel(const AttnArgs a, uint4* kbits, uint8_t* cls) {
   const int kt = blockIdx.x, item = blockIdx.y;
   const int b = item / a.q_tiles, qp = item - b * a.q_tiles;
   const int s0 = qp * 2 * a.QT;
   const int rows = min(2 * a.QT, a.S_q - s0);
   const int seq_off = a.seq ? a.seq[b * a.seq_stride] : 0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool half_mask = a.mask_mode == MM_KEEP && !a.pmask && seq_off >= 0 &&
+                         (a.mask_dtype == RBLN_DT_BF16 || a.mask_dtype == RBLN_DT_F16);
+  const uint32_t inf_bits = a.mask_dtype == RBLN_DT_BF16 ? 0x7f80u : 0x7c00u;
   bool any_keep = false, any_drop = false;
-  for (int task = warp; task < rows * 4; task += 8) {
+  for (int task = threadIdx.x; task < rows * 4; task += blockDim.x) {
     const int i = task >> 2, w = task & 3;
     const int s = s0 + i;
-    const uint32_t bits = __ballot_sync(0xffffffffu, keep_key(a, b, s, kt * 128 + w * 32 + lane, seq_off));
-    if (lane == 0) reinterpret_cast<uint32_t*>(kbits + ((int64_t)b * a.S_q + s) * a.nkt + kt)[w] = bits;
+    const int t0 = kt * 128 + w * 32;
+    uint32_t bits = 0;
+    const int64_t e0 = b * a.m_b + (int64_t)s * a.m_s + t0;
+    const uint16_t* hp = static_cast<const uint16_t*>(a.mask) + e0;
+    if (half_mask && t0 + 32 <= min(a.mask_len, a.span) && (reinterpret_cast<uintptr_t>(hp) & 15u) == 0) {
+      bits = keep_bits16(reinterpret_cast<const uint4*>(hp), inf_bits);
+    } else {
+#pragma unroll 8
+      for (int e = 0; e < 32; ++e) bits |= (uint32_t)keep_key(a, b, s, t0 + e, seq_off) << e;
+    }
+    reinterpret_cast<uint32_t*>(kbits + ((int64_t)b * a.S_q + s) * a.nkt + kt)[w] = bits;
     any_keep |= bits != 0u;
     any_drop |= bits != 0xffffffffu;
   }

@@ -484,6 +484,29 @@ def decode_record(args, ctx: Ctx, wl_name: str, n_parity: int = 8, cpu_leg: bool
         ctx.barrier()
     ms_step = t0.elapsed_time(t1) / args.steps
 
+    # ---- head-sharded: the same local decode without the exchange (outputs in
+    # local memory only), timed the same way, to state what the exchange costs
+    local_ms = None
+    if peer is not None:
+        pl, keepl = cabi.paged_params(q, k, v, kc, vc, seq, bt, d["bs"], d["scale"])
+        cabi.attach_workspace(pl, dev, keepl)
+        pl.error_flags = err.data_ptr()
+        plref = ctypes.byref(pl)
+        for _ in range(args.warmup):
+            L.rbln_paged_causal_attn_decode(plref, sh)
+        torch.cuda.synchronize()
+        ctx.barrier()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for _ in range(args.steps):
+            if L.rbln_paged_causal_attn_decode(plref, sh) != 0:
+                raise RuntimeError("rbln_paged_causal_attn_decode failed")
+        l1.record(stream)
+        torch.cuda.synchronize()
+        ctx.barrier()
+        local_ms = l0.elapsed_time(l1) / args.steps
+        del keepl
+
     # ---- roofline: the main kernel alone, events the C-ABI records around it
     kev = _event_pairs(args.steps, stream)
     ctx.barrier()
@@ -562,6 +585,12 @@ def decode_record(args, ctx: Ctx, wl_name: str, n_parity: int = 8, cpu_leg: bool
         "clocks": clk.summary(),
         "parity": parity,
     }
+    if local_ms is not None:
+        local_ms = ctx.reduce([local_ms], "max")[0]
+        rec["exchange"] = {"local_decode_ms_per_step": round(local_ms, 4),
+                           "exchange_us_per_step": round((ms_step - local_ms) * 1e3, 2),
+                           "note": "the same rank's decode with outputs in local memory only, timed the same way; "
+                                   "the difference is what the peer stores and the epoch exchange cost per call"}
     if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:
         rec["cpu_baseline"] = cpu_decode_baseline(d, budget_s=args.cpu_budget)
     ctx.barrier()  # every rank is past its last call before any buffer is unmapped

@@ -110,3 +110,28 @@ def test_invalid_block_id_sets_the_flag():
     torch.cuda.synchronize()
     assert int(err.item()) & cabi.DEVERR_BLOCK_ID_RANGE
     assert torch.count_nonzero(kc) == 0
+
+
+@pytest.mark.parametrize("cache", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("bs,D", [(8, 128), (16, 128), (32, 64), (32, 128), (64, 64), (128, 128)])
+def test_block_sizes_both_kernels(cache, bs, D):
+    """Block sizes on both sides of the register kernel's limit (bs * D <=
+    2048 keeps a block's new rows in registers; larger blocks take the
+    two-pass kernel), with writes that start and end inside blocks, span
+    several blocks, and fill a block exactly: caches and scales bit-exact."""
+    B, Hkv, mb = 4, 2, 6
+    dt = torch.bfloat16
+    g, bt, kc0, vc0, ks0, vs0 = setup(B, Hkv, D, bs, mb, dt, cache, seed=bs * 1000 + D)
+    kc, vc = (kc0.to(DEV), kc0.clone()), (vc0.to(DEV), vc0.clone())
+    ks = None if ks0 is None else (ks0.to(DEV), ks0.clone())
+    vs = None if vs0 is None else (vs0.to(DEV), vs0.clone())
+    S = bs + bs // 2 + 3
+    starts = torch.tensor([0, bs // 2 + 1, bs, 2 * bs - 1], dtype=torch.int32)
+    k = (torch.randn([B, Hkv, 1, S, D], generator=g) * 3).to(dt)
+    v = (torch.randn([B, Hkv, 1, S, D], generator=g) * 0.25).to(dt)
+    write_both(k, v, kc, vc, starts, bt, bs, ks, vs)
+    assert_same(kc[0], kc[1], "k cache")
+    assert_same(vc[0], vc[1], "v cache")
+    if ks is not None:
+        assert_same(ks[0], ks[1], "k scales")
+        assert_same(vs[0], vs[1], "v scales")

@@ -665,13 +665,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanc
 }
 
 // Weighted sum of `nsplit` partials (index (base + s) * G + g) of sequence b,
-// KV head h into the output. `sw` holds nsplit*G + G floats.
+// KV head h into the output, for the query heads [g0, g0 + gn) of this CTA.
+// `sw` holds nsplit*G + G floats.
 template <int D, bool Q_BF16>
 __device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h, int64_t base, int nsplit,
-                                               float* sw) {
+                                               float* sw, int g0, int gn) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* s_inv = sw + nsplit * a.G;
-  for (int g = warp; g < a.G; g += kWarps) {
+  for (int g = g0 + warp; g < g0 + gn; g += kWarps) {
     float M = neg_inf();
     for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, a.part_lse[(base + s) * a.G + g]);
 #pragma unroll
@@ -690,14 +691,27 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h
     if (lane == 0) s_inv[g] = (M == neg_inf()) ? 0.f : 1.f / S;
   }
   __syncthreads();
-  for (int idx = tid; idx < a.G * (D / 4); idx += kThreads) {
-    const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+  for (int idx = tid; idx < gn * (D / 4); idx += kThreads) {
+    const int g = g0 + idx / (D / 4), d4 = (idx % (D / 4)) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = sw[s * a.G + g];
-      if (w != 0.f) {
-        const float4 o = *reinterpret_cast<const float4*>(a.part_o + ((base + s) * a.G + g) * D + d4);
-        acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
+    // eight partials at a time, their loads issued together (a sequence
+    // split over many chunks would otherwise pay one L2 round trip per
+    // partial); summed in the same order as one at a time
+    const float* po = a.part_o + (base * a.G + g) * D + d4;
+    const int64_t ps = (int64_t)a.G * D;  // floats from one partial slot to the next
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {
+      float w[8];
+      float4 o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) w[u] = s0 + u < nsplit ? sw[(s0 + u) * a.G + g] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        o[u] = w[u] != 0.f ? *reinterpret_cast<const float4*>(po + (s0 + u) * ps) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (w[u] != 0.f) {
+          acc.x += w[u] * o[u].x; acc.y += w[u] * o[u].y; acc.z += w[u] * o[u].z; acc.w += w[u] * o[u].w;
+        }
       }
     }
     float inv = s_inv[g];
@@ -710,19 +724,27 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h
   // through its arrival chain
 }
 
+// The merge kernels are programmatic dependents of the decode kernel: they
+// wait for it at their start, and let the next launch on the stream be
+// scheduled only at the end of their work. Measured on B200: signalling at
+// the start let the next decode grid's CTAs wait resident beside a small
+// merge grid (32 CTAs of 18 us for 32 sequences x 1 KV head) and slowed the
+// call from 101 us to 141 us.
+__device__ __forceinline__ void merge_done() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Combines the per-split partials of one (sequence, KV head) of the
-// per-sequence split kernel.
+// per-sequence split kernel; blockIdx.z takes a slice of the query heads.
 template <int D, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const DecodeArgs a) {
-  // launched as a programmatic dependent of the split kernel: wait here until
-  // that grid has completed and its writes are visible
-  pdl_enter();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = blockIdx.x, b = blockIdx.y;
+  const int gn = a.G / (int)gridDim.z, g0 = (int)blockIdx.z * gn;
   int pos, L, nsplit;
   decode_extent(a, b, pos, L, nsplit);
   if (nsplit <= 1) return;
   extern __shared__ float sw[];
-  merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, sw);
+  merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, sw, g0, gn);
+  merge_done();
 }
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -761,15 +783,16 @@ __device__ __forceinline__ void peer_epoch_exchange(uint32_t* const* flags, int 
 // exchange, so the call needs no separate barrier launch.
 template <int D, int KV, bool Q_BF16>
 __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(const DecodeArgs a) {
-  pdl_enter();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = blockIdx.x, b = blockIdx.y;
+  const int gn = a.G / (int)gridDim.z, g0 = (int)blockIdx.z * gn;  // this CTA's query heads
   int pos;
   const int L = seq_len(a, b, pos);
-  if (pos < 0 && h == 0 && threadIdx.x == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
+  if (pos < 0 && h == 0 && blockIdx.z == 0 && threadIdx.x == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
   if (L == 0) {
-    if (a.k_new != nullptr && pos >= 0 && pos < a.span) append_token<D, KV, Q_BF16>(a, b, h, pos);
-    for (int idx = threadIdx.x; idx < a.G * (D / 4); idx += kThreads) {
-      const int g = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+    if (a.k_new != nullptr && pos >= 0 && pos < a.span && blockIdx.z == 0) append_token<D, KV, Q_BF16>(a, b, h, pos);
+    for (int idx = threadIdx.x; idx < gn * (D / 4); idx += kThreads) {
+      const int g = g0 + idx / (D / 4), d4 = (idx % (D / 4)) * 4;
       const float n = a.sinks ? 0.f : pos_nan();  // all softmax mass on the sink
       store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n)));
     }
@@ -779,9 +802,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
     // cf == cl: one chunk held the whole sequence and wrote the output
     if (cf != cl) {
       extern __shared__ float sw[];
-      merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw);
+      merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw, g0, gn);
     }
   }
+  merge_done();
   if (a.peer_flags == nullptr) return;
   // Ordering of the peer stores before the epoch release: the CTA's stores
   // reach thread 0 through the barrier, its GPU-scope fence orders them
@@ -795,7 +819,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    last = atomicAdd(a.merge_ctr, 1) == (int)(gridDim.x * gridDim.y) - 1;
+    last = atomicAdd(a.merge_ctr, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1;
     __threadfence();
   }
   __syncthreads();
@@ -959,8 +983,19 @@ int launch_dependent(void (*kernel)(DecodeArgs), dim3 grid, size_t smem, cudaStr
   return cudaLaunchKernelEx(&cfg, kernel, a) == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
+// Slices of the query heads per merge CTA: (KV head, sequence) pairs are
+// split over heads (halving while G allows) until the merge grid has about
+// two CTAs per SM. At 32 sequences x 1 KV head (a long-context decode
+// sharded over 8 GPUs) that is 8 CTAs per pair; at 64 x 8 pairs, none.
+int merge_head_split(int Hkv, int B, int G) {
+  int gz = 1;
+  while (G % (2 * gz) == 0 && (int64_t)Hkv * B * gz < 2 * 148) gz *= 2;
+  return gz;
+}
+
 template <int D, int KV, bool QB, int NT, bool LA>
 int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* const* ev) {
+  const int gz = merge_head_split(a.Hkv, a.B, a.G);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
   if (pl.balanced) {
     const size_t smem = segment_smem<D, NT>() + (size_t)(a.B + 1) * sizeof(int);
@@ -976,7 +1011,8 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
     static SmemOptIn mdone;
     if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_balanced_kernel<D, KV, QB>), (int)msmem, mdone))
       return RBLN_ERR_LAUNCH;
-    const int rc = launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B), msmem, st, a);
+    const int rc =
+        launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B, gz), msmem, st, a);
     if (rc != RBLN_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
   }
@@ -993,7 +1029,7 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
     static SmemOptIn mdone;
     if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_kernel<D, QB>), (int)smem, mdone))
       return RBLN_ERR_LAUNCH;
-    const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B), smem, st, a);
+    const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B, gz), smem, st, a);
     if (rc != RBLN_OK) return rc;
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;

@@ -197,7 +197,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   auto bar = [&](int i) { return sbase + Lay::BAR + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // one-dimensional grid, key tile major: under a causal mask the first key
+  // tiles see the most query tiles, so the longest CTAs launch first
+  const int hb = (int)(blockIdx.x % (unsigned)(a.Hkv * a.B));
+  const int kt = (int)(blockIdx.x / (unsigned)(a.Hkv * a.B)), h = hb % a.Hkv, b = hb / a.Hkv;
   const int t0 = kt * BT;
   const int nq = (a.L + BT - 1) / BT;
   // top-left causal: query l sees key t only when t <= l, so tiles before
@@ -494,7 +497,39 @@ struct QLayout {
   static constexpr int ALLOC = (TOTAL + 1024 > 120 * 1024) ? TOTAL + 1024 : 120 * 1024;
 };
 
-enum QBar { QB_Q = 0, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SFA, QB_SFB, QB_PFA, QB_PFB, QB_DONE, QB_COUNT };
+// Persistent: one CTA per SM walks the units (query tile, query head, batch)
+// in longest-first order (the last query tiles see the most keys under a
+// causal mask), dealt to the CTAs in snake order so that every CTA gets a
+// near-equal share of key tiles. The K/V ring, the S/dP halves and their
+// barriers follow a running count of the CTA's key tiles, so the pipeline
+// runs on across units; Q and dO of the next unit are loaded as soon as the
+// last S/dP MMAs of the current one have completed (QB_QE). dQ is
+// accumulated in two TMEM buffers used by alternate units, so the compute
+// warps store one unit's dQ while the tensor cores start the next unit; a
+// buffer is reused two units later, after its store (QB_DQE).
+enum QBar {
+  QB_Q = 0, QB_QE, QB_KF0, QB_KF1, QB_KE0, QB_KE1, QB_SFA, QB_SFB, QB_PFA, QB_PFB,
+  QB_DQF0, QB_DQF1, QB_DQE0, QB_DQE1, QB_DONE, QB_COUNT
+};
+
+// Unit k of this CTA: false when the CTA has no k-th unit.
+__device__ __forceinline__ bool q_unit(const BwdArgs& a, int nqt, int k, int& qt, int& hq, int& b) {
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  const int64_t idx = (int64_t)k * G + ((k & 1) ? G - 1 - c : c);
+  const int64_t per = (int64_t)a.H * a.B;
+  if (idx >= (int64_t)nqt * per) return false;
+  qt = nqt - 1 - (int)(idx / per);
+  const int rem = (int)(idx % per);
+  hq = rem % a.H;
+  b = rem / a.H;
+  return true;
+}
+
+// Key tiles unit (qt) attends: all of them, or those up to the diagonal.
+__device__ __forceinline__ int q_unit_tiles(const BwdArgs& a, int qt) {
+  const int nk_all = (a.S + BT - 1) / BT;
+  return a.causal ? min(nk_all, qt + 1) : nk_all;
+}
 
 template <int D, bool BF16, bool MASK>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -511,17 +546,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   auto bar = [&](int i) { return sbase + Lay::BAR + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the last query tiles see the most keys under a causal mask: launch them first
-  const int qt = gridDim.x - 1 - blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
-  const int h = hq / a.G;
-  const int l0 = qt * BT;
-  const int nk_all = (a.S + BT - 1) / BT;
-  const int nk = a.causal ? min(nk_all, (l0 + BT - 1) / BT + 1) : nk_all;
+  const int nqt = (a.L + BT - 1) / BT;
 
   if (threadIdx.x == 0) {
     *abort = 0;
     for (int i = 0; i < QB_COUNT; ++i)
-      mbar_init(bar(i), (i == QB_PFA || i == QB_PFB) ? (uint32_t)(kComputeWarps / 2) : 1u);
+      mbar_init(bar(i), (i == QB_PFA || i == QB_PFB) ? (uint32_t)(kComputeWarps / 2)
+                        : (i == QB_DQE0 || i == QB_DQE1) ? (uint32_t)kComputeWarps
+                                                         : 1u);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -532,34 +564,58 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
+  const uint32_t t_s = tmem, t_dp = tmem + 128;
+  auto t_dq = [&](int x) { return tmem + 256 + x * D; };
 
   if (warp == 0) {
-    if (lane == 0 && nk > 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       prefetch_tmap(&tm_do);
-      mbar_arrive_expect_tx(bar(QB_Q), 2 * NP * kPanel);
-      for (int p = 0; p < NP; ++p) {
-        tma_load_4d(sbase + Lay::Q + p * kPanel, &tm_q, bar(QB_Q), p * 64, l0, hq, b);
-        tma_load_4d(sbase + Lay::DO + p * kPanel, &tm_do, bar(QB_Q), p * 64, l0, hq, b);
-      }
-      int issued = 0;
-      for (int j = 0; j < nk; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(bar(QB_KE0 + st), ((j >> 1) - 1) & 1, abort)) break;
-        mbar_arrive_expect_tx(bar(QB_KF0 + st), 2 * NP * kPanel);
-        for (int p = 0; p < NP; ++p) {
-          tma_load_4d(sbase + Lay::K0 + (st * NP + p) * kPanel, &tm_k, bar(QB_KF0 + st), p * 64, j * BT, h, b);
-          tma_load_4d(sbase + Lay::V0 + (st * NP + p) * kPanel, &tm_v, bar(QB_KF0 + st), p * 64, j * BT, h, b);
+      int T = 0, uc = 0, issued = 0, q_issued = 0;
+      bool ok = true;
+      int qt, hq, b;
+      for (int k = 0; ok && q_unit(a, nqt, k, qt, hq, b); ++k) {
+        const int nk = q_unit_tiles(a, qt), h = hq / a.G;
+        if (nk == 0) continue;
+        for (int j = 0; j < nk; ++j) {
+          const int Tj = T + j, st = Tj & 1;
+          if (Tj >= 2 && !mbar_wait(bar(QB_KE0 + st), ((Tj >> 1) - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar(QB_KF0 + st), 2 * NP * kPanel);
+          for (int p = 0; p < NP; ++p) {
+            tma_load_4d(sbase + Lay::K0 + (st * NP + p) * kPanel, &tm_k, bar(QB_KF0 + st), p * 64, j * BT, h, b);
+            tma_load_4d(sbase + Lay::V0 + (st * NP + p) * kPanel, &tm_v, bar(QB_KF0 + st), p * 64, j * BT, h, b);
+          }
+          issued = Tj + 1;
+          if (j == 0) {
+            // Q and dO of this unit once the previous unit's last S / dP MMAs
+            // are done (its first K/V tile went out before that wait)
+            if (uc >= 1 && !mbar_wait(bar(QB_QE), (uc - 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(bar(QB_Q), 2 * NP * kPanel);
+            for (int p = 0; p < NP; ++p) {
+              tma_load_4d(sbase + Lay::Q + p * kPanel, &tm_q, bar(QB_Q), p * 64, qt * BT, hq, b);
+              tma_load_4d(sbase + Lay::DO + p * kPanel, &tm_do, bar(QB_Q), p * 64, qt * BT, hq, b);
+            }
+            q_issued = uc + 1;
+          }
         }
-        issued = j + 1;
+        T += nk;
+        ++uc;
       }
       if (*abort) {
+        // let the copies in flight land before the CTA exits
         const long long c0 = clock64();
-        while (!mbar_try_wait(bar(QB_Q), 0) && clock64() - c0 < 2000000) {
-        }
+        if (q_issued > 0)
+          while (!mbar_try_wait(bar(QB_Q), (q_issued - 1) & 1) && clock64() - c0 < 2000000) {
+          }
         for (int j = max(0, issued - 2); j < issued; ++j) {
           const long long c1 = clock64();
           while (!mbar_try_wait(bar(QB_KF0 + (j & 1)), (j >> 1) & 1) && clock64() - c1 < 2000000) {
@@ -568,11 +624,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && nk > 0) {
+    // ------------------------------------------------------------- MMA
+    if (lane == 0) {
       const uint32_t id_s = idesc_f16(BF16, BT, BT / 2, false);  // S, dP halves (64 keys each)
       const uint32_t id_dq = idesc_f16(BF16, BT, D, true);       // B (K) MN-major
-      auto issue_s = [&](int j, int hh) {  // S, dP of keys [64 hh, 64 hh + 64) of tile j
-        const int st = j & 1;
+      auto issue_s = [&](int Tj, int hh) {  // S, dP of keys [64 hh, 64 hh + 64) of ring tile Tj
+        const int st = Tj & 1;
         const uint32_t kb = sbase + Lay::K0 + st * NP * kPanel + hh * 8192;
         const uint32_t vb = sbase + Lay::V0 + st * NP * kPanel + hh * 8192;
 #pragma unroll
@@ -589,47 +646,66 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         umma_commit(bar(QB_SFA + hh));
       };
-      auto issue_dq = [&](int j, int hh) {  // dQ += dS K over half hh's 64 keys
-        const uint32_t kb = sbase + Lay::K0 + (j & 1) * NP * kPanel;
+      auto issue_dq = [&](int Tj, int j, int hh, int x) {  // dQ_x += dS K over half hh's 64 keys
+        const uint32_t kb = sbase + Lay::K0 + (Tj & 1) * NP * kPanel;
 #pragma unroll
         for (int k4 = 0; k4 < BT / 32; ++k4) {
           const int kk = hh * (BT / 32) + k4;
-          umma_f16_ts(t_dq, t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
+          umma_f16_ts(t_dq(x), t_s + kPackOff + kk * 8, sw128_desc(kb + kk * 16 * 128, kPanel, 1024), id_dq,
                       (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
-      // the same two-half software pipeline as the dK/dV kernel
-      bool ok = mbar_wait(bar(QB_Q), 0, abort) && mbar_wait(bar(QB_KF0), 0, abort);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(0, 1);
-      }
-      for (int j = 0; ok && j < nk; ++j) {
-        const int st = j & 1;
-        const bool more = j + 1 < nk;
-        if (!mbar_wait(bar(QB_PFA), j & 1, abort)) {
+      int T = 0, uc = 0;
+      bool ok = true;
+      int qt, hq, b;
+      for (int k = 0; ok && q_unit(a, nqt, k, qt, hq, b); ++k) {
+        const int nk = q_unit_tiles(a, qt);
+        if (nk == 0) continue;
+        const int x = uc & 1;
+        // dQ buffer x: its store two units ago has completed; Q / dO loaded;
+        // the first key tile landed
+        if ((uc >= 2 && !mbar_wait(bar(QB_DQE0 + x), ((uc >> 1) - 1) & 1, abort)) ||
+            !mbar_wait(bar(QB_Q), uc & 1, abort) || !mbar_wait(bar(QB_KF0 + (T & 1)), (T >> 1) & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        issue_dq(j, 0);
-        if (more) {
-          if (!mbar_wait(bar(QB_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort)) {
+        issue_s(T, 0);
+        issue_s(T, 1);
+        // the same two-half software pipeline as the dK/dV kernel
+        for (int j = 0; j < nk; ++j) {
+          const int Tj = T + j;
+          const bool more = j + 1 < nk;
+          if (!mbar_wait(bar(QB_PFA), Tj & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_s(j + 1, 0);
+          issue_dq(Tj, j, 0, x);
+          if (more) {
+            if (!mbar_wait(bar(QB_KF0 + ((Tj + 1) & 1)), ((Tj + 1) >> 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(Tj + 1, 0);
+          }
+          if (!mbar_wait(bar(QB_PFB), Tj & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_dq(Tj, j, 1, x);
+          umma_commit(bar(QB_KE0 + (Tj & 1)));
+          if (more) {
+            issue_s(Tj + 1, 1);
+          } else {
+            umma_commit(bar(QB_QE));        // every S / dP of the unit done: Q and dO may be reloaded
+            umma_commit(bar(QB_DQF0 + x));  // the unit's dQ is complete
+          }
         }
-        if (!mbar_wait(bar(QB_PFB), j & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_dq(j, 1);
-        umma_commit(bar(QB_KE0 + st));
-        if (more) issue_s(j + 1, 1);
+        T += nk;
+        ++uc;
       }
       umma_commit(bar(QB_DONE));
       if (!ok) {
@@ -639,98 +715,111 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
+    // --------------------------------------------------------- compute
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // query row == TMEM lane
-    const int l = l0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const float2 rw = a.rows[((int64_t)b * a.H + hq) * a.Lp + l];  // padding rows: {+inf, 0}
-    const int64_t mrow = MASK ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h + (int64_t)min(l, a.L - 1) * a.m_l : 0;
+    int T = 0, uc = 0;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      const int kt0 = j * BT;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SFA + half), j & 1, abort))) {
+    int qt, hq, b;
+    for (int k = 0; ok && q_unit(a, nqt, k, qt, hq, b); ++k) {
+      const int nk = q_unit_tiles(a, qt);
+      if (nk == 0) continue;
+      const int l = qt * BT + r;
+      const float2 rw = a.rows[((int64_t)b * a.H + hq) * a.Lp + l];  // padding rows: {+inf, 0}
+      const int64_t mrow = MASK ? (int64_t)b * a.m_b + (int64_t)hq * a.m_h + (int64_t)min(l, a.L - 1) * a.m_l : 0;
+      for (int j = 0; j < nk; ++j) {
+        const int Tj = T + j;
+        const int kt0 = j * BT;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_SFA + half), Tj & 1, abort))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c4 = half == 0 ? 1 - cc : 2 + cc;
+          uint32_t sv[32], dv[32];
+          __syncwarp();
+          tmem_ld32(t_s + lane_off + c4 * 32, sv);
+          tmem_ld32(t_dp + lane_off + c4 * 32, dv);
+          tmem_wait_ld();
+          const int ta = kt0 + c4 * 32;
+          // 0: nothing visible, 1: every key (rows past L have lse +inf), 2: per key
+          const int cls = (ta >= a.S || (a.causal && ta > l)) ? 0
+                          : ((!a.causal || ta + 31 <= l) && ta + 31 < a.S) ? 1 : 2;
+          uint32_t dk[16];
+          if (cls == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) dk[e] = 0u;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float dd[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int t = ta + 2 * e + u;
+                float xs = fmaf(__uint_as_float(sv[2 * e + u]), a.qk_mult, -rw.x);
+                bool keep = cls == 1 || (t < a.S && (!a.causal || t <= l));
+                if (MASK) {
+                  if (keep && l < a.L) {
+                    const float mv = bias_value(a.mask, a.mask_dtype, mrow + t);
+                    if (a.mask_additive) {
+                      xs = fmaf(mv, kLog2e, xs);
+                    } else {
+                      keep = mv > 0.f;
+                    }
+                  }
+                }
+                const float p = keep ? exp2_approx(xs) : 0.f;
+                dd[u] = keep ? p * (__uint_as_float(dv[2 * e + u]) - rw.y) : 0.f;
+              }
+              dk[e] = pack2<BF16>(dd[0], dd[1]);
+            }
+          }
+          tmem_st16(t_s + lane_off + kPackOff + c4 * 16, dk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(QB_PFA + half));
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      // this unit's dQ: wait for its last MMA, store it, release the buffer
+      const int x = uc & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_DQF0 + x), (uc >> 1) & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (a.dq) {
+        char* qrow = a.dq + b * a.dq_b + hq * a.dq_h + (int64_t)l * a.dq_l;
 #pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c4 = half == 0 ? 1 - cc : 2 + cc;
-        uint32_t sv[32], dv[32];
-        __syncwarp();
-        tmem_ld32(t_s + lane_off + c4 * 32, sv);
-        tmem_ld32(t_dp + lane_off + c4 * 32, dv);
-        tmem_wait_ld();
-        const int ta = kt0 + c4 * 32;
-        // 0: nothing visible, 1: every key (rows past L have lse +inf), 2: per key
-        const int cls = (ta >= a.S || (a.causal && ta > l)) ? 0
-                        : ((!a.causal || ta + 31 <= l) && ta + 31 < a.S) ? 1 : 2;
-        uint32_t dk[16];
-        if (cls == 0) {
+        for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
+          uint32_t ov[32];
+          __syncwarp();
+          tmem_ld32(t_dq(x) + lane_off + c * 32, ov);
+          tmem_wait_ld();
+          if (l < a.L) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) dk[e] = 0u;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float dd[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int t = ta + 2 * e + u;
-              float x = fmaf(__uint_as_float(sv[2 * e + u]), a.qk_mult, -rw.x);
-              bool keep = cls == 1 || (t < a.S && (!a.causal || t <= l));
-              if (MASK) {
-                if (keep && l < a.L) {
-                  const float mv = bias_value(a.mask, a.mask_dtype, mrow + t);
-                  if (a.mask_additive) {
-                    x = fmaf(mv, kLog2e, x);
-                  } else {
-                    keep = mv > 0.f;
-                  }
-                }
-              }
-              const float p = keep ? exp2_approx(x) : 0.f;
-              dd[u] = keep ? p * (__uint_as_float(dv[2 * e + u]) - rw.y) : 0.f;
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint4 w;
+              w.x = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 0]) * a.scale, __uint_as_float(ov[q4 * 8 + 1]) * a.scale);
+              w.y = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 2]) * a.scale, __uint_as_float(ov[q4 * 8 + 3]) * a.scale);
+              w.z = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 4]) * a.scale, __uint_as_float(ov[q4 * 8 + 5]) * a.scale);
+              w.w = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 6]) * a.scale, __uint_as_float(ov[q4 * 8 + 7]) * a.scale);
+              *reinterpret_cast<uint4*>(qrow + (c * 32 + q4 * 8) * 2) = w;
             }
-            dk[e] = pack2<BF16>(dd[0], dd[1]);
           }
         }
-        tmem_st16(t_s + lane_off + kPackOff + c4 * 16, dk);
       }
-      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(QB_PFA + half));
-    }
-
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(QB_DONE), 0, abort));
-    tc_fence_after();
-    if (ok && a.dq) {
-      char* qrow = a.dq + b * a.dq_b + hq * a.dq_h + (int64_t)l * a.dq_l;
-#pragma unroll 1
-      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
-        uint32_t ov[32];
-        if (nk > 0) {
-          __syncwarp();
-          tmem_ld32(t_dq + lane_off + c * 32, ov);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = 0u;
-        }
-        if (l < a.L) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 w;
-            w.x = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 0]) * a.scale, __uint_as_float(ov[q4 * 8 + 1]) * a.scale);
-            w.y = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 2]) * a.scale, __uint_as_float(ov[q4 * 8 + 3]) * a.scale);
-            w.z = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 4]) * a.scale, __uint_as_float(ov[q4 * 8 + 5]) * a.scale);
-            w.w = pack2<BF16>(__uint_as_float(ov[q4 * 8 + 6]) * a.scale, __uint_as_float(ov[q4 * 8 + 7]) * a.scale);
-            *reinterpret_cast<uint4*>(qrow + (c * 32 + q4 * 8) * 2) = w;
-          }
-        }
-      }
+      if (lane == 0) mbar_arrive(bar(QB_DQE0 + x));
+      T += nk;
+      ++uc;
     }
   }
 
@@ -762,8 +851,9 @@ int launch_kv(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   constexpr int sm = KvLayout<D>::ALLOC;
   auto* k = sdpa_bwd_kv_kernel<D, BF16, MASK, DBIAS>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
-  dim3 grid((a.S + BT - 1) / BT, a.Hkv, a.B);
-  k<<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
+  const int64_t n = (int64_t)((a.S + BT - 1) / BT) * a.Hkv * a.B;
+  if (n > 2147483647LL) return RBLN_ERR_UNSUPPORTED;
+  k<<<(unsigned)n, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }
 
@@ -772,7 +862,16 @@ int launch_q(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   constexpr int sm = QLayout<D>::ALLOC;
   auto* k = sdpa_bwd_q_kernel<D, BF16, MASK>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
-  dim3 grid((a.L + BT - 1) / BT, a.H, a.B);
+  // persistent: one CTA per SM (at most one per unit)
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      sms = n;
+    if (sms <= 0) sms = 148;
+  }
+  const int64_t units = (int64_t)((a.L + BT - 1) / BT) * a.H * a.B;
+  const int grid = (int)std::min<int64_t>(units, sms);
   k<<<grid, kBwdThreads, sm, st>>>(m.q, m.k, m.v, m.dout, a);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }

@@ -375,14 +375,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       const float2* ri = reinterpret_cast<const float2*>(sgen + Lay::RI0 + st * BT * 8);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c4 = half == 0 ? 1 - cc : 2 + cc;
-        uint32_t sv[32], dv[32];
-        __syncwarp();
-        tmem_ld32(t_s + lane_off + c4 * 32, sv);
-        tmem_ld32(t_dp + lane_off + c4 * 32, dv);
-        tmem_wait_ld();
+      // both of this warp's 32-column chunks of S^T and dP^T come in one TMEM
+      // round trip (half 0: chunks 1 then 0; half 1: chunks 2 then 3), so
+      // every packed store below lands on columns already read
+      const int c4a = half == 0 ? 1 : 2, c4b = half == 0 ? 0 : 3;
+      uint32_t sva[32], dva[32], svb[32], dvb[32];
+      __syncwarp();
+      tmem_ld32(t_s + lane_off + c4a * 32, sva);
+      tmem_ld32(t_dp + lane_off + c4a * 32, dva);
+      tmem_ld32(t_s + lane_off + c4b * 32, svb);
+      tmem_ld32(t_dp + lane_off + c4b * 32, dvb);
+      tmem_wait_ld();
+      auto chunk = [&](int c4, const uint32_t(&sv)[32], const uint32_t(&dv)[32]) {
         const int la = l0 + c4 * 32;
         // 0: nothing visible, 1: everything (but padding rows, whose lse is
         // +inf), 2: the causal diagonal crosses the chunk
@@ -391,6 +395,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (cls == 0) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) pk[e] = dk[e] = 0u;
+        } else if (!MASK && !DBIAS && cls == 1) {  // every query row sees this key: no per-element test
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float2 r0 = ri[c4 * 32 + 2 * e], r1 = ri[c4 * 32 + 2 * e + 1];  // shared-memory broadcasts
+            const float p0 = exp2_approx(fmaf(__uint_as_float(sv[2 * e]), a.qk_mult, -r0.x));
+            const float p1 = exp2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), a.qk_mult, -r1.x));
+            pk[e] = pack2<BF16>(p0, p1);
+            dk[e] = pack2<BF16>(p0 * (__uint_as_float(dv[2 * e]) - r0.y), p1 * (__uint_as_float(dv[2 * e + 1]) - r1.y));
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -424,7 +437,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tmem_st16(t_s + lane_off + kPackOff + c4 * 16, pk);
         tmem_st16(t_dp + lane_off + kPackOff + c4 * 16, dk);
-      }
+      };
+      chunk(c4a, sva, dva);
+      chunk(c4b, svb, dvb);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -737,14 +752,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c4 = half == 0 ? 1 - cc : 2 + cc;
-          uint32_t sv[32], dv[32];
-          __syncwarp();
-          tmem_ld32(t_s + lane_off + c4 * 32, sv);
-          tmem_ld32(t_dp + lane_off + c4 * 32, dv);
-          tmem_wait_ld();
+        // both of this warp's 32-column chunks of S and dP come in one TMEM
+        // round trip (half 0: chunks 1 then 0; half 1: chunks 2 then 3), so
+        // every packed store below lands on columns already read
+        const int c4a = half == 0 ? 1 : 2, c4b = half == 0 ? 0 : 3;
+        uint32_t sva[32], dva[32], svb[32], dvb[32];
+        __syncwarp();
+        tmem_ld32(t_s + lane_off + c4a * 32, sva);
+        tmem_ld32(t_dp + lane_off + c4a * 32, dva);
+        tmem_ld32(t_s + lane_off + c4b * 32, svb);
+        tmem_ld32(t_dp + lane_off + c4b * 32, dvb);
+        tmem_wait_ld();
+        auto chunk = [&](int c4, const uint32_t(&sv)[32], const uint32_t(&dv)[32]) {
           const int ta = kt0 + c4 * 32;
           // 0: nothing visible, 1: every key (rows past L have lse +inf), 2: per key
           const int cls = (ta >= a.S || (a.causal && ta > l)) ? 0
@@ -753,6 +772,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (cls == 0) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) dk[e] = 0u;
+          } else if (!MASK && cls == 1) {  // every key visible: no per-key test
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = exp2_approx(fmaf(__uint_as_float(sv[2 * e]), a.qk_mult, -rw.x));
+              const float p1 = exp2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), a.qk_mult, -rw.x));
+              dk[e] = pack2<BF16>(p0 * (__uint_as_float(dv[2 * e]) - rw.y), p1 * (__uint_as_float(dv[2 * e + 1]) - rw.y));
+            }
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
@@ -779,7 +805,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
           tmem_st16(t_s + lane_off + kPackOff + c4 * 16, dk);
-        }
+        };
+        chunk(c4a, sva, dva);
+        chunk(c4b, svb, dvb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();

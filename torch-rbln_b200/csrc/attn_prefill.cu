@@ -527,60 +527,6 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
-// Packed fp32 pairs (sm_100a f32x2 instructions): one issue slot for two
-// values.
-__device__ __forceinline__ void fma2(float& a, float& b, float m0, float m1, float c0, float c1) {
-  asm("{\n\t.reg .b64 ra, rm, rc;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rm, {%2, %3};\n\t"
-      "mov.b64 rc, {%4, %5};\n\tfma.rn.f32x2 ra, ra, rm, rc;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a), "+f"(b)
-      : "f"(m0), "f"(m1), "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void add2(float& a, float& b, float c0, float c1) {
-  asm("{\n\t.reg .b64 ra, rc;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rc, {%2, %3};\n\t"
-      "add.rn.f32x2 ra, ra, rc;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a), "+f"(b)
-      : "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void mul2(float& a, float& b, float m0, float m1) {
-  asm("{\n\t.reg .b64 ra, rm;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rm, {%2, %3};\n\t"
-      "mul.rn.f32x2 ra, ra, rm;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a), "+f"(b)
-      : "f"(m0), "f"(m1));
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// 2^x for a pair of x <= 8 on the FMA pipe (no SFU or conversion-unit
-// instruction): x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the
-// rounding happens in the add), f in [-0.5, 0.5]; 2^f by a cubic with
-// minimax relative error 7.5e-5 (2^-13.7) on that interval; 2^n built as the
-// float with exponent field n + 127 by an integer multiply-add on the bits of
-// the shifted value. x is clamped to -127 first, where the scale is exactly
-// 0, so masked scores (-inf) give exactly 0.
-__device__ __forceinline__ void exp2_poly2(float& x0, float& x1) {
-  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
-  x0 = fmaxf(x0, -127.f);
-  x1 = fmaxf(x1, -127.f);
-  float t0 = x0, t1 = x1;
-  add2(t0, t1, kRound, kRound);
-  float f0 = t0, f1 = t1;
-  add2(f0, f1, -kRound, -kRound);        // round(x)
-  fma2(f0, f1, -1.f, -1.f, x0, x1);      // f = x - round(x)
-  float p0 = 0.05517132207751274f, p1 = 0.05517132207751274f;
-  fma2(p0, p1, f0, f1, 0.24261054396629333f, 0.24261054396629333f);
-  fma2(p0, p1, f0, f1, 0.6932609677314758f, 0.6932609677314758f);
-  fma2(p0, p1, f0, f1, 0.9999281167984009f, 0.9999281167984009f);
-  // bits(t) = 0x4B400000 + n, and 0x4B400000 * 2^23 = 0 (mod 2^32)
-  const float s0 = __uint_as_float(__float_as_uint(t0) * 0x800000u + 0x3F800000u);
-  const float s1 = __uint_as_float(__float_as_uint(t1) * 0x800000u + 0x3F800000u);
-  mul2(p0, p1, s0, s1);
-  x0 = p0;
-  x1 = p1;
-}
-
 template <int D>
 struct SmemLayout2 {
   static constexpr int NP = D / 64;

@@ -33,17 +33,23 @@
 //                         read those as the A operand straight from TMEM.
 //                         Each tile is handled in two halves of 64 query rows
 //                         with their own barriers, pipelined across tiles.
-//   sdpa_bwd_q_kernel     one CTA per (128-query tile, query head, batch): Q and
-//                         dO stay, K and V tiles stream; S = Q K^T, dP = dO V^T,
-//                         dS over S's buffer, dQ += dS K (two halves of 64 keys,
-//                         pipelined the same way).
+//                         The grid is 1-D, key tile major: under a causal
+//                         mask the first key tiles see the most query tiles,
+//                         so the longest CTAs launch first.
+//   sdpa_bwd_q_kernel     persistent, one CTA per SM walking the units (128-query
+//                         tile, query head, batch): per unit Q and dO stay, K
+//                         and V tiles stream; S = Q K^T, dP = dO V^T, dS over
+//                         S's buffer, dQ += dS K (two halves of 64 keys,
+//                         pipelined the same way, and on across units).
 // No atomics: every output element has one writer.
 //
-// Warp roles in both tile kernels (320 threads): warp 0 issues the TMA copies
+// Warp roles in both tile kernels (384 threads): warp 0 issues the TMA copies
 // (one thread; in the dK/dV kernel also a bulk copy of the tile's 128 row
 // pairs into shared memory), warp 1 owns TMEM and issues the MMAs (one
-// thread), warps 2-9 compute: thread = TMEM lane, the two warps of a lane
-// quadrant each take 64 of the tile's 128 columns. The mask, the dbias store
+// thread), warps 2-3 idle, warps 4-11 compute: thread = TMEM lane, the two
+// warps of a lane quadrant each take 64 of the tile's 128 columns. The
+// compute warpgroups take 192 registers per thread, the first one 112 (the
+// largest compute share with no spills in either). The mask, the dbias store
 // and the causal test are compile-time or per-32-column-chunk decisions, so
 // an unmasked chunk costs one FMA, one exp2, two FP ops and a pack per
 // element. Every mbarrier wait is bounded (sm100.cuh);
@@ -178,9 +184,23 @@ __device__ __forceinline__ void kv_tile(int i, int per_g, int qt0, int& g, int& 
 // warps of a lane quadrant never touch each other's columns.
 constexpr int kPackOff = 32;
 
-// 8 compute warps (2..9): lane quadrant warp % 4, column half (warp - 2) / 4.
-constexpr int kBwdThreads = 320;
+// 12 warps: producer 0, MMA 1, 2-3 idle, and 8 compute warps (4..11) with
+// lane quadrant warp % 4 and column half (warp - 4) / 4. The first warpgroup
+// gives registers up (setmaxnreg) so that a compute thread holds both of its
+// chunks of S and dP without spilling (168 per thread at launch).
+constexpr int kBwdThreads = 384;
 constexpr int kComputeWarps = 8;
+constexpr uint32_t kRegsCompute = 192, kRegsCtl = 112;
+static_assert(2 * 128 * kRegsCompute + 128 * kRegsCtl <= kBwdThreads * 168, "register split exceeds the launch");
+
+// The split needs the 168 registers per thread at launch: with fewer, a
+// warpgroup raising its count would never be served.
+template <typename K>
+bool bwd_regs_ok(K* kernel) {
+  cudaFuncAttributes fa{};
+  return cudaFuncGetAttributes(&fa, kernel) == cudaSuccess &&
+         2 * 128 * kRegsCompute + 128 * kRegsCtl <= (uint32_t)fa.numRegs * kBwdThreads;
+}
 
 template <int D, bool BF16, bool MASK, bool DBIAS>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -225,7 +245,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
 
-  if (warp == 0) {
+  // Each warpgroup changes its register count at the top of its own branch,
+  // so the code of the branch is compiled for that count.
+  if (warp < 4) {
+   setmaxnreg_dec<kRegsCtl>();
+   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && ntiles > 0) {
       prefetch_tmap(&tm_q);
@@ -349,10 +373,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
     }
+   }
   } else {
+    setmaxnreg_inc<kRegsCompute>();
     // ------------------------------------------------------------- compute
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 4) >> 2;
     const int r = quad * 32 + lane;  // key row == TMEM lane
     const int t = t0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -398,11 +424,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         } else if (!MASK && !DBIAS && cls == 1) {  // every query row sees this key: no per-element test
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float2 r0 = ri[c4 * 32 + 2 * e], r1 = ri[c4 * 32 + 2 * e + 1];  // shared-memory broadcasts
-            const float p0 = exp2_approx(fmaf(__uint_as_float(sv[2 * e]), a.qk_mult, -r0.x));
-            const float p1 = exp2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), a.qk_mult, -r1.x));
+            const float4 rr = *reinterpret_cast<const float4*>(ri + c4 * 32 + 2 * e);  // shared-memory broadcast
+            float p0 = __uint_as_float(sv[2 * e]), p1 = __uint_as_float(sv[2 * e + 1]);
+            fma2(p0, p1, a.qk_mult, a.qk_mult, -rr.x, -rr.z);
+            p0 = exp2_approx(p0);
+            p1 = exp2_approx(p1);
+            float d0 = __uint_as_float(dv[2 * e]), d1 = __uint_as_float(dv[2 * e + 1]);
+            add2(d0, d1, -rr.y, -rr.w);
+            mul2(d0, d1, p0, p1);
             pk[e] = pack2<BF16>(p0, p1);
-            dk[e] = pack2<BF16>(p0 * (__uint_as_float(dv[2 * e]) - r0.y), p1 * (__uint_as_float(dv[2 * e + 1]) - r1.y));
+            dk[e] = pack2<BF16>(d0, d1);
           }
         } else {
 #pragma unroll
@@ -582,7 +613,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t t_s = tmem, t_dp = tmem + 128;
   auto t_dq = [&](int x) { return tmem + 256 + x * D; };
 
-  if (warp == 0) {
+  // Each warpgroup changes its register count at the top of its own branch,
+  // so the code of the branch is compiled for that count.
+  if (warp < 4) {
+   setmaxnreg_dec<kRegsCtl>();
+   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tm_q);
@@ -729,10 +764,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
     }
+   }
   } else {
+    setmaxnreg_inc<kRegsCompute>();
     // --------------------------------------------------------- compute
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 4) >> 2;
     const int r = quad * 32 + lane;  // query row == TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     int T = 0, uc = 0;
@@ -775,9 +812,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           } else if (!MASK && cls == 1) {  // every key visible: no per-key test
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const float p0 = exp2_approx(fmaf(__uint_as_float(sv[2 * e]), a.qk_mult, -rw.x));
-              const float p1 = exp2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), a.qk_mult, -rw.x));
-              dk[e] = pack2<BF16>(p0 * (__uint_as_float(dv[2 * e]) - rw.y), p1 * (__uint_as_float(dv[2 * e + 1]) - rw.y));
+              float p0 = __uint_as_float(sv[2 * e]), p1 = __uint_as_float(sv[2 * e + 1]);
+              fma2(p0, p1, a.qk_mult, a.qk_mult, -rw.x, -rw.x);
+              p0 = exp2_approx(p0);
+            p1 = exp2_approx(p1);
+              float d0 = __uint_as_float(dv[2 * e]), d1 = __uint_as_float(dv[2 * e + 1]);
+              add2(d0, d1, -rw.y, -rw.y);
+              mul2(d0, d1, p0, p1);
+              dk[e] = pack2<BF16>(d0, d1);
             }
           } else {
 #pragma unroll
@@ -878,6 +920,8 @@ template <int D, bool BF16, bool MASK, bool DBIAS>
 int launch_kv(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   constexpr int sm = KvLayout<D>::ALLOC;
   auto* k = sdpa_bwd_kv_kernel<D, BF16, MASK, DBIAS>;
+  static const bool regs_ok = bwd_regs_ok(k);
+  if (!regs_ok) return RBLN_ERR_LAUNCH;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
   const int64_t n = (int64_t)((a.S + BT - 1) / BT) * a.Hkv * a.B;
   if (n > 2147483647LL) return RBLN_ERR_UNSUPPORTED;
@@ -889,6 +933,8 @@ template <int D, bool BF16, bool MASK>
 int launch_q(const BwdMaps& m, const BwdArgs& a, cudaStream_t st) {
   constexpr int sm = QLayout<D>::ALLOC;
   auto* k = sdpa_bwd_q_kernel<D, BF16, MASK>;
+  static const bool regs_ok = bwd_regs_ok(k);
+  if (!regs_ok) return RBLN_ERR_LAUNCH;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) return RBLN_ERR_LAUNCH;
   // persistent: one CTA per SM (at most one per unit)
   static int sms = 0;

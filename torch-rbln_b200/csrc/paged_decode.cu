@@ -932,7 +932,9 @@ int plan_decode(const rbln_paged_attn_params_t* p, Plan* pl) {
     // B=64 bf16 and B=256 fp8 workloads and on 32 x 32768 tokens).
     const int waves = env.waves > 0 ? env.waves : 1;
     const int per_sm = p->group <= 8 ? 4 : 2;
-    pl->nchunk = std::max(1, (148 * per_sm * waves + p->num_kv_heads - 1) / p->num_kv_heads);
+    // rounded down: a CTA past the resident slots would run as a second
+    // wave of its own, a whole chunk long
+    pl->nchunk = std::max(1, 148 * per_sm * waves / p->num_kv_heads);
     pl->min_w = env.min_w >= 16 ? env.min_w / 16 * 16 : 256;
     const size_t slots = (size_t)p->num_kv_heads * (pl->nchunk + p->batch) * p->group;
     pl->ws_bytes = prefix_bytes(p->batch) + slots * p->head_dim * sizeof(float) +

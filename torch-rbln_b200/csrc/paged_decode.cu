@@ -666,56 +666,52 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 4 : 2) paged_decode_balanc
 
 // Weighted sum of `nsplit` partials (index (base + s) * G + g) of sequence b,
 // KV head h into the output, for the query heads [g0, g0 + gn) of this CTA.
-// `sw` holds nsplit*G + G floats.
+// Thread = (query head, 4 dims). Each thread loads the log-sum-exps and its
+// 4 output values of 8 partials at once, so a batch costs one L2 round trip,
+// and keeps a running maximum across batches (the merge is latency-bound: a
+// sequence split over 19 chunks took six dependent round trips with the
+// weights computed first). The sink, when given, starts the sum.
 template <int D, bool Q_BF16>
-__device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h, int64_t base, int nsplit,
-                                               float* sw, int g0, int gn) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_inv = sw + nsplit * a.G;
-  for (int g = g0 + warp; g < g0 + gn; g += kWarps) {
-    float M = neg_inf();
-    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, a.part_lse[(base + s) * a.G + g]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float sk = sink_log2(a, h, g);
-    M = fmaxf(M, sk);
-    float S = (lane == 0 && sk != neg_inf()) ? exp2f(sk - M) : 0.f;
-    for (int s = lane; s < nsplit; s += 32) {
-      const float l = a.part_lse[(base + s) * a.G + g];
-      const float w = (l == neg_inf()) ? 0.f : exp2_approx(l - M);
-      sw[s * a.G + g] = w;
-      S += w;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    if (lane == 0) s_inv[g] = (M == neg_inf()) ? 0.f : 1.f / S;
-  }
-  __syncthreads();
-  for (int idx = tid; idx < gn * (D / 4); idx += kThreads) {
+__device__ __forceinline__ void merge_partials(const DecodeArgs& a, int b, int h, int64_t base, int nsplit, int g0,
+                                               int gn) {
+  constexpr int kBatch = 8;
+  const int64_t ps = (int64_t)a.G * D;  // floats from one partial slot to the next
+  for (int idx = threadIdx.x; idx < gn * (D / 4); idx += kThreads) {
     const int g = g0 + idx / (D / 4), d4 = (idx % (D / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    // eight partials at a time, their loads issued together (a sequence
-    // split over many chunks would otherwise pay one L2 round trip per
-    // partial); summed in the same order as one at a time
+    const float* pl = a.part_lse + base * a.G + g;
     const float* po = a.part_o + (base * a.G + g) * D + d4;
-    const int64_t ps = (int64_t)a.G * D;  // floats from one partial slot to the next
-    for (int s0 = 0; s0 < nsplit; s0 += 8) {
-      float w[8];
-      float4 o[8];
+    float M = sink_log2(a, h, g);
+    float S = (M == neg_inf()) ? 0.f : 1.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < nsplit; s0 += kBatch) {
+      float l[kBatch];
+      float4 o[kBatch];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) w[u] = s0 + u < nsplit ? sw[(s0 + u) * a.G + g] : 0.f;
+      for (int u = 0; u < kBatch; ++u) {
+        const bool in = s0 + u < nsplit;
+        l[u] = in ? pl[(int64_t)(s0 + u) * a.G] : neg_inf();
+        o[u] = in ? *reinterpret_cast<const float4*>(po + (s0 + u) * ps) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float mb = M;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        o[u] = w[u] != 0.f ? *reinterpret_cast<const float4*>(po + (s0 + u) * ps) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < kBatch; ++u) mb = fmaxf(mb, l[u]);
+      if (mb != M) {  // M == -inf: S and acc are still 0
+        const float c = (M == neg_inf()) ? 0.f : exp2_approx(M - mb);
+        S *= c;
+        acc.x *= c; acc.y *= c; acc.z *= c; acc.w *= c;
+        M = mb;
+      }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (w[u] != 0.f) {
-          acc.x += w[u] * o[u].x; acc.y += w[u] * o[u].y; acc.z += w[u] * o[u].z; acc.w += w[u] * o[u].w;
+      for (int u = 0; u < kBatch; ++u) {
+        if (l[u] != neg_inf()) {  // a partial with nothing visible carries no weight
+          const float w = exp2_approx(l[u] - M);
+          S += w;
+          acc.x += w * o[u].x; acc.y += w * o[u].y; acc.z += w * o[u].z; acc.w += w * o[u].w;
         }
       }
     }
-    float inv = s_inv[g];
-    if (inv == 0.f) inv = pos_nan();  // every position masked: NaN, as softmax of all -inf
+    // every position masked and no sink: NaN, as softmax of all -inf
+    const float inv = (M == neg_inf()) ? pos_nan() : 1.f / S;
     acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
     store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(acc.x, acc.y), pack2<Q_BF16>(acc.z, acc.w)));
   }
@@ -742,8 +738,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_kernel(const Deco
   int pos, L, nsplit;
   decode_extent(a, b, pos, L, nsplit);
   if (nsplit <= 1) return;
-  extern __shared__ float sw[];
-  merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, sw, g0, gn);
+  merge_partials<D, Q_BF16>(a, b, h, (int64_t)(b * a.Hkv + h) * a.max_splits, nsplit, g0, gn);
   merge_done();
 }
 
@@ -786,6 +781,9 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = blockIdx.x, b = blockIdx.y;
   const int gn = a.G / (int)gridDim.z, g0 = (int)blockIdx.z * gn;  // this CTA's query heads
+  // the chunk size and the sequence's padded range, loaded together with
+  // its length (one round trip instead of two)
+  const int W = a.prefix[a.B + 1], pb = a.prefix[b], pe = a.prefix[b + 1];
   int pos;
   const int L = seq_len(a, b, pos);
   if (pos < 0 && h == 0 && blockIdx.z == 0 && threadIdx.x == 0) flag_error(a.err, RBLN_DEVERR_SEQ_RANGE);
@@ -797,12 +795,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_merge_balanced_kernel(c
       store_out(a, b, h, g, d4, make_uint2(pack2<Q_BF16>(n, n), pack2<Q_BF16>(n, n)));
     }
   } else {
-    const int W = a.prefix[a.B + 1];
-    const int cf = a.prefix[b] / W, cl = (a.prefix[b + 1] - 1) / W;
+    const int cf = pb / W, cl = (pe - 1) / W;
     // cf == cl: one chunk held the whole sequence and wrote the output
     if (cf != cl) {
-      extern __shared__ float sw[];
-      merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, sw, g0, gn);
+      merge_partials<D, Q_BF16>(a, b, h, (int64_t)h * (a.nchunk + a.B) + cf + b, cl - cf + 1, g0, gn);
     }
   }
   merge_done();
@@ -1008,13 +1004,7 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
         launch_dependent(paged_decode_balanced_kernel<D, KV, QB, NT, LA>, dim3(pl.nchunk, a.Hkv), smem, st, a);
     if (drc != RBLN_OK) return drc;
     if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
-    // a sequence spans at most nchunk + 1 chunks
-    const size_t msmem = ((size_t)(pl.nchunk + 1) * a.G + a.G) * sizeof(float);
-    static SmemOptIn mdone;
-    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_balanced_kernel<D, KV, QB>), (int)msmem, mdone))
-      return RBLN_ERR_LAUNCH;
-    const int rc =
-        launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B, gz), msmem, st, a);
+    const int rc = launch_dependent(paged_decode_merge_balanced_kernel<D, KV, QB>, dim3(a.Hkv, a.B, gz), 0, st, a);
     if (rc != RBLN_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
   }
@@ -1027,11 +1017,7 @@ int launch_typed(const DecodeArgs& a, const Plan& pl, cudaStream_t st, void* con
   if (drc != RBLN_OK) return drc;
   if (ev && ev[1]) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
   if (pl.max_splits > 1) {
-    const size_t smem = ((size_t)pl.max_splits * a.G + a.G) * sizeof(float);
-    static SmemOptIn mdone;
-    if (!allow_smem(reinterpret_cast<const void*>(paged_decode_merge_kernel<D, QB>), (int)smem, mdone))
-      return RBLN_ERR_LAUNCH;
-    const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B, gz), smem, st, a);
+    const int rc = launch_dependent(paged_decode_merge_kernel<D, QB>, dim3(a.Hkv, a.B, gz), 0, st, a);
     if (rc != RBLN_OK) return rc;
   }
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;

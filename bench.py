@@ -37,8 +37,10 @@ timed region. Decode pools are far larger than the 126 MB L2; the compute
 workloads flush L2 (a 256 MB write) before each timed iteration.
 
 Under torchrun (N > 1) the headline runs N replicas of the decode batch
-(sequences are independent; no collective on the data path); every number
-is whole-job work over the max-over-ranks device time.
+(sequences are independent; no collective on the data path): every rank the
+one-GPU workload's lengths and block table over its own KV data, so the
+per-GPU work is fixed; every number is whole-job work over the
+max-over-ranks device time.
 
 `parity` in each record compares the output of the last timed call with the
 CPU oracle (oracle/paged_attention.py, oracle/sdpa.py) on a seeded subset of
@@ -347,7 +349,9 @@ def _decode_dict(wl, lay, kc, vc, ks, vs):
 def build_decode_sharded(wl: dict, mode: str, rank: int, ws: int, device):
     """This rank's decode inputs under `mode` (see WORKLOADS)."""
     if mode == "replicas":
-        return build_decode(wl, device, seed=1000 * rank)
+        # weak scaling: every rank runs the one-GPU workload itself (the same
+        # lengths and block table, so the same bytes), over its own KV data
+        return build_decode(wl, device, seed=0, pool_seed=1 + rank)
     if mode == "heads":
         # same sequences and block table on every rank; rank r holds KV heads
         # [r * Hkv / N, (r + 1) * Hkv / N) of the pool (and their query heads)
@@ -392,7 +396,8 @@ def decode_config(wl_name, ws, mode, global_batch, pool_bytes, step_bytes):
     arm prints the same."""
     wl = WORKLOADS[wl_name]
     par = {"single": "single GPU",
-           "replicas": f"replicas x{ws}: every rank its own batch of {wl['B']} sequences, no collective",
+           "replicas": (f"replicas x{ws}: every rank the one-GPU batch of {wl['B']} sequences (same lengths "
+                        f"and block table) over its own KV data, no collective"),
            "heads": (f"kv-head-sharded x{ws}: head outputs stored into every rank's buffer by the decode "
                      f"kernels (NVLink peer stores) + epoch exchange in the merge kernel"),
            "batch": f"batch-sharded x{ws}: each rank its share of the {wl['B']} sequences, own pool and table"}[mode]

@@ -840,21 +840,26 @@ def _timed_kernel_loop(args, stream, step, kernel_step, flush, kernel_events=Fal
     (`step`) and, in separate iterations, around the main kernel alone
     (`kernel_step`; with kernel_events it takes the event pair and has the
     C-ABI record it right around the kernel), each preceded by an L2 flush
-    outside the timed window."""
-    def timed(fn, inner=False):
-        ev = _event_pairs(args.steps, stream)
-        for i in range(args.steps):
-            flush.zero_()
-            if inner:
-                fn(*ev[i])
-                continue
-            ev[i][0].record(stream)
-            fn()
-            ev[i][1].record(stream)
-        torch.cuda.synchronize()
-        return statistics.mean(a.elapsed_time(b) for a, b in ev)
-
-    return timed(step), timed(kernel_step, kernel_events)
+    outside the timed window. The two kinds of iteration alternate, so that
+    both see the same clocks: timed one loop after the other, the second
+    loop of a tensor-bound op ran under the power cap and read 5 % slower
+    than the first for the very same launches."""
+    ev_op, ev_k = _event_pairs(args.steps, stream), _event_pairs(args.steps, stream)
+    for i in range(args.steps):
+        flush.zero_()
+        ev_op[i][0].record(stream)
+        step()
+        ev_op[i][1].record(stream)
+        flush.zero_()
+        if kernel_events:
+            kernel_step(*ev_k[i])
+        else:
+            ev_k[i][0].record(stream)
+            kernel_step()
+            ev_k[i][1].record(stream)
+    torch.cuda.synchronize()
+    return (statistics.mean(a.elapsed_time(b) for a, b in ev_op),
+            statistics.mean(a.elapsed_time(b) for a, b in ev_k))
 
 
 def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:

@@ -1371,6 +1371,80 @@ def run_suite_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def peer_emulation_record(args, wl_name: str, ranks: int) -> dict:
+    """One GPU: rank 0's share of a head-sharded decode at `ranks` ranks,
+    timed through the plain entry point and through the peers entry point
+    with n = 1, 2 and `ranks` emulated ranks whose output buffers and flag
+    arrays all live in this GPU's memory, the other ranks' announcements
+    pre-set. The difference is the peer path's own cost (the stores into n
+    buffers, the merge kernel's arrival chain, the system-scope releases)
+    without NVLink."""
+    import torch_rbln_b200  # noqa: F401
+    from torch_rbln_b200 import cabi
+
+    wl = WORKLOADS[wl_name]
+    if wl["shard"] != "heads" or ranks < 2 or wl["Hkv"] % ranks:
+        raise SystemExit(f"--emulate-ranks needs a head-sharded workload whose KV heads divide by {ranks}")
+    ctx = Ctx()
+    dev, stream = ctx.dev, ctx.stream
+    d = build_decode_sharded(wl, "heads", 0, ranks, dev)
+    q, k, v, seq, bt = (d[x].to(dev) for x in ("q", "k", "v", "seq", "bt"))
+    L = cabi.lib()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    B, Hkv, G, _, D = q.shape
+
+    def time_us(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps * 1e3
+
+    p, keep = cabi.paged_params(q, k, v, d["kcache"], d["vcache"], seq, bt, d["bs"], d["scale"])
+    cabi.attach_workspace(p, dev, keep)
+    p.error_flags = err.data_ptr()
+
+    def plain():
+        if L.rbln_paged_causal_attn_decode(ctypes.byref(p), sh) != 0:
+            raise RuntimeError("rbln_paged_causal_attn_decode failed")
+
+    rec = {"metric": "head-sharded decode per call, peer path emulated on one GPU", "unit": "us",
+           "workload": wl["desc"], "emulated_ranks": ranks, "steps": args.steps, "warmup": args.warmup,
+           "plain_op_us": round(time_us(plain), 2), "peers_op_us": {}}
+    with torch.cuda.stream(stream):
+        for n in sorted({1, 2, ranks}):
+            outs = [torch.zeros([B, n * Hkv, G, 1, D], dtype=q.dtype, device=dev) for _ in range(n)]
+            flags = [torch.zeros(n, dtype=torch.int32, device=dev) for _ in range(n)]
+            flags[0][1:] = 0x40000000  # every other rank has announced every epoch used here
+            out_ptrs = torch.tensor([o.data_ptr() for o in outs], dtype=torch.int64, device=dev)
+            flag_ptrs = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=dev)
+            pp, kp = cabi.paged_params(q, k, v, d["kcache"], d["vcache"], seq, bt, d["bs"], d["scale"], out=outs[0])
+            cabi.attach_workspace(pp, dev, kp)
+            pp.error_flags = err.data_ptr()
+            po = cabi.PeerOut()
+            po.out, po.flags = out_ptrs.data_ptr(), flag_ptrs.data_ptr()
+            po.n, po.rank, po.head0, po.wait_limit_us = n, 0, 0, 100000
+            epoch = [0]
+
+            def peers():
+                epoch[0] += 1
+                po.epoch = epoch[0]
+                if L.rbln_paged_causal_attn_decode_peers(ctypes.byref(pp), ctypes.byref(po), sh) != 0:
+                    raise RuntimeError("rbln_paged_causal_attn_decode_peers failed")
+
+            rec["peers_op_us"][str(n)] = round(time_us(peers), 2)
+    torch.cuda.synchronize()
+    rec["device_error_bits"] = int(err.item())
+    ctx.close()
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1381,9 +1455,15 @@ def main():
                     choices=["suite"] + sorted(WORKLOADS) + sorted(COMPUTE) + sorted(KVWRITE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--emulate-ranks", type=int, default=0,
+                    help="one GPU: time rank 0's share of a head-sharded decode at this many ranks through the "
+                         "plain and the peers entry points, every rank's buffers local (the peer path's own cost)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.emulate_ranks:
+        print(json.dumps(peer_emulation_record(args, args.workload, args.emulate_ranks)), flush=True)
+        return
     if args.workload == "suite":
         (run_suite_reference if args.impl == "reference" else run_suite_ours)(args)
         return

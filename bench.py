@@ -1045,6 +1045,14 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
+    if dtype == "f32":
+        # the exact-fp32 kernel runs on the FMA pipes, not the tensor cores:
+        # its own ceiling is the nominal fp32 FMA rate (148 SMs x 128 lanes
+        # x 2 FLOP at the 1965 MHz maximum clock; no measured figure exists)
+        simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        rec["roofline"]["fp32_simt"] = {"peak": round(simt_peak, 1), "unit": "TFLOP/s",
+                                        "frac": round(achieved / simt_peak, 4),
+                                        "peak_source": "nominal fp32 FMA rate (148 x 128 x 2 x 1.965 GHz)"}
     if parity is not None:
         rec["parity"] = parity
     if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:

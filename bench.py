@@ -847,6 +847,21 @@ def build_sdpa(wl, seed=0):
     return d
 
 
+L2_FLUSH_NOTE = "L2 flushed between iterations (256 MB write, outside the timed events)"
+
+
+def compute_config(wl: dict, d: dict, ws: int) -> dict:
+    """The `config` of a compute workload's record, the same in both arms."""
+    return {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+            "l2": L2_FLUSH_NOTE, "flops_per_step": d["flops"]}
+
+
+def kv_write_config(wl: dict, d: dict, ws: int) -> dict:
+    """The `config` of the KV-write record, the same in both arms."""
+    return {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+            "l2": L2_FLUSH_NOTE, "bytes_per_step": d["bytes"]}
+
+
 def _timed_kernel_loop(args, stream, step, kernel_step, flush, kernel_events=False):
     """Per-iteration CUDA events on the launch stream around the whole op
     (`step`) and, in separate iterations, around the main kernel alone
@@ -991,7 +1006,6 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
                   else "attn_fwd_tc3_kernel<128, bf16> (tcgen05/TMEM/TMA, 128-key tiles, P in TMEM, two query tiles per CTA)")
         dtype = "f32" if wl["dtype"] == torch.float32 else "bf16"
         result["parity"] = lambda: sdpa_parity(d, out)
-    l2 = "L2 flushed between iterations (256 MB write, outside the timed events)"
 
     for _ in range(args.warmup):
         step()
@@ -1041,8 +1055,7 @@ def compute_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
         "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded N(0,1) inputs" + (", seeded cached lengths and block-table permutation)"
                                                      if wl["kind"] == "prefill" else ")"),
-        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
-                   "l2": l2, "flops_per_step": flops},
+        "config": compute_config(wl, d, ws),
         "e2e": {"value": round(ws * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": {"prefill": ("torch.ops.rbln_custom_ops.paged_attn_prefill" if wl.get("keep_mask") else
@@ -1186,7 +1199,7 @@ def reference_compute_line(args, ctx: Ctx, wl_name: str, budget_s=120.0) -> dict
     return {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": "TFLOP/s", "n_gpus": ctx.ws,
             "steps": len(times), "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)",
-            "config": {"workload": wl["desc"]},
+            "config": compute_config(wl, d, ctx.ws),
             "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
                              "sample": sample + ", " + _cpu_stats_note(times)},
             "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1297,9 +1310,7 @@ def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(op_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded N(0,1) rows, seeded starts and block-table permutation)",
-        "config": {"workload": wl["desc"], "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
-                   "l2": "L2 flushed between iterations (256 MB write, outside the timed events)",
-                   "bytes_per_step": d["bytes"]},
+        "config": kv_write_config(wl, d, ws),
         "e2e": {"value": round(ws * d["bytes"] / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "torch.ops.rbln_attn.paged_kv_write"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -1329,7 +1340,7 @@ def reference_kv_write_line(args, ctx: Ctx, wl_name: str, budget_s=10.0) -> dict
             "unit": "GB/s", "n_gpus": ctx.ws, "steps": len(times), "warmup": args.warmup,
             "ms_per_step": round(med * 1e3 * d["B"], 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)",
-            "config": {"workload": wl["desc"]},
+            "config": kv_write_config(wl, d, ctx.ws),
             "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

@@ -26,11 +26,12 @@
 //    (cvt.rn.f16x2.e4m3x2); the per-(block, head) K scale multiplies the
 //    scores and the V scale is folded into P before the PV product.
 //  * Work is cut into equal chunks across the whole batch ("balanced"
-//    split-K): the sequences' lengths, each rounded up to 16, are laid end to
-//    end and CTA (c, h) takes tokens [c*W, (c+1)*W) of KV head h, whatever
-//    sequences they belong to. Each CTA computes that prefix itself from seq,
-//    so no host synchronisation is needed. One wave of CTAs (4 per SM) with
-//    equal work leaves no tail of long sequences.
+//    split-K): the sequences' lengths, each rounded up to 16 and preceded by
+//    seg_cost virtual tokens (the cost of starting a segment), are laid end to
+//    end and CTA (c, h) takes list positions [c*W, (c+1)*W) of KV head h,
+//    whatever sequences they belong to. Each CTA computes that prefix itself
+//    from seq, so no host synchronisation is needed. One wave of CTAs (4 per
+//    SM) with equal work leaves no tail of long sequences.
 //  * A CTA writes one (O/l, log2-sum-exp) partial per sequence it touches; a
 //    merge kernel (launched as a programmatic dependent) combines them. A
 //    sequence held by one CTA is written directly by it.
@@ -634,8 +635,9 @@ __device__ __forceinline__ int balanced_prefix(const DecodeArgs& a, int* P) {
 }
 
 // Balanced split: the batch's tokens, each sequence padded to a multiple of
-// 16, are cut into equal chunks of W tokens, so every CTA has the same work
-// however unequal the sequences are. CTA (c, h) takes chunk c of KV head h,
+// 16 and preceded by seg_cost virtual tokens, are cut into equal chunks of W
+// list positions, so every CTA has about the same work however unequal the
+// sequences are. CTA (c, h) takes chunk c of KV head h,
 // which may cover the end of one sequence and the start of the next ones: one
 // segment (and one partial, at slot c + b of head h) per sequence touched.
 template <int D, int KV, bool Q_BF16, int NT, bool LA>

@@ -50,19 +50,28 @@ __device__ __forceinline__ float f32_mask(const void* base, int dt, int64_t i) {
   }
 }
 
-// Thread (ty, tx) owns query rows 4ty..4ty+3; for scores the key columns
-// 4tx..4tx+3 of the tile, for the output the head-dim columns tx + 16c.
+// Thread (ty, tx) owns query rows 4ty..4ty+3; for scores the keys
+// tx + 16j (j < 4) of the tile, for the output the head-dim columns
+// 4tx + 64c .. 4tx + 64c + 3 (c < D / 64). Shared-memory rows are padded to
+// D + 4 floats: 16-byte aligned, so every operand is read as a float4 (one
+// load per 8 FMAs; scalar reads made the kernel load-bound at one per two),
+// and rows tx + 16j of consecutive tx start 4 banks apart, so the K reads
+// of a warp are conflict-free. Every dot product and every output column
+// accumulates in the same order as a scalar loop over d or over the keys.
 template <int D>
 __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
-  constexpr int DP = D + 1;
-  constexpr int DC = D / 16;
-  extern __shared__ float fsm[];
+  constexpr int DP = D + 4;
+  constexpr int PP = FK + 4;
+  constexpr int DC = D / 64;  // float4 output columns per thread
+  extern __shared__ __align__(16) float fsm[];
   float* Qs = fsm;           // [FQ][DP]
   float* Ks = Qs + FQ * DP;  // [FK][DP]
   float* Vs = Ks + FK * DP;  // [FK][DP]
-  float* Ps = Vs + FK * DP;  // [FQ][FK + 1]
+  float* Ps = Vs + FK * DP;  // [FQ][PP]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int qb = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  // grid (head, query tile, batch), query tiles in reverse: CTAs are
+  // dispatched head-fastest, so every head's longest causal tiles start first
+  const int qb = (int)gridDim.y - 1 - (int)blockIdx.y, hq = blockIdx.x, b = blockIdx.z;
   const int hk = hq / (a.Hq / a.Hkv);
   const int l0 = qb * FQ;
 
@@ -71,13 +80,14 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
     const int l = l0 + r;
     Qs[r * DP + d] = (l < a.L) ? a.q[b * a.qs_b + hq * a.qs_h + (int64_t)l * a.qs_l + d] : 0.f;
   }
-  float m_run[4], l_run[4], o[4][DC];
+  float m_run[4], l_run[4];
+  float4 o[4][DC];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     m_run[i] = neg_inf();
     l_run[i] = 0.f;
 #pragma unroll
-    for (int c = 0; c < DC; ++c) o[i][c] = 0.f;
+    for (int c = 0; c < DC; ++c) o[i][c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   int kend = a.S;
   if (a.causal) kend = min(kend, l0 + FQ);
@@ -99,17 +109,22 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < D; ++d) {
-      float qv[4], kv[4];
+#pragma unroll 4
+    for (int d = 0; d < D; d += 4) {
+      float4 qv[4], kv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) qv[i] = Qs[(4 * ty + i) * DP + d];
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(&Qs[(4 * ty + i) * DP + d]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) kv[j] = Ks[(4 * tx + j) * DP + d];
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(&Ks[(tx + 16 * j) * DP + d]);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+          s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+          s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+          s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+        }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -117,7 +132,7 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
       float mx = neg_inf();
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int kk = k0 + 4 * tx + j;
+        const int kk = k0 + tx + 16 * j;
         bool keep = (l < a.L) && (kk < a.S) && (!a.causal || kk <= l);
         float x = s[i][j] * a.scale;
         if (keep && a.mask) {
@@ -137,7 +152,7 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float p = expf(s[i][j] - mu);
-        Ps[(4 * ty + i) * (FK + 1) + 4 * tx + j] = p;
+        Ps[(4 * ty + i) * PP + tx + 16 * j] = p;
         sum += p;
       }
 #pragma unroll
@@ -145,20 +160,31 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
       l_run[i] = l_run[i] * alpha + sum;
       m_run[i] = mn;
 #pragma unroll
-      for (int c = 0; c < DC; ++c) o[i][c] *= alpha;
+      for (int c = 0; c < DC; ++c) {
+        o[i][c].x *= alpha; o[i][c].y *= alpha; o[i][c].z *= alpha; o[i][c].w *= alpha;
+      }
     }
     __syncthreads();
-#pragma unroll 4
-    for (int kk = 0; kk < FK; ++kk) {
-      float pv[4], vv[DC];
+#pragma unroll 2
+    for (int kk = 0; kk < FK; kk += 4) {
+      float4 pv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pv[i] = Ps[(4 * ty + i) * (FK + 1) + kk];
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(&Ps[(4 * ty + i) * PP + kk]);
 #pragma unroll
-      for (int c = 0; c < DC; ++c) vv[c] = Vs[kk * DP + tx + 16 * c];
+      for (int u = 0; u < 4; ++u) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int c = 0; c < DC; ++c) {
+          const float4 vv = *reinterpret_cast<const float4*>(&Vs[(kk + u) * DP + 4 * tx + 64 * c]);
 #pragma unroll
-        for (int c = 0; c < DC; ++c) o[i][c] = fmaf(pv[i], vv[c], o[i][c]);
+          for (int i = 0; i < 4; ++i) {
+            const float pw = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
+            o[i][c].x = fmaf(pw, vv.x, o[i][c].x);
+            o[i][c].y = fmaf(pw, vv.y, o[i][c].y);
+            o[i][c].z = fmaf(pw, vv.z, o[i][c].z);
+            o[i][c].w = fmaf(pw, vv.w, o[i][c].w);
+          }
+        }
+      }
     }
   }
 #pragma unroll
@@ -168,7 +194,13 @@ __global__ void __launch_bounds__(FT) sdpa_f32_kernel(const F32Args a) {
     const float inv = 1.f / l_run[i];
     float* orow = a.out + b * a.os_b + hq * a.os_h + (int64_t)l * a.os_l;
 #pragma unroll
-    for (int c = 0; c < DC; ++c) orow[tx + 16 * c] = o[i][c] * inv;
+    for (int c = 0; c < DC; ++c) {
+      const int d = 4 * tx + 64 * c;
+      orow[d] = o[i][c].x * inv;
+      orow[d + 1] = o[i][c].y * inv;
+      orow[d + 2] = o[i][c].z * inv;
+      orow[d + 3] = o[i][c].w * inv;
+    }
     if (a.lse && tx == 0)
       a.lse[b * a.ls_b + hq * a.ls_h + (int64_t)l * a.ls_l] =
           (m_run[i] == neg_inf()) ? neg_inf() : m_run[i] + logf(l_run[i]);
@@ -179,10 +211,11 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int D>
 int launch_f32(const F32Args& a, int L, int H, int B, cudaStream_t stream) {
-  const size_t sm = (size_t)(3 * 64 * (D + 1) + 64 * 65) * sizeof(float);
+  const size_t sm = (size_t)(3 * 64 * (D + 4) + 64 * (FK + 4)) * sizeof(float);
   if (cudaFuncSetAttribute(sdpa_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
     return RBLN_ERR_LAUNCH;
-  dim3 grid((L + FQ - 1) / FQ, H, B);
+  if ((L + FQ - 1) / FQ > 65535) return RBLN_ERR_UNSUPPORTED;
+  dim3 grid(H, (L + FQ - 1) / FQ, B);
   sdpa_f32_kernel<D><<<grid, FT, sm, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
 }

@@ -279,6 +279,14 @@ def test_decode_balanced_chunks_span_many_sequences():
     check(run_op(d), oracle(d))
 
 
+def test_decode_balanced_single_token_sequences():
+    """512 one-token sequences: the balanced split charges each sequence start
+    a run of virtual tokens, so most chunks cover only virtual tokens of some
+    sequences and must skip them; every sequence still gets its output."""
+    d = make_decode(512, 2, 4, 128, 16, [1] * 512, seed=24)
+    check(run_op(d), oracle(d))
+
+
 @pytest.mark.parametrize("G", [4, 16])
 def test_decode_balanced_one_long_sequence(G):
     """One sequence spread over many chunks, next to short ones."""

@@ -1074,6 +1074,12 @@ __global__ void __launch_bounds__(kThreads3, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched as a programmatic dependent of the append kernel on the paged
+  // path: the set-up above (barriers, TMEM) reads no global memory and
+  // overlaps the previous grid; everything below reads its results (the
+  // appended rows, the schedule), so it waits for that grid here. Without a
+  // programmatic launch this returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   auto t_s = [&](int x) { return tmem + x * 128; };
   auto t_o = [&](int x) { return tmem + 256 + x * 128; };
@@ -1396,7 +1402,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
         for (int e = 0; e < BN3; e += 2) fma2(xv[e], xv[e + 1], mult, mult, nmu, nmu);
 #pragma unroll
         for (int e = 0; e < BN3; e += 2) {
-          if (POLY > 0 && (e / 2) % POLY == POLY - 1) {
+          if (POLY > 0 && (e / 2) % (POLY > 0 ? POLY : 1) == POLY - 1) {
             exp2_poly2(xv[e], xv[e + 1]);
           } else {
             xv[e] = exp2_approx(xv[e]);
@@ -1649,6 +1655,9 @@ __global__ void __launch_bounds__(256)
   constexpr int PER_LANE = 2 * kAppendTok * CPR / 32;    // pieces per lane: 16 (D = 128) or 8 (D = 64)
   constexpr int BATCH = 8;
   static_assert(PER_LANE % BATCH == 0, "pieces per lane");
+  // the attention kernel after this one may be scheduled now: it waits in
+  // its own code for this grid to complete before reading the cache
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = (blockIdx.x * 8 + warp) * kAppendTok;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -1703,6 +1712,7 @@ struct TcLaunch {
   AttnArgs a;
   int D;
   bool bf16;
+  bool dependent = false;  // 128-key kernel: programmatic dependent of the previous launch
 };
 
 template <int D, bool BF16>
@@ -1766,8 +1776,24 @@ int launch_tc3(const TcLaunch& Lc, cudaStream_t st) {
   // persistent: one CTA per SM, each striding through the units
   const int grid = (int)std::min<long long>(n, sm_count());
   if (grid == 0) return RBLN_OK;
-  attn_fwd_tc3_kernel<D, BF16, POLY, MASKED><<<grid, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n);
-  return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+  if (!Lc.dependent) {
+    attn_fwd_tc3_kernel<D, BF16, POLY, MASKED><<<grid, kThreads3, SL::ALLOC, st>>>(Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n);
+    return cudaGetLastError() == cudaSuccess ? RBLN_OK : RBLN_ERR_LAUNCH;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads3);
+  cfg.dynamicSmemBytes = SL::ALLOC;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_fwd_tc3_kernel<D, BF16, POLY, MASKED>, Lc.tq, Lc.tk, Lc.tv, Lc.a, (int)n) ==
+                 cudaSuccess
+             ? RBLN_OK
+             : RBLN_ERR_LAUNCH;
 }
 
 // Share of the 128-key kernel's exponentials evaluated on the FMA pipe:
@@ -2029,6 +2055,8 @@ int run_prefill(const rbln_paged_attn_params_t* p, cudaStream_t st, bool keep_ma
     }
   }
   if (p->prof_events[0]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[0]), st);
+  // the 128-key kernel's set-up overlaps the append (or schedule) kernel before it
+  Lc.dependent = kern == 3;
   const int rc = kern == 3 ? launch_tc3_any(Lc, st) : kern == 2 ? launch_tc2_any(Lc, st) : launch_tc_any(Lc, st);
   if (p->prof_events[1]) cudaEventRecord(static_cast<cudaEvent_t>(p->prof_events[1]), st);
   return rc;

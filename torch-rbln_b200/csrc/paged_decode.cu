@@ -463,10 +463,16 @@ __device__ __forceinline__ void decode_segment(const DecodeArgs& a, unsigned cha
       l_run[nt][1] = l_run[nt][1] * al1 + p1 + p3;
       m_run[nt][0] = mn0;
       m_run[nt][1] = mn1;
+      // once the running maxima settle the factors are exactly 1 (their
+      // exponent is exactly 0): the fp8 variant, which spends more issue
+      // slots per tile on conversions, skips the rescale for the warp then
+      // (measured +0.4 %); for 16-bit caches the vote cost as much as it saved
+      if (KV != KV_FP8 || __any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
-      for (int mt = 0; mt < C::MT; ++mt) {
-        o_acc[nt][mt][0] *= al0; o_acc[nt][mt][2] *= al0;
-        o_acc[nt][mt][1] *= al1; o_acc[nt][mt][3] *= al1;
+        for (int mt = 0; mt < C::MT; ++mt) {
+          o_acc[nt][mt][0] *= al0; o_acc[nt][mt][2] *= al0;
+          o_acc[nt][mt][1] *= al1; o_acc[nt][mt][3] *= al1;
+        }
       }
       pb0[nt] = movmatrix_trans(pack2<MB>(p0 * vs0, p1 * vs0));
       pb1[nt] = movmatrix_trans(pack2<MB>(p2 * vs1, p3 * vs1));

@@ -18,8 +18,12 @@
 // One warp per (touched block slot, KV head, K or V, sequence), HBM-bound:
 // 16-byte loads of the new rows, an amax by warp shuffles, then one
 // correctly rounded reciprocal of the scale per block and one multiply per
-// element (q = e4m3(x * (1 / scale))). New rows are read twice (amax, then
-// quantization; the second read mostly hits L2) and written once.
+// element (q = e4m3(x * (1 / scale))). When a block holds at most 256
+// 16-byte chunks (bs x D / 8; bs <= 16 at D = 128, bs <= 32 at D = 64) the
+// new rows are loaded once into registers, ahead of the block-table lookup,
+// since their addresses need only the sequence start; larger blocks stream
+// the new rows twice (amax, then quantization; the second read mostly hits
+// L2).
 
 #include "common.cuh"
 
@@ -28,6 +32,7 @@ namespace {
 
 constexpr int kWriteThreads = 256;
 constexpr float kFp8Max = 448.f;
+constexpr int kRegChunks = 8;  // 16-byte chunks of new rows one lane holds
 
 struct WriteArgs {
   const char* k_new;
@@ -111,21 +116,39 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
   }
   const int bi = s0 / a.bs + j;
   if (bi > (s0 + a.S - 1) / a.bs) return;
-  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
-  if (phys < 0 || phys >= a.num_blocks) {
-    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
-    return;
-  }
   const int base = bi * a.bs;
   const int lo = max(s0, base) - base;               // first new row in the block
   const int hi = min(s0 + a.S, base + a.bs) - base;  // one past the last
   const int held = s0 > base ? lo : 0;               // rows [0, held) hold the sequence's context
   const char* src = part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h : a.v_new + b * a.vn_b + h * a.vn_h;
   const int64_t src_s = part == 0 ? a.kn_s : a.vn_s;
+  const int cpr = a.D / 8;                           // 8-element chunks per row (8 or 16)
+  const int cshift = a.D == 128 ? 4 : 3;
+  auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
+
+  // fp8 caches whose blocks hold at most 256 chunks: each lane loads its
+  // chunks of the new rows into registers now, before the block-table
+  // lookup, so the row loads overlap it, and quantizes from the registers.
+  const bool in_regs = FP8 && (a.bs << cshift) <= 32 * kRegChunks;
+  const int n_new = (hi - lo) << cshift;  // new chunks in the block
+  uint4 w[kRegChunks];
+  if constexpr (FP8) {
+    if (in_regs) {
+#pragma unroll
+      for (int k = 0; k < kRegChunks; ++k) {
+        const int i = lane + 32 * k;
+        if (i < n_new) w[k] = ld_stream_v4(new_row(lo + (i >> cshift)) + (i & (cpr - 1)) * 16);
+      }
+    }
+  }
+
+  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+  if (phys < 0 || phys >= a.num_blocks) {
+    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    return;
+  }
   char* cache = part == 0 ? a.kcache : a.vcache;
   const int64_t cbase = phys * a.cs_block + (int64_t)h * a.cs_head;  // elements
-  const int cpr = a.D / 8;                                           // 8-element chunks per row
-  auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
 
   if constexpr (!FP8) {
     for (int i = lane; i < (hi - lo) * cpr; i += 32) {
@@ -145,12 +168,24 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
 #pragma unroll
       for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
-    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
-      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-      float x[8];
-      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+    if (in_regs) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+      for (int k = 0; k < kRegChunks; ++k) {
+        if (lane + 32 * k < n_new) {
+          float x[8];
+          unpack8<IN_BF16>(w[k], x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+        }
+      }
+    } else {
+      for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+        float x[8];
+        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+      }
     }
     const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
     const float inv = __frcp_rn(scale);
@@ -163,11 +198,24 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
         *q = pack8_e4m3(x, inv);
       }
     }
-    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
-      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-      float x[8];
-      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
-      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
+    if (in_regs) {
+#pragma unroll
+      for (int k = 0; k < kRegChunks; ++k) {
+        const int i = lane + 32 * k;
+        if (i < n_new) {
+          float x[8];
+          unpack8<IN_BF16>(w[k], x);
+          const int r = lo + (i >> cshift), c = i & (cpr - 1);
+          *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
+        }
+      }
+    } else {
+      for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+        float x[8];
+        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+        *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
+      }
     }
     __syncwarp();  // every lane has read `old` before it is replaced
     if (lane == 0) *sp = scale;

@@ -18,21 +18,23 @@
 // One warp per (touched block slot, KV head, K or V, sequence), HBM-bound:
 // 16-byte loads of the new rows, an amax by warp shuffles, then one
 // correctly rounded reciprocal of the scale per block and one multiply per
-// element (q = e4m3(x * (1 / scale))). When a block holds at most 256
-// 16-byte chunks (bs x D / 8; bs <= 16 at D = 128, bs <= 32 at D = 64) the
-// new rows are loaded once into registers, ahead of the block-table lookup,
-// since their addresses need only the sequence start; larger blocks stream
-// the new rows twice (amax, then quantization; the second read mostly hits
-// L2).
+// element (q = e4m3(x * (1 / scale))). For fp8 caches whose blocks hold at
+// most 256 16-byte chunks of new rows (bs x D / 8; bs <= 16 at D = 128,
+// bs <= 32 at D = 64) the warp bulk-copies the block's new rows into shared
+// memory as soon as the sequence start is known -- their addresses need
+// nothing else -- and reads the block-table entry while they land. Larger
+// blocks stream the new rows twice (amax, then quantization; the second
+// read mostly hits L2).
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace rbln {
 namespace {
 
 constexpr int kWriteThreads = 256;
 constexpr float kFp8Max = 448.f;
-constexpr int kRegChunks = 8;  // 16-byte chunks of new rows one lane holds
+constexpr int kStageChunks = 256;  // 16-byte chunks of new rows one warp stages (4 KB)
 
 struct WriteArgs {
   const char* k_new;
@@ -116,39 +118,21 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
   }
   const int bi = s0 / a.bs + j;
   if (bi > (s0 + a.S - 1) / a.bs) return;
+  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+  if (phys < 0 || phys >= a.num_blocks) {
+    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+    return;
+  }
   const int base = bi * a.bs;
   const int lo = max(s0, base) - base;               // first new row in the block
   const int hi = min(s0 + a.S, base + a.bs) - base;  // one past the last
   const int held = s0 > base ? lo : 0;               // rows [0, held) hold the sequence's context
   const char* src = part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h : a.v_new + b * a.vn_b + h * a.vn_h;
   const int64_t src_s = part == 0 ? a.kn_s : a.vn_s;
-  const int cpr = a.D / 8;                           // 8-element chunks per row (8 or 16)
-  const int cshift = a.D == 128 ? 4 : 3;
-  auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
-
-  // fp8 caches whose blocks hold at most 256 chunks: each lane loads its
-  // chunks of the new rows into registers now, before the block-table
-  // lookup, so the row loads overlap it, and quantizes from the registers.
-  const bool in_regs = FP8 && (a.bs << cshift) <= 32 * kRegChunks;
-  const int n_new = (hi - lo) << cshift;  // new chunks in the block
-  uint4 w[kRegChunks];
-  if constexpr (FP8) {
-    if (in_regs) {
-#pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        const int i = lane + 32 * k;
-        if (i < n_new) w[k] = ld_stream_v4(new_row(lo + (i >> cshift)) + (i & (cpr - 1)) * 16);
-      }
-    }
-  }
-
-  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
-  if (phys < 0 || phys >= a.num_blocks) {
-    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
-    return;
-  }
   char* cache = part == 0 ? a.kcache : a.vcache;
   const int64_t cbase = phys * a.cs_block + (int64_t)h * a.cs_head;  // elements
+  const int cpr = a.D / 8;                                           // 8-element chunks per row
+  auto new_row = [&](int r) { return src + (int64_t)(base + r - s0) * src_s; };
 
   if constexpr (!FP8) {
     for (int i = lane; i < (hi - lo) * cpr; i += 32) {
@@ -168,24 +152,12 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
 #pragma unroll
       for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
-    if (in_regs) {
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
 #pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        if (lane + 32 * k < n_new) {
-          float x[8];
-          unpack8<IN_BF16>(w[k], x);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
-        }
-      }
-    } else {
-      for (int i = lane; i < (hi - lo) * cpr; i += 32) {
-        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-        float x[8];
-        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
-      }
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
     }
     const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
     const float inv = __frcp_rn(scale);
@@ -198,28 +170,128 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
         *q = pack8_e4m3(x, inv);
       }
     }
-    if (in_regs) {
-#pragma unroll
-      for (int k = 0; k < kRegChunks; ++k) {
-        const int i = lane + 32 * k;
-        if (i < n_new) {
-          float x[8];
-          unpack8<IN_BF16>(w[k], x);
-          const int r = lo + (i >> cshift), c = i & (cpr - 1);
-          *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
-        }
-      }
-    } else {
-      for (int i = lane; i < (hi - lo) * cpr; i += 32) {
-        const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
-        float x[8];
-        unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
-        *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
-      }
+    for (int i = lane; i < (hi - lo) * cpr; i += 32) {
+      const int r = lo + i / cpr, c = i - (i / cpr) * cpr;
+      float x[8];
+      unpack8<IN_BF16>(*reinterpret_cast<const uint4*>(new_row(r) + c * 16), x);
+      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
     }
     __syncwarp();  // every lane has read `old` before it is replaced
     if (lane == 0) *sp = scale;
   }
+}
+
+// fp8 caches, blocks of at most kStageChunks chunks: one warp per (touched
+// block slot j, KV head h, K or V, sequence b), as above. Lane t copies new
+// row t of the block into the warp's 4 KB stage with one bulk copy; the
+// bytes in flight cost no registers, so an SM keeps 7 CTAs (56 warps) with
+// 28 KB of rows each in flight. The warp does not leave before its copies
+// have landed (a bounded wait; on expiry it raises RBLN_DEVERR_TIMEOUT).
+template <bool IN_BF16>
+__global__ void __launch_bounds__(kWriteThreads) paged_kv_write_staged_kernel(const WriteArgs a, int slots) {
+  constexpr int kWarps = kWriteThreads / 32;
+  __shared__ __align__(128) uint4 stage[kWarps][kStageChunks];
+  __shared__ __align__(8) uint64_t bars[kWarps];
+  __shared__ int aborts[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t units = (int64_t)slots * a.Hkv * 2 * a.B;
+  if (unit >= units) return;
+  const int j = (int)(unit % slots);
+  const int64_t rest = unit / slots;
+  const int part = (int)(rest & 1), h = (int)((rest >> 1) % a.Hkv), b = (int)(rest / (2 * a.Hkv));
+  const int s0 = a.seq[b * a.seq_stride];
+  if (s0 < 0 || (int64_t)s0 + a.S > (int64_t)a.max_blocks * a.bs) {
+    if (lane == 0 && j == 0 && h == 0 && part == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_SEQ_RANGE);
+    return;
+  }
+  const int bi = s0 / a.bs + j;
+  if (bi > (s0 + a.S - 1) / a.bs) return;
+  const int base = bi * a.bs;
+  const int lo = max(s0, base) - base;               // first new row in the block
+  const int hi = min(s0 + a.S, base + a.bs) - base;  // one past the last
+  const int held = s0 > base ? lo : 0;               // rows [0, held) hold the sequence's context
+  const char* src = part == 0 ? a.k_new + b * a.kn_b + h * a.kn_h : a.v_new + b * a.vn_b + h * a.vn_h;
+  const int64_t src_s = part == 0 ? a.kn_s : a.vn_s;
+  const int cpr = a.D / 8;  // 8-element chunks per row (8 or 16)
+  const int cshift = a.D == 128 ? 4 : 3;
+  const int rows = hi - lo;  // at most bs <= 32: one lane per row
+  const uint32_t rbytes = (uint32_t)a.D * 2;
+
+  // stage the new rows: 16-byte aligned rows (the host checks the base and
+  // the strides), rbytes a multiple of 16
+  const uint32_t bar = smem_u32(&bars[warp]);
+  volatile int* abort = &aborts[warp];
+  if (lane == 0) {
+    *abort = 0;
+    sm100::mbar_init(bar, 1);
+    sm100::fence_mbar_init();
+    sm100::mbar_arrive_expect_tx(bar, (uint32_t)rows * rbytes);
+  }
+  __syncwarp();
+  if (lane < rows)
+    sm100::bulk_load(smem_u32(&stage[warp][lane * cpr]), src + (int64_t)(base + lo + lane - s0) * src_s, rbytes, bar);
+
+  // while the rows land: block-table entry, old scale, held rows' amax
+  const int64_t phys = load_index(a.bt, a.bt_dtype, b * a.bt_stride + bi);
+  const bool bad = phys < 0 || phys >= a.num_blocks;
+  if (bad && lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_BLOCK_ID_RANGE);
+  float* sp = nullptr;
+  uint8_t* c8 = nullptr;
+  float old = 0.f, m = 0.f;
+  if (!bad) {
+    sp = (part == 0 ? a.k_scale : a.v_scale) + phys * a.ss_block + (int64_t)h * a.ss_head;
+    old = *sp;
+    c8 = reinterpret_cast<uint8_t*>(part == 0 ? a.kcache : a.vcache) + phys * a.cs_block + (int64_t)h * a.cs_head;
+    for (int i = lane; i < held * cpr; i += 32) {
+      const int r = i >> cshift, c = i & (cpr - 1);
+      float x[8];
+      unpack8_e4m3(*reinterpret_cast<const uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8), old, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+    }
+  }
+  if (!__all_sync(0xffffffffu, sm100::mbar_wait(bar, 0, abort))) {
+    if (lane == 0 && a.err) atomicOr(a.err, RBLN_DEVERR_TIMEOUT);
+    return;
+  }
+  if (bad) return;
+
+  const int n_new = rows << cshift;  // staged chunks; chunk i is row lo + (i >> cshift)
+  const uint4* st = stage[warp];
+#pragma unroll
+  for (int k = 0; k < kStageChunks / 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i < n_new) {
+      float x[8];
+      unpack8<IN_BF16>(st[i], x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+    }
+  }
+  const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
+  const float inv = __frcp_rn(scale);
+  if (held > 0 && scale != old) {
+    for (int i = lane; i < held * cpr; i += 32) {
+      const int r = i >> cshift, c = i & (cpr - 1);
+      uint2* q = reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8);
+      float x[8];
+      unpack8_e4m3(*q, old, x);
+      *q = pack8_e4m3(x, inv);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kStageChunks / 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i < n_new) {
+      float x[8];
+      unpack8<IN_BF16>(st[i], x);
+      const int r = lo + (i >> cshift), c = i & (cpr - 1);
+      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
+    }
+  }
+  __syncwarp();  // every lane has read `old` before it is replaced
+  if (lane == 0) *sp = scale;
 }
 
 }  // namespace
@@ -274,7 +346,10 @@ extern "C" int rbln_paged_kv_write(const rbln_paged_attn_params_t* p, cudaStream
   if (ctas > INT32_MAX) return RBLN_ERR_UNSUPPORTED;
   const dim3 grid((unsigned)ctas);
   const bool bf = p->q_dtype == RBLN_DT_BF16;
-  if (fp8) {
+  if (fp8 && p->block_size * (p->head_dim / 8) <= kStageChunks) {
+    if (bf) paged_kv_write_staged_kernel<true><<<grid, kWriteThreads, 0, stream>>>(a, slots);
+    else paged_kv_write_staged_kernel<false><<<grid, kWriteThreads, 0, stream>>>(a, slots);
+  } else if (fp8) {
     if (bf) paged_kv_write_kernel<true, true><<<grid, kWriteThreads, 0, stream>>>(a, slots);
     else paged_kv_write_kernel<false, true><<<grid, kWriteThreads, 0, stream>>>(a, slots);
   } else {

@@ -92,6 +92,37 @@ __device__ __forceinline__ uint2 pack8_e4m3(const float (&x)[8], float inv) {
   }
   return make_uint2(u[0], u[1]);
 }
+// pack8_e4m3 with the products x * inv taken in pairs (mul.rn.f32x2, the
+// same rounding as one multiply each)
+__device__ __forceinline__ uint2 pack8_e4m3x2(const float (&x)[8], float inv) {
+  uint32_t u[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float a0 = x[4 * i], a1 = x[4 * i + 1], a2 = x[4 * i + 2], a3 = x[4 * i + 3];
+    sm100::mul2(a0, a1, inv, inv);
+    sm100::mul2(a2, a3, inv, inv);
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a0, a1), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(a2, a3), __NV_SATFINITE, __NV_E4M3);
+    u[i] = (lo & 0xffffu) | (hi << 16);
+  }
+  return make_uint2(u[0], u[1]);
+}
+
+// Running max of |x| over 8 new values (16 bytes of bf16 / f16) kept as a
+// packed pair of 16-bit values: sign bits cleared, then max.{bf16,f16}x2,
+// which, like fmaxf, returns the other operand when one is NaN. Exact: the
+// pair converts to floats without rounding.
+template <bool IN_BF16>
+__device__ __forceinline__ uint32_t amax8_packed(uint4 w, uint32_t acc) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t a = u[i] & 0x7fff7fffu;
+    if constexpr (IN_BF16) asm("max.bf16x2 %0, %0, %1;" : "+r"(acc) : "r"(a));
+    else asm("max.f16x2 %0, %0, %1;" : "+r"(acc) : "r"(a));
+  }
+  return acc;
+}
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -259,15 +290,15 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_staged_kernel(co
 
   const int n_new = rows << cshift;  // staged chunks; chunk i is row lo + (i >> cshift)
   const uint4* st = stage[warp];
+  uint32_t am = 0;  // packed +0, +0
 #pragma unroll
   for (int k = 0; k < kStageChunks / 32; ++k) {
     const int i = lane + 32 * k;
-    if (i < n_new) {
-      float x[8];
-      unpack8<IN_BF16>(st[i], x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
-    }
+    if (i < n_new) am = amax8_packed<IN_BF16>(st[i], am);
+  }
+  {
+    const float2 f = unpack2<IN_BF16>(am);
+    m = fmaxf(m, fmaxf(f.x, f.y));
   }
   const float scale = __fdiv_rn(fmaxf(warp_max(m), 1e-6f), kFp8Max);
   const float inv = __frcp_rn(scale);
@@ -287,7 +318,7 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_staged_kernel(co
       float x[8];
       unpack8<IN_BF16>(st[i], x);
       const int r = lo + (i >> cshift), c = i & (cpr - 1);
-      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3(x, inv);
+      *reinterpret_cast<uint2*>(c8 + (int64_t)r * a.cs_tok + c * 8) = pack8_e4m3x2(x, inv);
     }
   }
   __syncwarp();  // every lane has read `old` before it is replaced

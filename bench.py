@@ -1315,7 +1315,7 @@ def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "torch.ops.rbln_attn.paged_kv_write"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(gbs / hbm_peak, 4), "traffic": _traffic_from_profiles(wl_name),
-                     "kernel": "paged_kv_write_kernel<bf16, fp8>", "kernel_ms": round(op_ms, 4),
+                     "kernel": "paged_kv_write_staged_kernel<bf16>", "kernel_ms": round(op_ms, 4),
                      "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs), of measured" if peak_src == "measured"
                                      else "fallback 6.65 TB/s")},
         "gpu_launches": args.steps,

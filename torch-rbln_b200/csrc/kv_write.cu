@@ -215,8 +215,9 @@ __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_kernel(const Wri
 // fp8 caches, blocks of at most kStageChunks chunks: one warp per (touched
 // block slot j, KV head h, K or V, sequence b), as above. Lane t copies new
 // row t of the block into the warp's 4 KB stage with one bulk copy; the
-// bytes in flight cost no registers, so an SM keeps 7 CTAs (56 warps) with
-// 28 KB of rows each in flight. The warp does not leave before its copies
+// bytes in flight cost no registers, so an SM keeps 6 CTAs (48 warps, the
+// limit of both the registers and the shared memory) with up to 32 KB of
+// rows each in flight. The warp does not leave before its copies
 // have landed (a bounded wait; on expiry it raises RBLN_DEVERR_TIMEOUT).
 template <bool IN_BF16>
 __global__ void __launch_bounds__(kWriteThreads) paged_kv_write_staged_kernel(const WriteArgs a, int slots) {

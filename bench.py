@@ -1248,6 +1248,40 @@ def _cpu_kv_write(d, budget_s):
     return per_seq / med / 1e9, med, times
 
 
+def kv_write_parity(d, kc, vc, ks, vs, step, n=4, seed=7):
+    """One more C-ABI write over the whole batch, outside the timed region,
+    checked on a seeded subset of the sequences: their touched blocks (caches
+    and scales) are copied out before and after the call, and the oracle
+    applies the same write to the copy taken before. Caches and scales must
+    match bit for bit."""
+    from oracle import paged_attention as opa
+
+    B, bs, S = d["B"], d["bs"], d["S"]
+    n = min(n, B)
+    idx = torch.randperm(B, generator=torch.Generator().manual_seed(seed))[:n].sort().values
+    blocks, tabs = [], []
+    for b in idx.tolist():
+        s0 = int(d["seq"][b])
+        first, last = s0 // bs, (s0 + S - 1) // bs
+        tab = torch.zeros(d["bt"].shape[1], dtype=torch.int64)
+        tab[first:last + 1] = torch.arange(len(blocks), len(blocks) + last - first + 1)
+        blocks += d["bt"][b, first:last + 1].long().tolist()
+        tabs.append(tab)
+    sel = torch.tensor(blocks, dtype=torch.int64, device=kc.device)
+    torch.cuda.synchronize()
+    before = [t[sel].cpu() for t in (kc, vc, ks, vs)]
+    step()
+    torch.cuda.synchronize()
+    after = [t[sel].cpu() for t in (kc, vc, ks, vs)]
+    kc0, vc0, ks0, vs0 = before
+    opa.kv_write(d["k"][idx], d["v"][idx], kc0, vc0, d["seq"][idx], torch.stack(tabs), bs, ks0, vs0)
+    same = [torch.equal(a.view(torch.uint8), b.view(torch.uint8)) for a, b in zip((kc0, vc0), after[:2])]
+    same += [torch.equal(a, b) for a, b in zip((ks0, vs0), after[2:])]
+    return {"ok": all(same), "n_checked": n, "blocks_checked": len(blocks),
+            "checked": f"sequences {idx.tolist()}: every touched block's K and V cache rows and scales",
+            "tolerance": "bit-exact", "oracle": "oracle.paged_attention.kv_write"}
+
+
 def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
     import torch_rbln_b200  # noqa: F401
     from torch_rbln_b200 import cabi
@@ -1302,6 +1336,9 @@ def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    parity = kv_write_parity(d, kc, vc, ks, vs, step, seed=7 + rank)
+    failed = ctx.reduce([0.0 if parity["ok"] else 1.0], "max")[0]
+    parity["ok"] = parity["ok"] and failed == 0
     op_ms, e2e_ms = ctx.reduce([op_ms, e2e_ms], "max")
     hbm_peak, _, peak_src = load_peaks()
     gbs = d["bytes"] / (op_ms * 1e-3) / 1e9
@@ -1320,6 +1357,7 @@ def kv_write_record(args, ctx: Ctx, wl_name: str, cpu_leg: bool = True) -> dict:
                                      else "fallback 6.65 TB/s")},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
+        "parity": parity,
     }
     if rank == 0 and cpu_leg and ws == 1 and not args.no_cpu_baseline:
         val, med, times = _cpu_kv_write(build_kv_write(wl), min(args.cpu_budget, 10.0))

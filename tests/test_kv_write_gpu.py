@@ -93,6 +93,25 @@ def test_prefill_then_decode_writes(cache, D):
         torch.testing.assert_close(out.cpu().float(), ref, rtol=1e-3, atol=1.2e-2)
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_f16_rows_into_fp8_cache(D):
+    """f16 rows into an fp8 cache (the amax taken on packed f16 pairs): a
+    chunk that starts and ends inside blocks, over held rows that are
+    re-quantized; caches and scales bit-exact."""
+    B, Hkv, bs, mb = 3, 2, 16, 8
+    g, bt, kc0, vc0, ks0, vs0 = setup(B, Hkv, D, bs, mb, torch.float16, torch.float8_e4m3fn, seed=100 + D)
+    kc, vc = [kc0.to(DEV), kc0.clone()], [vc0.to(DEV), vc0.clone()]
+    ks, vs = [ks0.to(DEV), ks0.clone()], [vs0.to(DEV), vs0.clone()]
+    starts = torch.tensor([0, 5, 30], dtype=torch.int32)
+    k = (torch.randn([B, Hkv, 1, 37, D], generator=g) * 2).to(torch.float16)
+    v = (torch.randn([B, Hkv, 1, 37, D], generator=g) * 2).to(torch.float16)
+    write_both(k, v, kc, vc, starts, bt, bs, ks, vs)
+    assert_same(kc[0], kc[1], "kcache")
+    assert_same(vc[0], vc[1], "vcache")
+    assert_same(ks[0], ks[1], "k_scale")
+    assert_same(vs[0], vs[1], "v_scale")
+
+
 def test_invalid_block_id_sets_the_flag():
     from torch_rbln_b200 import cabi
 
